@@ -1,0 +1,2 @@
+#pragma once
+#include "xrt_stub_types.h"
