@@ -1,0 +1,415 @@
+"""Benchmark of the int4 group-32 weight-only matmul path on B200 (one JSON line on rank 0).
+
+Default workload: the Qwen3-8B decode projections, 36 layers of
+random int4 weights (q/k/v fused 6144x4096, gate/up fused 24576x4096 with the SwiGLU fused into
+its epilogue, down 4096x12288), M tokens (default 1) of bf16 N(0,1) activations. One step = one
+decode pass over the 36 layers' projections = 108 GEMV launches, replayed from a CUDA graph.
+3.57 GB of weights per step (> the 126 MB L2), so every step streams HBM; no flush is needed.
+
+Metric: achieved HBM GB/s = algorithmic bytes (int4 codes + fp16 scales + activations in +
+outputs) per step / step time. Also reported: tokens/s = M / step time.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config qwen3-8b|gemv] [--m M]
+
+--gpus N > 1 runs under torchrun, one rank per GPU, each rank an independent replica of the
+decode stack on its own tokens (the dense projections of one replica need no exchange: replicas
+only, weak scaling). Time = max over ranks of the device-timed region.
+--impl reference times the reference's CPU dequantise-then-matmul path (restated in oracle/) on
+this host's cores, on a bounded sample of the same workload.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+HIDDEN, INTER, LAYERS = 4096, 12288, 36
+QKV_N = 4096 + 2 * 1024
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+# ------------------------------------------------------------------ workloads
+def qwen3_8b_matrices():
+    """(name, N, K, gateup) of one layer, in execution order."""
+    return [("qkv", QKV_N, HIDDEN, False), ("gate_up", 2 * INTER, HIDDEN, True), ("down", HIDDEN, INTER, False)]
+
+
+def int4_param_bytes(N, K):
+    return N * K // 2 + N * (K // 32) * 2
+
+
+def gen_int4_cuda(N, K, gen):
+    qk = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=gen)
+    s = ((torch.randn(N, K // 32, device="cuda", generator=gen) * 0.02).abs() + 1e-4).to(torch.float16)
+    return qk, s
+
+
+class DecodeStack:
+    """The Qwen3-8B projection stack on one GPU (libonpu dense matrices)."""
+
+    def __init__(self, M, seed, layers=LAYERS):
+        from opennpu_b200 import dense
+        self.dense = dense
+        self.M = M
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+        self.layers = []
+        for _ in range(layers):
+            mats = {}
+            for name, N, K, gu in qwen3_8b_matrices():
+                qk, s = gen_int4_cuda(N, K, gen)
+                mats[name] = dense.DenseMatrix.from_int4(qk, s, gateup=gu)
+                del qk, s
+            self.layers.append(mats)
+        torch.cuda.synchronize()
+        self.x = [torch.randn(M, HIDDEN, device="cuda", generator=gen).to(torch.bfloat16) for _ in range(layers)]
+        self.y_qkv = torch.empty(M, QKV_N, device="cuda")
+        self.a = torch.empty(M, INTER, device="cuda", dtype=torch.bfloat16)
+        self.y = torch.empty(M, HIDDEN, device="cuda")
+        per_layer = 0
+        for name, N, K, gu in qwen3_8b_matrices():
+            per_layer += int4_param_bytes(N, K) + M * K * 2
+        per_layer += M * QKV_N * 4 + M * INTER * 2 + M * HIDDEN * 4
+        self.bytes_per_step = per_layer * layers
+        self.weight_bytes_per_step = sum(int4_param_bytes(N, K) for _, N, K, _ in qwen3_8b_matrices()) * layers
+        self.launches_per_step = 3 * layers
+
+    def step(self):
+        d = self.dense
+        for l, mats in enumerate(self.layers):
+            mats["qkv"].mv(self.x[l], out=self.y_qkv)
+            mats["gate_up"].mv(self.x[l], out=self.a, epi=d.EPI_SWIGLU)
+            mats["down"].mv(self.a, out=self.y)
+
+    def step_host(self, xs_host, ys_host):
+        """The same pass through the reference ABI's host-pointer call (onpu_dense_mv): fp32 host
+        inputs/outputs, copies and a synchronisation inside every call, SwiGLU on the host."""
+        from opennpu_b200 import libonpu as L
+        lib = L.load()
+        for l, mats in enumerate(self.layers):
+            x = xs_host[l]
+            lib.onpu_dense_mv(mats["qkv"].h, L.fp(x), self.M, L.fp(ys_host["qkv"]))
+            lib.onpu_dense_mv(mats["gate_up"].h, L.fp(x), self.M, L.fp(ys_host["gate_up"]))
+            h = ys_host["gate_up"]
+            g, u = h[:, :INTER], h[:, INTER:]
+            a = np.ascontiguousarray(g / (1.0 + np.exp(-g)) * u, np.float32)
+            lib.onpu_dense_mv(mats["down"].h, L.fp(a), self.M, L.fp(ys_host["down"]))
+        err = L.last_error()
+        if err:
+            raise RuntimeError(err)
+
+
+class GemvRotation:
+    """one 4096x4096 int4 GEMV, M=1; the step rotates over 32 weight copies (302 MB
+    > L2) so every launch reads HBM."""
+
+    def __init__(self, M, seed, copies=32, N=4096, K=4096):
+        from opennpu_b200 import dense
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+        self.mats = []
+        for _ in range(copies):
+            qk, s = gen_int4_cuda(N, K, gen)
+            self.mats.append(dense.DenseMatrix.from_int4(qk, s))
+        self.M = M
+        self.x = torch.randn(M, K, device="cuda", generator=gen).to(torch.bfloat16)
+        self.y = torch.empty(M, N, device="cuda")
+        self.bytes_per_step = copies * (int4_param_bytes(N, K) + M * K * 2 + M * N * 4)
+        self.weight_bytes_per_step = copies * int4_param_bytes(N, K)
+        self.launches_per_step = copies
+
+    def step(self):
+        for m in self.mats:
+            m.mv(self.x, out=self.y)
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [v.strip() for v in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle port)
+def cpu_reference_sample(M, seconds=10.0, seed=0):
+    """The reference's CPU path on one Qwen3-8B layer's projections: dequantise per 32
+    (reference.py:24-28 semantics, v * s) and fp32 matmul (reference.py:55-57), all host threads.
+    Returns (GB/s with dequant per call, GB/s steady-state on pre-dequantised W, cores, sample)."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    mats = []
+    for name, N, K, gu in qwen3_8b_matrices():
+        v = torch.randint(-8, 8, (N, K), dtype=torch.int8, generator=g)
+        s = ((torch.randn(N, K // 32, generator=g) * 0.02).abs() + 1e-4).to(torch.float16)
+        mats.append((N, K, v, s))
+    x = torch.randn(M, HIDDEN, generator=g).to(torch.bfloat16).float()
+    a = torch.randn(M, INTER, generator=g).to(torch.bfloat16).float()
+    layer_bytes = sum(int4_param_bytes(N, K) for N, K, _, _ in mats)
+
+    def deq(v, s):
+        N, K = v.shape
+        return (v.view(N, K // 32, 32).float() * s.float()[..., None]).view(N, K)
+
+    def one_layer(pre=None):
+        ys = []
+        for i, (N, K, v, s) in enumerate(mats):
+            W = pre[i] if pre is not None else deq(v, s)
+            ys.append((x if K == HIDDEN else a) @ W.T)
+        return ys
+
+    one_layer()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 1:
+        one_layer()
+        n += 1
+    dq = n * layer_bytes / (time.perf_counter() - t0) / 1e9
+    pre = [deq(v, s) for _, _, v, s in mats]
+    one_layer(pre)
+    n2, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds / 2 or n2 < 1:
+        one_layer(pre)
+        n2 += 1
+    ss = n2 * layer_bytes / (time.perf_counter() - t0) / 1e9
+    sample = f"{n} x one Qwen3-8B layer's q/k/v, gate/up, down (dequant + fp32 matmul, M={M})"
+    return dq, ss, torch.get_num_threads(), sample
+
+
+# ------------------------------------------------------------------ runs
+def dist_setup(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def run_ours(args):
+    rank, world, local = dist_setup(args.gpus)
+    hbm, _, peak_kind = peaks()
+    M = args.m
+    work = DecodeStack(M, seed=1000 + rank) if args.config == "qwen3-8b" else GemvRotation(M, seed=1000 + rank)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(max(args.warmup, 1)):
+            work.step()
+    s.synchronize()
+    from opennpu_b200 import dense
+    dense.check_device()
+
+    use_graph = os.environ.get("ONPU_BENCH_GRAPH", "1") != "0"
+    graph = None
+    if use_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            work.step()
+        torch.cuda.synchronize()
+
+    def run_steps(k):
+        with torch.cuda.stream(s):
+            for _ in range(k):
+                if graph is not None:
+                    graph.replay()
+                else:
+                    work.step()
+
+    run_steps(args.warmup)                              # warm-up of the timed path itself
+    s.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(s)
+    run_steps(args.steps)
+    ev1.record(s)
+    ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    clk = clocks.stop()
+    dense.check_device()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    ms_step = ms / args.steps
+    gbs = work.bytes_per_step * world / (ms_step * 1e-3) / 1e9
+    per_gpu_gbs = work.bytes_per_step / (ms_step * 1e-3) / 1e9
+
+    # end to end through the reference ABI's host-pointer call (rank-local, not graph-replayed)
+    e2e = None
+    if isinstance(work, DecodeStack) and not args.no_e2e:
+        xs = [np.ascontiguousarray(xl.float().cpu().numpy()) for xl in work.x]
+        ys = {"qkv": np.empty((M, QKV_N), np.float32), "gate_up": np.empty((M, 2 * INTER), np.float32),
+              "down": np.empty((M, HIDDEN), np.float32)}
+        work.step_host(xs, ys)
+        e_steps = max(2, min(args.steps, 5))
+        if world > 1:
+            torch.distributed.barrier()
+        t0 = time.perf_counter()
+        for _ in range(e_steps):
+            work.step_host(xs, ys)
+        dt = (time.perf_counter() - t0) / e_steps
+        if world > 1:
+            t = torch.tensor([dt], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            dt = float(t.item())
+        h2d = LAYERS * M * (HIDDEN * 4 * 2 + INTER * 4)
+        d2h = LAYERS * M * (QKV_N + 2 * INTER + HIDDEN) * 4
+        e2e = {"value": round(work.bytes_per_step * world / dt / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3),
+               "path": "onpu_dense_mv (host fp32 in/out, reference ABI)"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu and isinstance(work, DecodeStack):
+        dq, ss, cores, sample = cpu_reference_sample(M, seconds=args.cpu_seconds)
+        cpu = {"value": round(dq, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample,
+               "steady_state_prequantised_value": round(ss, 3)}
+
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get(args.config)
+    if rank == 0:
+        achieved = per_gpu_gbs
+        line = {
+            "metric": "int4 GEMV achieved HBM GB/s (Qwen3-8B decode projections, 36 layers)"
+            if args.config == "qwen3-8b" else "int4 GEMV achieved HBM GB/s (4096x4096, M=1)",
+            "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4xbf16->fp32", "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1))",
+            "config": {"workload": "qwen3-8b-decode-projections" if args.config == "qwen3-8b" else "gemv-4096x4096",
+                       "M": M, "layers": LAYERS if args.config == "qwen3-8b" else 1,
+                       "bytes_per_step_per_gpu": work.bytes_per_step,
+                       "weight_bytes_per_step_per_gpu": work.weight_bytes_per_step,
+                       "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (no flush needed)",
+                       "cuda_graph": graph is not None},
+            "tokens_per_s": round(M * world / (ms_step * 1e-3), 1) if args.config == "qwen3-8b" else None,
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": work.launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    if graph is not None:
+        del graph
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    M = args.m
+    vals = []
+    samples = None
+    for i in range(args.warmup + args.steps):
+        dq, ss, cores, sample = cpu_reference_sample(M, seconds=1.0, seed=i)
+        if i >= args.warmup:
+            vals.append(dq)
+            samples = sample
+    v = float(np.median(vals))
+    line = {"impl": "reference", "metric": "int4 GEMV achieved HBM GB/s (Qwen3-8B decode projections, 36 layers)",
+            "value": round(v, 3), "unit": "GB/s", "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4xbf16->fp32", "data": "synthetic",
+            "config": {"workload": "qwen3-8b-decode-projections", "M": M, "layers": LAYERS},
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                             "sample": f"per step: {samples}"},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv"])
+    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,143 @@
+/*
+ * libonpu for NVIDIA B200 (sm_100a): the C ABI of OpenNPU's int4 weight-only matmul path.
+ *
+ * Part 1 keeps the reference library's exported names, signatures, argument meaning and error
+ * behaviour (NULL handle / 0 return = "not supported, fall back"), so the reference's ctypes
+ * binding (opennpu/native/npu4/model.py:281-335) and its callers load this library unchanged.
+ * Every declaration cites the reference definition it replaces (llama/ggml-opennpu/...).
+ * Buffers passed as float* / int32_t* are HOST memory, fp32, row-major, contiguous, as in the
+ * reference; the library copies them to the GPU and back. Outputs are overwritten.
+ *
+ * Part 2 adds B200-specific entry points (device pointers + CUDA streams, packed-int4 ingest,
+ * error reporting). They have no counterpart in the reference.
+ *
+ * Errors never throw across the ABI. A failing call records a message readable with
+ * onpu_last_error() and, for calls that return a value, returns NULL / 0 / a negative code.
+ */
+#ifndef ONPU_H
+#define ONPU_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ======================================================================== part 1: reference ABI */
+
+/* 1 when a CUDA device is usable (reference: NPU device found, onpu_api.cpp:59). */
+int onpu_ok(void);
+/* 1 when the batched (multi-token) path is available (onpu_api.cpp:60). Always equal to onpu_ok():
+ * the GPU kernels take 1..any tokens per weight pass. */
+int onpu_batched_ok(void);
+/* Kernel launches so far and host seconds spent waiting for them (onpu_api.cpp:72-80). */
+void onpu_stats(int64_t *calls, double *wait_s);
+/* 1 if a device shape exists (onpu_api.cpp:82-84). The GPU kernels are shape-generic: 1 whenever
+ * onpu_ok(). */
+int onpu_has_shape(int tiles, int kc, int batched);
+
+/* R, S, tiles, kc, ks, rows_col, cb, nbytes of an [N, K] matrix on ncols columns; all 0 when
+ * there is no geometry (onpu_api.cpp:64-69). Identical arithmetic: these sizes define the upload
+ * buffers below, and opennpu/native/npu4/model.py:353-360 checks them against its own Mat. */
+void onpu_geometry2(int64_t N, int64_t K, int ncols, int sym, int64_t *out);
+void onpu_geometry(int64_t N, int64_t K, int ncols, int64_t *out);
+
+/* ---- dense matrices (onpu_api.cpp:87-156) */
+/* New [N, K] matrix; sym 0 = q4nx (bf16 scale+min per 32), 1 = q4s (bf16 scale). NULL when the
+ * shape has no 8-column geometry or no device (onpu_api.cpp:87-101). */
+void *onpu_dense_new2(int64_t N, int64_t K, int sym);
+void *onpu_dense_new(int64_t N, int64_t K);                 /* onpu_api.cpp:102 */
+/* Host buffer of onpu_dense_bytes() bytes for the caller to fill with the stream-order packets
+ * of opennpu_core.hpp:178-254 (onpu_api.cpp:103-104). */
+uint8_t *onpu_dense_buf(void *h);
+int64_t onpu_dense_bytes(void *h);
+/* Upload the buffer and convert it to the GPU layout (onpu_api.cpp:106-114). */
+void onpu_dense_sync(void *h);
+/* y[rows][N] = x[rows][K] . W^T; x rounded to bf16 first, fp32 accumulate, fp32 y
+ * (onpu_api.cpp:119-156). */
+void onpu_dense_mv(void *h, const float *x, int64_t rows, float *y);
+void onpu_dense_free(void *h);                              /* onpu_api.cpp:116 */
+
+/* ---- expert banks: E experts of [N, K], expert e's packets at e * expert_bytes (onpu_api.cpp:159-250) */
+void *onpu_bank_new2(int64_t N, int64_t K, int64_t E, int ncols, int sym);
+void *onpu_bank_new(int64_t N, int64_t K, int64_t E, int ncols);   /* onpu_api.cpp:168 */
+uint8_t *onpu_bank_buf(void *h);                           /* onpu_api.cpp:169 */
+int64_t onpu_bank_expert_bytes(void *h);                   /* onpu_api.cpp:170 */
+void onpu_bank_sync(void *h);                              /* onpu_api.cpp:171-174 */
+/* y[T][k][N]: token t, slot j -> expert ids[t*k+j] applied to x[t] (x_per_slot == 0) or
+ * x[t][j] (x_per_slot != 0) (onpu_api.cpp:177-250). */
+void onpu_bank_run(void *h, const float *x, int x_per_slot, int64_t T, const int32_t *ids, int k, float *y);
+void onpu_bank_free(void *h);                              /* onpu_api.cpp:175 */
+
+/* ---- MoE glue (onpu_api.cpp:252-278, onpu_cpu.cpp:231-274) */
+/* y[T][Nd] = sum_j w[t][j] * (dn_e . act(gu_e . x_t + gu_bias[e]) + dn_bias[e]); act 0:
+ * silu(h[:I]) * h[I:]; act 1: gpt-oss interleaved clamped gate (alpha, limit). */
+void onpu_moe_ffn(void *gu, void *dn, const float *x, int64_t T, const int32_t *ids, int k, const float *w, int act,
+                  float alpha, float limit, const float *gu_bias, const float *dn_bias, float *y);
+/* Host CPU helpers with the reference's semantics (onpu_cpu.cpp:233-274). */
+void onpu_moe_act(const float *h, int64_t rows, int64_t Ng, const int32_t *ids, const float *gu_bias, int act,
+                  float alpha, float limit, float *a);
+void onpu_moe_sum(const float *o, int64_t T, int k, int64_t N, const int32_t *ids, const float *w, const float *bias,
+                  float *y);
+
+/* ---- fused routed-expert FFN (onpu_api.cpp:292-496) */
+void *onpu_ffn_new(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t E, int sym);
+void *onpu_ffn_gu(void *h);                                /* onpu_api.cpp:326 */
+void *onpu_ffn_dn(void *h);                                /* onpu_api.cpp:327 */
+int onpu_ffn_fused(void *h);                               /* onpu_api.cpp:328 */
+/* packed gate_up row r holds original row perm[r] (onpu_api.cpp:329-332). Identity here: the GPU
+ * interleaves gate/up rows itself when it converts the upload. */
+void onpu_ffn_perm(void *h, int32_t *out);
+/* one token: y[Nd] = sum_j w[j] * FFN_{ids[j]}(x); 1 = done (onpu_api.cpp:423-446) */
+int onpu_ffn_run(void *h, const float *x, const int32_t *ids, int k, const float *w, float *y);
+/* T tokens: y[T][Nd] (onpu_api.cpp:451-496) */
+int onpu_ffn_run_many(void *h, const float *x, int64_t T, const int32_t *ids, int k, const float *w, float *y);
+void onpu_ffn_free(void *h);                               /* onpu_api.cpp:333-339 */
+
+/* ---- codec (onpu_api.cpp:499-529): host CPU, load time */
+int64_t onpu_pack(const float *W, int64_t N, int64_t K, int ncols, int sym, uint8_t *out, int threads);
+void onpu_quant_dequant(const float *W, int64_t N, int64_t K, int sym, float *out, int threads);
+
+/* ======================================================================== part 2: B200 additions */
+/* No counterpart in the reference. */
+
+/* Weight formats of the GPU layout. */
+#define ONPU_FMT_Q4NX 0   /* q*s + m, bf16 s, m  (reference sym = 0)           */
+#define ONPU_FMT_Q4S 1    /* (q-8)*d, bf16 d     (reference sym = 1)           */
+#define ONPU_FMT_Q4F16 2  /* v*s, int4 v in [-8,7] packed along K, fp16 s      */
+
+/* Output epilogues of the device-pointer GEMV. */
+#define ONPU_EPI_F32 0    /* y fp32                                                    */
+#define ONPU_EPI_BF16 1   /* y bf16                                                    */
+#define ONPU_EPI_SWIGLU 2 /* y[i] = bf16(silu(acc[gate i]) * acc[up i]); needs a gate/up */
+                          /* matrix created with onpu_dense_new_int4(..., gateup = 1)     */
+
+/* Last error message of this thread (NULL if the last failing-capable call succeeded). */
+const char *onpu_last_error(void);
+/* Device-side status: 0 ok, else a kernel reported a timed-out wait (then reset). Synchronises. */
+int onpu_check_device(void);
+
+/* A dense [N, K] matrix filled from int4 packed along K: qk[N][K/2] (two's complement, element
+ * 2j in the low nibble of byte j) and fp16 scales s[N][K/32]. Any K % 32 == 0 (no geometry
+ * limit). gateup != 0: rows [0, N/2) are gate, [N/2, N) up, stored interleaved so that
+ * ONPU_EPI_SWIGLU can fuse the activation (N/2 % 8 == 0). */
+void *onpu_dense_new_int4(int64_t N, int64_t K, int gateup);
+/* Fill from host (on_device = 0) or device (on_device = 1) arrays; 0 ok, < 0 error. */
+int onpu_dense_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream);
+/* Format, N, K, bytes of the GPU-layout matrix. */
+int onpu_dense_info(void *h, int64_t *out4);
+/* y = x . W^T on the GPU, asynchronous on `stream` (NULL: the legacy default stream).
+ * x: bf16 [rows][ldx] device, 16-byte aligned rows (ldx % 8 == 0); y: [rows][ldy] fp32 or bf16
+ * device (by epi). A first call for a given row count allocates (call it outside stream capture);
+ * later calls with that row count allocate nothing. 0 ok, < 0 error. */
+int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream);
+/* Prepare (allocate descriptors and scratch for) `rows`-row calls without running one. */
+int onpu_dense_prepare(void *h, int64_t rows);
+/* GPU layout -> plain codes q[N][K] (0..15), scales[N][K/32] (and mins for q4nx), device pointers;
+ * for bit-exact verification. */
+int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ONPU_H */

@@ -1,0 +1,100 @@
+// The int4 weight layout libonpu keeps in B200 HBM, and the descriptors the kernels share.
+//
+// A matrix W [N][K] (K % 32 == 0; one 16-bit scale, and for q4nx one 16-bit min, per 32 weights
+// along K) is stored as row groups of 64 rows; each row group as chunks of 64 along K; each chunk
+// as 4 "strips" of 16 rows:
+//
+//   matrix  = [ceil(N/64) row groups][ceil(K/64) chunks][4 strips][strip bytes]
+//   strip   = 512 B codes | 64 B scales | (q4nx) 64 B mins         (576 or 640 B)
+//
+// so a chunk is 2304 B (q4s / int4-fp16) or 2560 B (q4nx), and any run of chunks in a row group
+// (or across row groups) is one contiguous byte range: the GEMV streams it with 1-D bulk copies.
+//
+// Inside a strip the 512 code bytes are 32 lanes x 16 B: lane L = 4r + t (r = L/4, t = L%4) owns
+// the codes its mma.sync.m16n8k16 A fragments need for strip rows r and r+8, K offsets
+// 8t .. 8t+7 of both 32-groups of the chunk. Word w = 2*gi + j (gi = group in the chunk, j = k16
+// step) holds 8 codes at bits 4p, p = i + 4h, for A register i (0..3) and half h (0/1):
+//     strip row  = r + 8*(i & 1)
+//     K in group = 8t + 4j + 2*(i >> 1) + h
+// so (w >> 4i) & 0x000F000F puts the two codes of A register i into its two 16-bit halves, and
+// OR-ing 0x43004300 makes them the exact bf16 values 128 + q. Because every lane's 8 K offsets of
+// a group are contiguous, its B fragments (activations) are one 16-B load per group.
+// Scales: [r 0..7][gi 0..1][h 0..1] 16-bit values, the scale of strip row r + 8h in group gi;
+// a lane loads its 4 with one 8-B load. Mins (q4nx) use the same order.
+//
+// Codes are always q in 0..15: q4nx w = q*s + m (bf16 s, m); q4s w = (q-8)*d (bf16 d); the
+// int4/fp16 format (int4 v in [-8, 7], fp16 scale) stores q = v + 8, w = (q-8)*s. Padding rows
+// or columns carry q = 8 (symmetric) or 0 (q4nx) with zero scale/min, and contribute 0.
+#pragma once
+#include <cstdint>
+
+namespace onpu_b200 {
+
+enum WeightFormat : int {
+    kFmtQ4NX = 0,   // asymmetric, bf16 scale + bf16 min      (reference "q4nx", sym = 0)
+    kFmtQ4S = 1,    // symmetric, bf16 scale                  (reference "q4s", sym = 1)
+    kFmtQ4F16 = 2,  // symmetric int4 [-8, 7], fp16 scale     (packed-along-K int4 + fp16 ingest)
+};
+
+constexpr int kRowGroup = 64;
+constexpr int kStripRows = 16;
+constexpr int kChunkK = 64;
+constexpr int kCodeBytes = 512;
+constexpr int kScaleBytes = 64;
+constexpr int kMaxTokensPerJob = 16;   // two n8 MMA tiles
+
+__host__ __device__ constexpr int strip_bytes(int fmt) { return fmt == kFmtQ4NX ? 640 : 576; }
+__host__ __device__ constexpr int chunk_bytes(int fmt) { return 4 * strip_bytes(fmt); }
+
+struct GpuMatrix {
+    int64_t N = 0, K = 0;
+    int fmt = kFmtQ4S;
+    int row_groups = 0, chunks = 0;    // ceil(N/64), ceil(K/64)
+    int64_t bytes = 0;
+};
+
+inline GpuMatrix make_gpu_matrix(int64_t N, int64_t K, int fmt) {
+    GpuMatrix g;
+    g.N = N;
+    g.K = K;
+    g.fmt = fmt;
+    g.row_groups = static_cast<int>((N + kRowGroup - 1) / kRowGroup);
+    g.chunks = static_cast<int>((K + kChunkK - 1) / kChunkK);
+    g.bytes = static_cast<int64_t>(g.row_groups) * g.chunks * chunk_bytes(fmt);
+    return g;
+}
+
+// One GEMV job: up to 16 activation rows against one matrix (an expert, or the dense matrix).
+struct GemvJob {
+    const uint8_t *w;                  // GPU-layout matrix
+    int m;                             // tokens in this job (1..16)
+    int pad_;
+    int xrow[kMaxTokensPerJob];        // activation row of token n
+    int yrow[kMaxTokensPerJob];        // output row of token n
+};
+
+enum GemvEpilogue : int {
+    kEpiF32 = 0,      // y[yrow][n] = acc (fp32)
+    kEpiBF16 = 1,     // y[yrow][n] = bf16(acc)
+    kEpiSwiGLU = 2,   // strip rows 0-7 gate, 8-15 up: y[yrow][i] = bf16(silu(gate_i) * up_i)
+};
+
+struct GemvParams {
+    const GemvJob *jobs;
+    int njobs;
+    int N, K;                          // every job's matrix shape (logical)
+    int row_groups, chunks;            // of one job
+    int total_chunks;                  // njobs * row_groups * chunks
+    int workers;                       // warps sharing the chunk sequence
+    const uint16_t *x;                 // bf16 activations, row stride ldx (elements)
+    int64_t ldx;
+    void *y;                           // output rows, stride ldy (elements of the output type)
+    int64_t ldy;
+    const int *row_map;                // optional: GPU row -> output column (fp32/bf16 epilogues)
+    float *part;                       // split-row partial sums: [2 * workers][4][NT][32][4]
+    unsigned *counters;                // [njobs * row_groups], zero between launches
+    int *err;                          // set non-zero on a timed-out wait
+    int jobs_ready;                    // job list not written by the previous kernel in the stream
+};
+
+}  // namespace onpu_b200

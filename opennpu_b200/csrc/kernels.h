@@ -1,0 +1,57 @@
+// Host-callable launchers of libonpu's CUDA kernels (no torch types; plain pointers + streams).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "gpu_layout.cuh"
+
+namespace onpu_b200 {
+
+// ---- GEMV (gemv.cu)
+int gemv_ctas_per_sm(int fmt, int ntiles);
+int gemv_warps_per_cta();
+int64_t gemv_part_floats_per_worker(int ntiles);
+cudaError_t gemv_launch(int fmt, int ntiles, int epi, const GemvParams &p, cudaStream_t stream, bool pdl);
+
+// ---- layout conversion (repack.cu)
+// Where the codes of the matrix come from.
+enum RepackSource : int {
+    kSrcStream = 0,     // the reference's stream-order packets (onpu_*_buf upload format)
+    kSrcInt4K = 1,      // int4 two's complement packed 2/byte along K (low nibble first) + fp16 scales
+    kSrcCodes = 2,      // plain codes q [N][K] (0..15) + 16-bit scales/mins [N][K/32]
+};
+
+struct RepackParams {
+    int src_kind;
+    const uint8_t *src;        // stream bytes / packed int4 / codes
+    const uint16_t *scales;    // kSrcInt4K, kSrcCodes
+    const uint16_t *mins;      // kSrcCodes (q4nx)
+    const int *src_row;        // optional: GPU row -> source row (row interleaving), null = identity
+    int64_t N, K;              // logical matrix
+    int fmt;                   // GPU format (decides symmetric padding and the mins section)
+    // reference stream-order geometry (kSrcStream)
+    int R, S, tiles, kc;
+    int64_t ks, rows_col, cb;
+    int pkt;
+    uint8_t *dst;              // GPU layout, make_gpu_matrix(N, K, fmt).bytes
+};
+cudaError_t repack_launch(const RepackParams &p, cudaStream_t stream);
+
+// GPU layout -> plain codes (q [N][K], scales [N][K/32], mins) for bit-exact checks.
+cudaError_t unpack_gpu_launch(const uint8_t *src, int64_t N, int64_t K, int fmt, uint8_t *q, uint16_t *s,
+                              uint16_t *m, cudaStream_t stream);
+
+// ---- small elementwise kernels (misc.cu)
+// fp32 -> bf16 bits with the reference's rounding (RNE; NaN -> quiet NaN), rows x cols with strides.
+cudaError_t f32_to_bf16_launch(const float *x, int64_t rows, int64_t cols, int64_t ldx, uint16_t *out, int64_t ldo,
+                               cudaStream_t stream);
+// a[r][i] = bf16(act(h[r] + gu_bias[ids[r]])), act 0 = silu(gate) * up, 1 = gpt-oss clamped gate.
+cudaError_t moe_act_launch(const float *h, int64_t ldh, int64_t rows, int64_t Ng, const int32_t *ids,
+                           const float *gu_bias, int act, float alpha, float limit, uint16_t *a, int64_t lda,
+                           cudaStream_t stream);
+// y[t][n] = sum_j w[t][j] * (o[(t*k + j)][n] + bias[ids[t*k+j]][n]) in slot order.
+cudaError_t moe_combine_launch(const float *o, int64_t ldo, int64_t T, int k, int64_t N, const int32_t *ids,
+                               const float *w, const float *bias, float *y, int64_t ldy, cudaStream_t stream);
+
+}  // namespace onpu_b200

@@ -1,0 +1,892 @@
+// libonpu for B200: the reference's C ABI (llama/ggml-opennpu/onpu_api.cpp, onpu_cpu.cpp) backed
+// by CUDA, plus device-pointer additions. See include/onpu.h for the per-function contract.
+//
+// Runtime model: one process per GPU; the library uses the CUDA device that is current when it is
+// first called. Host-pointer calls (the reference ABI) are serialised by one process-wide mutex
+// like the reference's g_mu (onpu_api.cpp:53) and run on the library's own stream; each copies its
+// inputs in, launches, copies out and waits. Device-pointer calls (_dev) are asynchronous on the
+// caller's stream and must be stream-ordered with respect to each other (they share the GEMV's
+// split-row scratch).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "gpu_layout.cuh"
+#include "host_codec.hpp"
+#include "kernels.h"
+#include "onpu.h"
+
+using namespace onpu_b200;
+
+namespace {
+
+// ------------------------------------------------------------------ errors
+thread_local std::string t_err;
+thread_local bool t_has_err = false;
+
+void set_err(const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_err = buf;
+    t_has_err = true;
+    if (std::getenv("ONPU_DEBUG")) fprintf(stderr, "onpu: %s\n", buf);
+}
+void clear_err() { t_has_err = false; }
+
+#define ONPU_CUDA(expr, ret)                                                               \
+    do {                                                                                   \
+        cudaError_t e_ = (expr);                                                           \
+        if (e_ != cudaSuccess) {                                                           \
+            set_err("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__); \
+            return ret;                                                                    \
+        }                                                                                  \
+    } while (0)
+
+std::mutex g_mu;
+
+// ------------------------------------------------------------------ device context
+template <typename T>
+bool grow(T *&p, int64_t &cap, int64_t n, bool zero = false) {
+    if (n <= cap) return true;
+    if (p) {
+        cudaDeviceSynchronize();   // the old buffer may still be in use by queued kernels
+        cudaFree(p);
+    }
+    p = nullptr;
+    cap = 0;
+    cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&p), static_cast<size_t>(n) * sizeof(T));
+    if (e != cudaSuccess) {
+        set_err("cudaMalloc(%lld bytes): %s", static_cast<long long>(n * sizeof(T)), cudaGetErrorString(e));
+        p = nullptr;
+        return false;
+    }
+    if (zero && cudaMemset(p, 0, static_cast<size_t>(n) * sizeof(T)) != cudaSuccess) return false;
+    cap = n;
+    return true;
+}
+
+struct Ctx {
+    bool tried = false, ok = false;
+    int device = 0, nsm = 0;
+    cudaStream_t stream = nullptr;
+    int *d_err = nullptr;
+    float *d_part = nullptr;
+    int64_t part_cap = 0;
+    unsigned *d_cnt = nullptr;
+    int64_t cnt_cap = 0;
+    // staging for host-pointer calls
+    float *d_in = nullptr;
+    int64_t in_cap = 0;
+    uint16_t *d_x = nullptr;
+    int64_t x_cap = 0;
+    float *d_h = nullptr;
+    int64_t h_cap = 0;
+    uint16_t *d_a = nullptr;
+    int64_t a_cap = 0;
+    float *d_o = nullptr;
+    int64_t o_cap = 0;
+    float *d_y = nullptr;
+    int64_t y_cap = 0;
+    GemvJob *d_jobs = nullptr;
+    int64_t jobs_cap = 0;
+    int32_t *d_ids = nullptr;
+    int64_t ids_cap = 0;
+    float *d_w = nullptr;
+    int64_t w_cap = 0;
+    float *d_gb = nullptr;
+    int64_t gb_cap = 0;
+    float *d_db = nullptr;
+    int64_t db_cap = 0;
+    std::vector<GemvJob> h_jobs;
+    int64_t calls = 0;
+    double wait_s = 0;
+};
+
+Ctx &ctx() {
+    static Ctx c;
+    if (!c.tried) {
+        c.tried = true;
+        int n = 0;
+        if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+            cudaGetLastError();
+            return c;
+        }
+        if (cudaGetDevice(&c.device) != cudaSuccess) return c;
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, c.device) != cudaSuccess) return c;
+        c.nsm = prop.multiProcessorCount;
+        if (prop.major < 10) {
+            fprintf(stderr, "onpu: %s (sm_%d%d) is not a B200-class GPU; libonpu targets sm_100a\n", prop.name,
+                    prop.major, prop.minor);
+            return c;
+        }
+        if (cudaStreamCreateWithFlags(&c.stream, cudaStreamNonBlocking) != cudaSuccess) return c;
+        if (cudaMalloc(&c.d_err, sizeof(int)) != cudaSuccess) return c;
+        cudaMemset(c.d_err, 0, sizeof(int));
+        c.ok = true;
+    }
+    return c;
+}
+
+// ------------------------------------------------------------------ matrices on the GPU
+struct GpuMat {
+    GpuMatrix gm;                 // one matrix (expert)
+    int64_t E = 1;
+    uint8_t *d_w = nullptr;       // E * gm.bytes
+    int *d_row_map = nullptr;     // GPU row -> original row (interleaved gate/up), null = identity
+    std::vector<int> src_row;     // host copy of the same map
+    ~GpuMat() {
+        if (d_w) cudaFree(d_w);
+        if (d_row_map) cudaFree(d_row_map);
+    }
+};
+
+// ONPU_PDL=0 turns programmatic dependent launch off (a diagnostic switch; on by default)
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char *e = std::getenv("ONPU_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
+}
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+bool alloc_mat(GpuMat &m, int64_t N, int64_t K, int fmt, int64_t E) {
+    m.gm = make_gpu_matrix(N, round_up(K, 32), fmt);
+    m.E = E;
+    cudaError_t e = cudaMalloc(&m.d_w, static_cast<size_t>(m.gm.bytes * E));
+    if (e != cudaSuccess) {
+        set_err("cudaMalloc of %lld weight bytes: %s", static_cast<long long>(m.gm.bytes * E), cudaGetErrorString(e));
+        m.d_w = nullptr;
+        return false;
+    }
+    return true;
+}
+
+// gate rows [0, N/2) and up rows [N/2, N) interleaved per 16-row strip: strip rows 0-7 gate
+// 8s..8s+7, rows 8-15 up 8s..8s+7, so the GEMV epilogue sees gate_i and up_i in one lane
+bool set_gateup_interleave(GpuMat &m) {
+    const int64_t N = m.gm.N, I = N / 2;
+    if (N % 2 || I % 8) return false;
+    m.src_row.resize(static_cast<size_t>(N));
+    for (int64_t rho = 0; rho < N; ++rho) {
+        const int64_t strip = rho / 16, rr = rho % 16;
+        m.src_row[rho] = static_cast<int>(rr < 8 ? 8 * strip + rr : I + 8 * strip + rr - 8);
+    }
+    if (cudaMalloc(&m.d_row_map, sizeof(int) * N) != cudaSuccess) return false;
+    return cudaMemcpy(m.d_row_map, m.src_row.data(), sizeof(int) * N, cudaMemcpyHostToDevice) == cudaSuccess;
+}
+
+// ------------------------------------------------------------------ GEMV driver
+int choose_workers(const Ctx &c, int fmt, int ntiles, int T) {
+    const int occ = gemv_ctas_per_sm(fmt, ntiles), per_wave = c.nsm * gemv_warps_per_cta();
+    if (T <= per_wave) return std::max(1, T);
+    const int k = std::min(occ, std::max(1, T / (per_wave * 2)));   // >= 2 chunks per warp, whole waves
+    return per_wave * k;
+}
+
+bool ensure_scratch(Ctx &c, int workers, int ntiles, int counters) {
+    const int64_t pf = static_cast<int64_t>(workers) * gemv_part_floats_per_worker(ntiles);
+    if (!grow(c.d_part, c.part_cap, pf)) return false;
+    if (!grow(c.d_cnt, c.cnt_cap, std::max<int64_t>(counters, 1024), true)) return false;
+    return true;
+}
+
+int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntiles, int epi, const uint16_t *x,
+             int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl) {
+    const int T = njobs * m.gm.row_groups * m.gm.chunks;
+    if (T == 0) return 0;
+    const int W = choose_workers(c, m.gm.fmt, ntiles, T);
+    if (!ensure_scratch(c, W, ntiles, njobs * m.gm.row_groups)) return -1;
+    GemvParams p{};
+    p.jobs = d_jobs;
+    p.njobs = njobs;
+    p.N = static_cast<int>(m.gm.N);
+    p.K = static_cast<int>(m.gm.K);
+    p.row_groups = m.gm.row_groups;
+    p.chunks = m.gm.chunks;
+    p.total_chunks = T;
+    p.workers = W;
+    p.x = x;
+    p.ldx = ldx;
+    p.y = y;
+    p.ldy = ldy;
+    p.row_map = epi == kEpiSwiGLU ? nullptr : m.d_row_map;
+    p.part = c.d_part;
+    p.counters = c.d_cnt;
+    p.err = c.d_err;
+    p.jobs_ready = 1;
+    ONPU_CUDA(gemv_launch(m.gm.fmt, ntiles, epi, p, s, pdl), -1);
+    ++c.calls;
+    return 0;
+}
+
+// after a synchronising host call: surface device-side timeouts and reset the split-row counters
+int check_device_err(Ctx &c) {
+    int h = 0;
+    if (cudaMemcpy(&h, c.d_err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess) {
+        set_err("reading the device status failed: %s", cudaGetErrorString(cudaGetLastError()));
+        return -1;
+    }
+    if (h) {
+        cudaMemset(c.d_err, 0, sizeof(int));
+        if (c.d_cnt) cudaMemset(c.d_cnt, 0, sizeof(unsigned) * c.cnt_cap);
+        set_err("a GEMV kernel timed out waiting for its weight copies (device status %d)", h);
+        return -2;
+    }
+    return 0;
+}
+
+// stage host fp32 rows [rows][K] -> bf16 [rows][Kp] (zero past K) on the library stream
+bool stage_x(Ctx &c, const float *x, int64_t rows, int64_t K, int64_t Kp) {
+    if (!grow(c.d_in, c.in_cap, rows * K) || !grow(c.d_x, c.x_cap, rows * Kp)) return false;
+    if (cudaMemcpyAsync(c.d_in, x, sizeof(float) * rows * K, cudaMemcpyHostToDevice, c.stream) != cudaSuccess) return false;
+    if (Kp != K && cudaMemsetAsync(c.d_x, 0, sizeof(uint16_t) * rows * Kp, c.stream) != cudaSuccess) return false;
+    return f32_to_bf16_launch(c.d_in, rows, K, K, c.d_x, Kp, c.stream) == cudaSuccess;
+}
+
+bool finish(Ctx &c) {
+    const auto t0 = std::chrono::steady_clock::now();
+    cudaError_t e = cudaStreamSynchronize(c.stream);
+    c.wait_s += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    if (e != cudaSuccess) {
+        set_err("kernel failed: %s", cudaGetErrorString(e));
+        return false;
+    }
+    return check_device_err(c) == 0;
+}
+
+// (token, slot) pairs grouped by expert (ascending id, then arrival order), <= 16 per job
+void build_expert_jobs(const GpuMat &m, const int32_t *ids, int64_t T, int k, bool x_per_slot, bool x_by_slot,
+                       std::vector<GemvJob> &jobs, int &ntiles) {
+    jobs.clear();
+    ntiles = 1;
+    std::vector<int64_t> count(static_cast<size_t>(m.E) + 1, 0);
+    for (int64_t i = 0; i < T * k; ++i) ++count[ids[i] + 1];
+    for (int64_t e = 0; e < m.E; ++e) count[e + 1] += count[e];
+    std::vector<int64_t> order(static_cast<size_t>(T * k));
+    std::vector<int64_t> pos(count.begin(), count.end() - 1);
+    for (int64_t i = 0; i < T * k; ++i) order[pos[ids[i]]++] = i;
+    for (int64_t e = 0; e < m.E; ++e) {
+        for (int64_t a = count[e]; a < count[e + 1]; a += kMaxTokensPerJob) {
+            GemvJob jb{};
+            jb.w = m.d_w + e * m.gm.bytes;
+            jb.m = static_cast<int>(std::min<int64_t>(kMaxTokensPerJob, count[e + 1] - a));
+            for (int n = 0; n < jb.m; ++n) {
+                const int64_t slot = order[a + n];
+                jb.xrow[n] = static_cast<int>(x_by_slot ? slot : (x_per_slot ? slot : slot / k));
+                jb.yrow[n] = static_cast<int>(slot);
+            }
+            if (jb.m > 8) ntiles = 2;
+            jobs.push_back(jb);
+        }
+    }
+}
+
+bool upload_jobs(Ctx &c, const std::vector<GemvJob> &jobs) {
+    if (!grow(c.d_jobs, c.jobs_cap, static_cast<int64_t>(jobs.size()))) return false;
+    return cudaMemcpyAsync(c.d_jobs, jobs.data(), sizeof(GemvJob) * jobs.size(), cudaMemcpyHostToDevice, c.stream) ==
+           cudaSuccess;
+}
+
+// ------------------------------------------------------------------ handles
+struct JobSet {
+    GemvJob *d = nullptr;
+    int n = 0, ntiles = 1;
+};
+
+struct DenseH {
+    Geometry geo;                 // reference upload geometry (8 columns); !ok for int4 ingest
+    int fmt = kFmtQ4S;
+    GpuMat mat;
+    uint8_t *h_buf = nullptr;     // pinned stream-order upload buffer
+    bool gateup = false;
+    std::map<int64_t, JobSet> jobs;
+    ~DenseH() {
+        if (h_buf) cudaFreeHost(h_buf);
+        for (auto &kv : jobs) cudaFree(kv.second.d);
+    }
+};
+
+struct BankH {
+    Geometry geo;
+    int fmt = kFmtQ4S;
+    GpuMat mat;
+    uint8_t *h_buf = nullptr;     // E * geo.nbytes
+    bool owns_buf = true;
+    ~BankH() {
+        if (h_buf && owns_buf) cudaFreeHost(h_buf);
+    }
+};
+
+struct FfnH {
+    BankH *gu = nullptr, *dn = nullptr;
+    bool fused = false;           // gate/up interleaved on the GPU: SwiGLU fused into the GEMV
+    ~FfnH() {
+        delete gu;
+        delete dn;
+    }
+};
+
+JobSet *dense_jobs(DenseH *d, int64_t rows) {
+    auto it = d->jobs.find(rows);
+    if (it != d->jobs.end()) return &it->second;
+    JobSet js;
+    js.n = static_cast<int>((rows + kMaxTokensPerJob - 1) / kMaxTokensPerJob);
+    std::vector<GemvJob> h(static_cast<size_t>(js.n));
+    for (int j = 0; j < js.n; ++j) {
+        GemvJob &jb = h[j];
+        jb.w = d->mat.d_w;
+        jb.m = static_cast<int>(std::min<int64_t>(kMaxTokensPerJob, rows - static_cast<int64_t>(j) * kMaxTokensPerJob));
+        for (int n = 0; n < jb.m; ++n) jb.xrow[n] = jb.yrow[n] = j * kMaxTokensPerJob + n;
+        if (jb.m > 8) js.ntiles = 2;
+    }
+    if (cudaMalloc(&js.d, sizeof(GemvJob) * js.n) != cudaSuccess ||
+        cudaMemcpy(js.d, h.data(), sizeof(GemvJob) * js.n, cudaMemcpyHostToDevice) != cudaSuccess) {
+        set_err("allocating GEMV descriptors failed");
+        return nullptr;
+    }
+    return &(d->jobs[rows] = js);
+}
+
+// stream-order upload (device copy at d_src) -> GPU layout of expert/matrix at dst
+cudaError_t repack_stream(const Geometry &g, const GpuMat &m, const uint8_t *d_src, uint8_t *dst, cudaStream_t s) {
+    RepackParams p{};
+    p.src_kind = kSrcStream;
+    p.src = d_src;
+    p.src_row = nullptr;
+    p.N = g.N;
+    p.K = m.gm.K;            // padded to 32; the stream buffer holds the quantised padding
+    p.fmt = m.gm.fmt;
+    p.R = g.R;
+    p.S = g.S;
+    p.tiles = g.tiles;
+    p.kc = g.kc;
+    p.ks = g.ks;
+    p.rows_col = g.rows_col;
+    p.cb = g.cb;
+    p.pkt = g.pkt();
+    p.dst = dst;
+    if (!m.src_row.empty()) {
+        // the interleave map is also the row_map on the device
+        p.src_row = m.d_row_map;
+    }
+    return repack_launch(p, s);
+}
+
+BankH *new_bank(int64_t N, int64_t K, int64_t E, int ncols, int sym) {
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    Geometry g(N, K, ncols, sym != 0);
+    if (!g.ok || E <= 0) {
+        set_err("no %d-column geometry for [%lld, %lld]", ncols, static_cast<long long>(N), static_cast<long long>(K));
+        return nullptr;
+    }
+    auto *b = new BankH;
+    b->geo = g;
+    b->fmt = sym ? kFmtQ4S : kFmtQ4NX;
+    if (!alloc_mat(b->mat, N, K, b->fmt, E)) {
+        delete b;
+        return nullptr;
+    }
+    if (cudaHostAlloc(&b->h_buf, static_cast<size_t>(g.nbytes * E), cudaHostAllocDefault) != cudaSuccess) {
+        set_err("pinned host buffer of %lld bytes", static_cast<long long>(g.nbytes * E));
+        delete b;
+        return nullptr;
+    }
+    std::memset(b->h_buf, 0, static_cast<size_t>(g.nbytes * E));
+    return b;
+}
+
+bool sync_bank(BankH *b) {
+    Ctx &c = ctx();
+    const int64_t per = b->geo.nbytes;
+    const int64_t batch = std::max<int64_t>(1, std::min<int64_t>(b->mat.E, (256LL << 20) / std::max<int64_t>(per, 1)));
+    uint8_t *tmp = nullptr;
+    ONPU_CUDA(cudaMalloc(&tmp, static_cast<size_t>(per * batch)), false);
+    bool ok = true;
+    for (int64_t e0 = 0; e0 < b->mat.E && ok; e0 += batch) {
+        const int64_t n = std::min(batch, b->mat.E - e0);
+        ok = cudaMemcpyAsync(tmp, b->h_buf + e0 * per, static_cast<size_t>(per * n), cudaMemcpyHostToDevice, c.stream) ==
+             cudaSuccess;
+        for (int64_t e = 0; e < n && ok; ++e)
+            ok = repack_stream(b->geo, b->mat, tmp + e * per, b->mat.d_w + (e0 + e) * b->mat.gm.bytes, c.stream) ==
+                 cudaSuccess;
+        ok = ok && cudaStreamSynchronize(c.stream) == cudaSuccess;
+    }
+    cudaFree(tmp);
+    if (!ok) set_err("bank upload failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return ok;
+}
+
+bool valid_ids(const int32_t *ids, int64_t n, int64_t E) {
+    for (int64_t i = 0; i < n; ++i)
+        if (ids[i] < 0 || ids[i] >= E) {
+            set_err("expert id %d out of range [0, %lld)", ids[i], static_cast<long long>(E));
+            return false;
+        }
+    return true;
+}
+
+// routed-expert FFN on the device; inputs already validated. fused: gate_up bank interleaved,
+// SwiGLU in the GEMV epilogue (act 0 and no biases only).
+bool moe_ffn_impl(BankH *gu, BankH *dn, const float *x, int64_t T, const int32_t *ids, int k, const float *w, int act,
+                  float alpha, float limit, const float *gu_bias, const float *dn_bias, float *y, bool fused) {
+    Ctx &c = ctx();
+    const int64_t Ng = gu->geo.N, I = Ng / 2, Nd = dn->geo.N, Kg = gu->geo.K, Kgp = gu->mat.gm.K;
+    const int64_t Kdp = dn->mat.gm.K, TK = T * k;
+    if (dn->geo.K != I) {
+        set_err("down bank K (%lld) != gate_up N/2 (%lld)", static_cast<long long>(dn->geo.K), static_cast<long long>(I));
+        return false;
+    }
+    if (!stage_x(c, x, T, Kg, Kgp)) return false;
+    std::vector<GemvJob> jg, jd;
+    int ntg = 1, ntd = 1;
+    build_expert_jobs(gu->mat, ids, T, k, false, false, jg, ntg);
+    build_expert_jobs(dn->mat, ids, T, k, false, true, jd, ntd);
+    std::vector<GemvJob> all(jg);
+    all.insert(all.end(), jd.begin(), jd.end());
+    if (!upload_jobs(c, all)) return false;
+    if (!grow(c.d_a, c.a_cap, TK * Kdp) || !grow(c.d_o, c.o_cap, TK * Nd) || !grow(c.d_y, c.y_cap, T * Nd) ||
+        !grow(c.d_ids, c.ids_cap, TK) || !grow(c.d_w, c.w_cap, TK))
+        return false;
+    ONPU_CUDA(cudaMemcpyAsync(c.d_ids, ids, sizeof(int32_t) * TK, cudaMemcpyHostToDevice, c.stream), false);
+    ONPU_CUDA(cudaMemcpyAsync(c.d_w, w, sizeof(float) * TK, cudaMemcpyHostToDevice, c.stream), false);
+    if (Kdp != I) ONPU_CUDA(cudaMemsetAsync(c.d_a, 0, sizeof(uint16_t) * TK * Kdp, c.stream), false);
+    const float *d_gb = nullptr, *d_db = nullptr;
+    if (gu_bias) {
+        if (!grow(c.d_gb, c.gb_cap, gu->mat.E * Ng)) return false;
+        ONPU_CUDA(cudaMemcpyAsync(c.d_gb, gu_bias, sizeof(float) * gu->mat.E * Ng, cudaMemcpyHostToDevice, c.stream), false);
+        d_gb = c.d_gb;
+    }
+    if (dn_bias) {
+        if (!grow(c.d_db, c.db_cap, dn->mat.E * Nd)) return false;
+        ONPU_CUDA(cudaMemcpyAsync(c.d_db, dn_bias, sizeof(float) * dn->mat.E * Nd, cudaMemcpyHostToDevice, c.stream), false);
+        d_db = c.d_db;
+    }
+    if (fused && act == 0 && !gu_bias) {
+        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, kEpiSwiGLU, c.d_x, Kgp, c.d_a, Kdp,
+                     c.stream, false))
+            return false;
+    } else {
+        if (!grow(c.d_h, c.h_cap, TK * Ng)) return false;
+        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, kEpiF32, c.d_x, Kgp, c.d_h, Ng, c.stream,
+                     false))
+            return false;
+        ONPU_CUDA(moe_act_launch(c.d_h, Ng, TK, Ng, c.d_ids, d_gb, act, alpha, limit, c.d_a, Kdp, c.stream), false);
+    }
+    if (run_gemv(c, dn->mat, c.d_jobs + jg.size(), static_cast<int>(jd.size()), ntd, kEpiF32, c.d_a, Kdp, c.d_o, Nd,
+                 c.stream, false))
+        return false;
+    ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, c.d_ids, c.d_w, d_db, c.d_y, Nd, c.stream), false);
+    ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * T * Nd, cudaMemcpyDeviceToHost, c.stream), false);
+    return finish(c);
+}
+
+}  // namespace
+
+// ======================================================================== part 1
+extern "C" {
+
+int onpu_ok(void) { return ctx().ok ? 1 : 0; }
+int onpu_batched_ok(void) { return onpu_ok(); }
+
+void onpu_stats(int64_t *calls, double *wait_s) {
+    Ctx &c = ctx();
+    *calls = c.calls;
+    *wait_s = c.wait_s;
+}
+
+int onpu_has_shape(int tiles, int kc, int batched) {
+    (void)tiles;
+    (void)kc;
+    (void)batched;
+    return onpu_ok();
+}
+
+void onpu_geometry2(int64_t N, int64_t K, int ncols, int sym, int64_t *out) {
+    const Geometry g(N, K, ncols, sym != 0);
+    const int64_t v[8] = {g.R, g.S, g.tiles, g.kc, g.ks, g.rows_col, g.cb, g.nbytes};
+    for (int i = 0; i < 8; ++i) out[i] = g.ok ? v[i] : 0;
+}
+
+void onpu_geometry(int64_t N, int64_t K, int ncols, int64_t *out) { onpu_geometry2(N, K, ncols, 0, out); }
+
+// ---- dense
+void *onpu_dense_new2(int64_t N, int64_t K, int sym) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    Geometry g(N, K, kNC, sym != 0);
+    if (!g.ok) {
+        set_err("no 8-column geometry for [%lld, %lld]", static_cast<long long>(N), static_cast<long long>(K));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *d = new DenseH;
+    d->geo = g;
+    d->fmt = sym ? kFmtQ4S : kFmtQ4NX;
+    if (!alloc_mat(d->mat, N, K, d->fmt, 1) ||
+        cudaHostAlloc(&d->h_buf, static_cast<size_t>(g.nbytes), cudaHostAllocDefault) != cudaSuccess) {
+        if (!t_has_err) set_err("pinned host buffer of %lld bytes", static_cast<long long>(g.nbytes));
+        delete d;
+        return nullptr;
+    }
+    std::memset(d->h_buf, 0, static_cast<size_t>(g.nbytes));
+    return d;
+}
+
+void *onpu_dense_new(int64_t N, int64_t K) { return onpu_dense_new2(N, K, 0); }
+uint8_t *onpu_dense_buf(void *h) { return static_cast<DenseH *>(h)->h_buf; }
+int64_t onpu_dense_bytes(void *h) { return static_cast<DenseH *>(h)->geo.nbytes; }
+
+void onpu_dense_sync(void *h) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    if (!d->h_buf) {
+        set_err("onpu_dense_sync: this matrix takes int4 uploads (onpu_dense_load_int4)");
+        return;
+    }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    uint8_t *tmp = nullptr;
+    ONPU_CUDA(cudaMalloc(&tmp, static_cast<size_t>(d->geo.nbytes)), );
+    cudaError_t e = cudaMemcpyAsync(tmp, d->h_buf, static_cast<size_t>(d->geo.nbytes), cudaMemcpyHostToDevice, c.stream);
+    if (e == cudaSuccess) e = repack_stream(d->geo, d->mat, tmp, d->mat.d_w, c.stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c.stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) set_err("onpu_dense_sync: %s", cudaGetErrorString(e));
+}
+
+void onpu_dense_mv(void *h, const float *x, int64_t rows, float *y) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    if (rows <= 0) return;
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int64_t K = d->mat.gm.K, N = d->mat.gm.N;
+    const int64_t Kin = d->geo.ok ? d->geo.K : K;
+    JobSet *js = dense_jobs(d, rows);
+    if (!js || !stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
+    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
+    ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * rows * N, cudaMemcpyDeviceToHost, c.stream), );
+    finish(c);
+}
+
+void onpu_dense_free(void *h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaDeviceSynchronize();
+    delete static_cast<DenseH *>(h);
+}
+
+// ---- banks
+void *onpu_bank_new2(int64_t N, int64_t K, int64_t E, int ncols, int sym) {
+    clear_err();
+    std::lock_guard<std::mutex> lk(g_mu);
+    return new_bank(N, K, E, ncols, sym);
+}
+void *onpu_bank_new(int64_t N, int64_t K, int64_t E, int ncols) { return onpu_bank_new2(N, K, E, ncols, 0); }
+uint8_t *onpu_bank_buf(void *h) { return static_cast<BankH *>(h)->h_buf; }
+int64_t onpu_bank_expert_bytes(void *h) { return static_cast<BankH *>(h)->geo.nbytes; }
+
+void onpu_bank_sync(void *h) {
+    clear_err();
+    std::lock_guard<std::mutex> lk(g_mu);
+    sync_bank(static_cast<BankH *>(h));
+}
+
+void onpu_bank_free(void *h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaDeviceSynchronize();
+    delete static_cast<BankH *>(h);
+}
+
+void onpu_bank_run(void *h, const float *x, int x_per_slot, int64_t T, const int32_t *ids, int k, float *y) {
+    clear_err();
+    auto *b = static_cast<BankH *>(h);
+    if (T <= 0 || k <= 0) return;
+    if (!valid_ids(ids, T * k, b->mat.E)) return;
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int64_t N = b->geo.N, Kp = b->mat.gm.K;
+    const int64_t xrows = x_per_slot ? T * k : T;
+    if (!stage_x(c, x, xrows, b->geo.K, Kp)) return;
+    std::vector<GemvJob> jobs;
+    int nt = 1;
+    build_expert_jobs(b->mat, ids, T, k, x_per_slot != 0, false, jobs, nt);
+    if (!upload_jobs(c, jobs) || !grow(c.d_y, c.y_cap, T * k * N)) return;
+    if (run_gemv(c, b->mat, c.d_jobs, static_cast<int>(jobs.size()), nt, kEpiF32, c.d_x, Kp, c.d_y, N, c.stream, false))
+        return;
+    ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * T * k * N, cudaMemcpyDeviceToHost, c.stream), );
+    finish(c);
+}
+
+// ---- MoE
+void onpu_moe_ffn(void *gu, void *dn, const float *x, int64_t T, const int32_t *ids, int k, const float *w, int act,
+                  float alpha, float limit, const float *gu_bias, const float *dn_bias, float *y) {
+    clear_err();
+    auto *g = static_cast<BankH *>(gu);
+    auto *d = static_cast<BankH *>(dn);
+    if (T <= 0) return;
+    if (!valid_ids(ids, T * k, std::min(g->mat.E, d->mat.E))) return;
+    std::lock_guard<std::mutex> lk(g_mu);
+    moe_ffn_impl(g, d, x, T, ids, k, w, act, alpha, limit, gu_bias, dn_bias, y, !g->mat.src_row.empty());
+}
+
+void onpu_moe_act(const float *h, int64_t rows, int64_t Ng, const int32_t *ids, const float *gu_bias, int act,
+                  float alpha, float limit, float *a) {
+    const int64_t I = Ng / 2;
+    std::vector<float> tmp(static_cast<size_t>(Ng));
+    for (int64_t r = 0; r < rows; ++r) {
+        const float *hr = h + r * Ng;
+        if (gu_bias) {
+            const float *b = gu_bias + static_cast<int64_t>(ids[r]) * Ng;
+            for (int64_t i = 0; i < Ng; ++i) tmp[i] = hr[i] + b[i];
+            hr = tmp.data();
+        }
+        float *ar = a + r * I;
+        for (int64_t i = 0; i < I; ++i) {
+            if (act == 1) {
+                const float gt = std::min(hr[2 * i], limit);
+                const float up = std::max(-limit, std::min(hr[2 * i + 1], limit));
+                ar[i] = (up + 1.f) * gt / (1.f + std::exp(-alpha * gt));
+            } else {
+                ar[i] = hr[i] / (1.f + std::exp(-hr[i])) * hr[I + i];
+            }
+        }
+    }
+}
+
+void onpu_moe_sum(const float *o, int64_t T, int k, int64_t N, const int32_t *ids, const float *w, const float *bias,
+                  float *y) {
+    for (int64_t t = 0; t < T; ++t) {
+        float *yt = y + t * N;
+        std::fill(yt, yt + N, 0.f);
+        for (int j = 0; j < k; ++j) {
+            const int64_t r = t * k + j;
+            const float wr = w[r], *orow = o + r * N;
+            const float *b = bias ? bias + static_cast<int64_t>(ids[r]) * N : nullptr;
+            for (int64_t i = 0; i < N; ++i) yt[i] += wr * (orow[i] + (b ? b[i] : 0.f));
+        }
+    }
+}
+
+// ---- fused FFN
+void *onpu_ffn_new(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t E, int sym) {
+    clear_err();
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *f = new FfnH;
+    f->gu = new_bank(Ng, Kg, E, 1, sym);
+    f->dn = f->gu ? new_bank(Nd, Kd, E, 1, sym) : nullptr;
+    if (!f->gu || !f->dn) {
+        delete f;
+        return nullptr;
+    }
+    f->fused = Kd == Ng / 2 && set_gateup_interleave(f->gu->mat);
+    return f;
+}
+void *onpu_ffn_gu(void *h) { return static_cast<FfnH *>(h)->gu; }
+void *onpu_ffn_dn(void *h) { return static_cast<FfnH *>(h)->dn; }
+int onpu_ffn_fused(void *h) { return static_cast<FfnH *>(h)->fused ? 1 : 0; }
+void onpu_ffn_perm(void *h, int32_t *out) {
+    const int64_t n = static_cast<FfnH *>(h)->gu->geo.N;
+    for (int64_t r = 0; r < n; ++r) out[r] = static_cast<int32_t>(r);
+}
+void onpu_ffn_free(void *h) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaDeviceSynchronize();
+    delete static_cast<FfnH *>(h);
+}
+
+int onpu_ffn_run(void *h, const float *x, const int32_t *ids, int k, const float *w, float *y) {
+    return onpu_ffn_run_many(h, x, 1, ids, k, w, y);
+}
+
+int onpu_ffn_run_many(void *h, const float *x, int64_t T, const int32_t *ids, int k, const float *w, float *y) {
+    clear_err();
+    auto *f = static_cast<FfnH *>(h);
+    if (T <= 0) return 1;
+    if (!valid_ids(ids, T * k, f->gu->mat.E)) return 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    return moe_ffn_impl(f->gu, f->dn, x, T, ids, k, w, 0, 0.f, 0.f, nullptr, nullptr, y, f->fused) ? 1 : 0;
+}
+
+// ---- codec
+int64_t onpu_pack(const float *W, int64_t N, int64_t K, int ncols, int sym, uint8_t *out, int threads) {
+    const Geometry g(N, K, ncols, sym != 0);
+    if (!g.ok) return 0;
+    pack_stream(g, W, out, threads);
+    return g.nbytes;
+}
+
+void onpu_quant_dequant(const float *W, int64_t N, int64_t K, int sym, float *out, int threads) {
+    quant_dequant(W, N, K, sym != 0, out, threads);
+}
+
+// ======================================================================== part 2
+const char *onpu_last_error(void) { return t_has_err ? t_err.c_str() : nullptr; }
+
+int onpu_check_device(void) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return -1;
+    }
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        set_err("device error: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return check_device_err(c);
+}
+
+void *onpu_dense_new_int4(int64_t N, int64_t K, int gateup) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    if (N <= 0 || K <= 0 || K % 32) {
+        set_err("onpu_dense_new_int4: need N > 0 and K %% 32 == 0 (got %lld, %lld)", static_cast<long long>(N),
+                static_cast<long long>(K));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *d = new DenseH;
+    d->fmt = kFmtQ4F16;
+    d->gateup = gateup != 0;
+    if (!alloc_mat(d->mat, N, K, d->fmt, 1)) {
+        delete d;
+        return nullptr;
+    }
+    if (d->gateup && !set_gateup_interleave(d->mat)) {
+        set_err("onpu_dense_new_int4: gate/up matrix needs N/2 %% 8 == 0");
+        delete d;
+        return nullptr;
+    }
+    return d;
+}
+
+int onpu_dense_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    if (d->fmt != kFmtQ4F16) {
+        set_err("onpu_dense_load_int4: matrix was not created by onpu_dense_new_int4");
+        return -1;
+    }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int64_t N = d->mat.gm.N, K = d->mat.gm.K;
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    uint8_t *tq = nullptr;
+    uint16_t *ts = nullptr;
+    const uint8_t *sq = qk;
+    const uint16_t *ss = scales;
+    if (!on_device) {
+        ONPU_CUDA(cudaMalloc(&tq, static_cast<size_t>(N * K / 2)), -1);
+        ONPU_CUDA(cudaMalloc(&ts, static_cast<size_t>(N * K / 32) * 2), -1);
+        ONPU_CUDA(cudaMemcpyAsync(tq, qk, static_cast<size_t>(N * K / 2), cudaMemcpyHostToDevice, s), -1);
+        ONPU_CUDA(cudaMemcpyAsync(ts, scales, static_cast<size_t>(N * K / 32) * 2, cudaMemcpyHostToDevice, s), -1);
+        sq = tq;
+        ss = ts;
+    }
+    RepackParams p{};
+    p.src_kind = kSrcInt4K;
+    p.src = sq;
+    p.scales = ss;
+    p.src_row = d->mat.d_row_map;
+    p.N = N;
+    p.K = K;
+    p.fmt = kFmtQ4F16;
+    p.dst = d->mat.d_w;
+    cudaError_t e = repack_launch(p, s);
+    if (e == cudaSuccess && (!on_device || !stream)) e = cudaStreamSynchronize(s);
+    if (tq) cudaFree(tq);
+    if (ts) cudaFree(ts);
+    if (e != cudaSuccess) {
+        set_err("onpu_dense_load_int4: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+int onpu_dense_info(void *h, int64_t *out4) {
+    auto *d = static_cast<DenseH *>(h);
+    out4[0] = d->fmt;
+    out4[1] = d->mat.gm.N;
+    out4[2] = d->mat.gm.K;
+    out4[3] = d->mat.gm.bytes;
+    return 0;
+}
+
+int onpu_dense_prepare(void *h, int64_t rows) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    JobSet *js = dense_jobs(d, rows);
+    if (!js) return -1;
+    const int T = js->n * d->mat.gm.row_groups * d->mat.gm.chunks;
+    const int W = choose_workers(c, d->mat.gm.fmt, js->ntiles, T);
+    return ensure_scratch(c, W, js->ntiles, js->n * d->mat.gm.row_groups) ? 0 : -1;
+}
+
+int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    if (rows <= 0) return 0;
+    if (epi < kEpiF32 || epi > kEpiSwiGLU || (epi == kEpiSwiGLU && !d->gateup)) {
+        set_err("onpu_dense_mv_dev: bad epilogue %d for this matrix", epi);
+        return -1;
+    }
+    if (d->geo.ok && d->geo.K != d->mat.gm.K) {
+        set_err("onpu_dense_mv_dev: K must be a multiple of 32");
+        return -1;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < d->mat.gm.K) {
+        set_err("onpu_dense_mv_dev: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+        return -1;
+    }
+    if (ldy < (epi == kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
+        set_err("onpu_dense_mv_dev: y row stride %lld is shorter than the output row", static_cast<long long>(ldy));
+        return -1;
+    }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    JobSet *js = dense_jobs(d, rows);
+    if (!js) return -1;
+    return run_gemv(c, d->mat, js->d, js->n, js->ntiles, epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
+                    static_cast<cudaStream_t>(stream), pdl_enabled());
+}
+
+int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    ONPU_CUDA(unpack_gpu_launch(d->mat.d_w, d->mat.gm.N, d->mat.gm.K, d->mat.gm.fmt, q, scales, mins,
+                                static_cast<cudaStream_t>(stream)),
+              -1);
+    return 0;
+}
+
+}  // extern "C"

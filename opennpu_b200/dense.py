@@ -1,0 +1,114 @@
+"""Device-resident dense int4 matrices driven with torch CUDA tensors (libonpu's _dev entry points).
+
+``DenseMatrix`` owns one libonpu dense handle. Weights come from int4 packed along K (two's
+complement, element 2j in the low nibble of byte j) with fp16 scales per 32 (``from_int4``), or
+from the reference's stream-order upload buffer (``from_stream``, formats q4nx / q4s). ``mv``
+runs y = x . W^T on the current torch stream, asynchronously.
+"""
+import numpy as np
+import torch
+
+from . import libonpu as L
+
+EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
+FMT_Q4NX, FMT_Q4S, FMT_Q4F16 = 0, 1, 2
+
+
+def _stream_ptr(stream=None):
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+class DenseMatrix:
+    def __init__(self, handle, N, K, fmt, gateup=False):
+        self.h, self.N, self.K, self.fmt, self.gateup = handle, N, K, fmt, gateup
+
+    # ---------------------------------------------------------------- construction
+    @classmethod
+    def from_int4(cls, qk, scales, gateup=False, stream=None):
+        """qk: uint8 [N, K/2] packed int4, scales: fp16 (or its uint16 bits) [N, K/32]; CUDA or CPU
+        tensors. gateup: rows [0, N/2) gate, [N/2, N) up (enables EPI_SWIGLU)."""
+        lib = L.require_device()
+        N, K = qk.shape[0], qk.shape[1] * 2
+        h = lib.onpu_dense_new_int4(N, K, int(gateup))
+        if not h:
+            raise L.OnpuError(f"onpu_dense_new_int4: {L.last_error()}")
+        m = cls(h, N, K, FMT_Q4F16, gateup)
+        m.load_int4(qk, scales, stream)
+        return m
+
+    def load_int4(self, qk, scales, stream=None):
+        lib = L.load()
+        qk = qk.contiguous()
+        sc = scales.contiguous().view(torch.int16) if scales.dtype == torch.float16 else scales.contiguous()
+        on_dev = qk.is_cuda
+        if on_dev:
+            rc = lib.onpu_dense_load_int4(self.h, qk.data_ptr(), sc.data_ptr(), 1, _stream_ptr(stream))
+        else:
+            qn, sn = qk.numpy(), sc.numpy()
+            rc = lib.onpu_dense_load_int4(self.h, qn.ctypes.data, sn.ctypes.data, 0, None)
+        L.check(rc, "onpu_dense_load_int4")
+
+    @classmethod
+    def from_stream(cls, N, K, sym, packed):
+        """The reference upload protocol: onpu_dense_new2 + fill onpu_dense_buf + onpu_dense_sync."""
+        lib = L.require_device()
+        h = lib.onpu_dense_new2(N, K, int(sym))
+        if not h:
+            raise L.OnpuError(f"onpu_dense_new2: {L.last_error()}")
+        nb = lib.onpu_dense_bytes(h)
+        buf = np.ctypeslib.as_array(lib.onpu_dense_buf(h), shape=(nb,))
+        buf[:] = np.asarray(packed, np.uint8)
+        lib.onpu_dense_sync(h)
+        if L.last_error():
+            raise L.OnpuError(L.last_error())
+        return cls(h, N, K, FMT_Q4S if sym else FMT_Q4NX)
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            L.load().onpu_dense_free(self.h)
+            self.h = None
+
+    # ---------------------------------------------------------------- use
+    def info(self):
+        out = (L.C.c_int64 * 4)()
+        L.load().onpu_dense_info(self.h, out)
+        return tuple(out)
+
+    @property
+    def nbytes(self):
+        return self.info()[3]
+
+    def prepare(self, rows):
+        L.check(L.load().onpu_dense_prepare(self.h, rows), "onpu_dense_prepare")
+
+    def mv(self, x, out=None, epi=EPI_F32, stream=None):
+        """x: bf16 CUDA [M, K] (row stride % 8 == 0) -> [M, N] fp32 (EPI_F32), bf16 (EPI_BF16) or
+        [M, N/2] bf16 silu(gate) * up (EPI_SWIGLU)."""
+        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+        M = x.shape[0]
+        if out is None:
+            ncol = self.N // 2 if epi == EPI_SWIGLU else self.N
+            out = torch.empty(M, ncol, device=x.device, dtype=torch.float32 if epi == EPI_F32 else torch.bfloat16)
+        rc = L.load().onpu_dense_mv_dev(self.h, x.data_ptr(), x.stride(0), M, out.data_ptr(), out.stride(0), epi,
+                                        _stream_ptr(stream))
+        L.check(rc, "onpu_dense_mv_dev")
+        return out
+
+    def unpack(self):
+        """GPU layout -> (codes uint8 [N, K], scale bits int16 [N, K/32], min bits or None), in GPU
+        row order (a gate/up matrix is interleaved per 16 rows)."""
+        dev = torch.device("cuda")
+        q = torch.zeros(self.N, self.K, dtype=torch.uint8, device=dev)
+        s = torch.zeros(self.N, self.K // 32, dtype=torch.int16, device=dev)
+        m = torch.zeros_like(s) if self.fmt == FMT_Q4NX else None
+        rc = L.load().onpu_dense_unpack_dev(self.h, q.data_ptr(), s.data_ptr(), 0 if m is None else m.data_ptr(),
+                                            _stream_ptr())
+        L.check(rc, "onpu_dense_unpack_dev")
+        torch.cuda.synchronize()
+        return q, s, m
+
+
+def check_device():
+    """Synchronise and raise if a kernel reported a timed-out wait."""
+    L.check(L.load().onpu_check_device(), "device status")

@@ -1,0 +1,110 @@
+"""ctypes binding of the in-tree libonpu.so (the onpu_* C ABI of include/onpu.h).
+
+The argtypes of the reference-compatible part mirror the reference's own binding
+(opennpu/native/npu4/model.py:281-335) so the same calls work unchanged. There is no CPU
+fallback: ``load()`` raises when the library is missing, and the device paths raise when
+``onpu_ok()`` is 0 (no B200).
+"""
+import ctypes as C
+import os
+from pathlib import Path
+
+LIB_PATH = Path(os.environ.get("OPENNPU_LIBONPU", Path(__file__).resolve().parent / "_lib" / "libonpu.so"))
+
+P, I64, I32, F = C.c_void_p, C.c_int64, C.c_int, C.POINTER(C.c_float)
+U8P, U16P, I32P, I64P = C.POINTER(C.c_uint8), C.POINTER(C.c_uint16), C.POINTER(C.c_int32), C.POINTER(C.c_int64)
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    # ---- reference ABI (onpu_api.cpp / onpu_cpu.cpp)
+    "onpu_ok": (I32, []),
+    "onpu_batched_ok": (I32, []),
+    "onpu_stats": (None, [I64P, C.POINTER(C.c_double)]),
+    "onpu_has_shape": (I32, [I32, I32, I32]),
+    "onpu_geometry2": (None, [I64, I64, I32, I32, I64P]),
+    "onpu_geometry": (None, [I64, I64, I32, I64P]),
+    "onpu_dense_new2": (P, [I64, I64, I32]),
+    "onpu_dense_new": (P, [I64, I64]),
+    "onpu_dense_buf": (U8P, [P]),
+    "onpu_dense_bytes": (I64, [P]),
+    "onpu_dense_sync": (None, [P]),
+    "onpu_dense_mv": (None, [P, F, I64, F]),
+    "onpu_dense_free": (None, [P]),
+    "onpu_bank_new2": (P, [I64, I64, I64, I32, I32]),
+    "onpu_bank_new": (P, [I64, I64, I64, I32]),
+    "onpu_bank_buf": (U8P, [P]),
+    "onpu_bank_expert_bytes": (I64, [P]),
+    "onpu_bank_sync": (None, [P]),
+    "onpu_bank_run": (None, [P, F, I32, I64, I32P, I32, F]),
+    "onpu_bank_free": (None, [P]),
+    "onpu_moe_ffn": (None, [P, P, F, I64, I32P, I32, F, I32, C.c_float, C.c_float, F, F, F]),
+    "onpu_moe_act": (None, [F, I64, I64, I32P, F, I32, C.c_float, C.c_float, F]),
+    "onpu_moe_sum": (None, [F, I64, I32, I64, I32P, F, F, F]),
+    "onpu_ffn_new": (P, [I64, I64, I64, I64, I64, I32]),
+    "onpu_ffn_gu": (P, [P]),
+    "onpu_ffn_dn": (P, [P]),
+    "onpu_ffn_fused": (I32, [P]),
+    "onpu_ffn_perm": (None, [P, I32P]),
+    "onpu_ffn_run": (I32, [P, F, I32P, I32, F, F]),
+    "onpu_ffn_run_many": (I32, [P, F, I64, I32P, I32, F, F]),
+    "onpu_ffn_free": (None, [P]),
+    "onpu_pack": (I64, [F, I64, I64, I32, I32, U8P, I32]),
+    "onpu_quant_dequant": (None, [F, I64, I64, I32, F, I32]),
+    # ---- B200 additions
+    "onpu_last_error": (C.c_char_p, []),
+    "onpu_check_device": (I32, []),
+    "onpu_dense_new_int4": (P, [I64, I64, I32]),
+    "onpu_dense_load_int4": (I32, [P, P, P, I32, P]),
+    "onpu_dense_info": (I32, [P, I64P]),
+    "onpu_dense_prepare": (I32, [P, I64]),
+    "onpu_dense_mv_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
+    "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
+}
+
+_LIB = None
+
+
+class OnpuError(RuntimeError):
+    pass
+
+
+def load():
+    """The library handle with every signature bound; raises if libonpu.so was not built."""
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.exists():
+            raise OnpuError(f"{LIB_PATH} is missing: build it with `python -m opennpu_b200.build`")
+        lib = C.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = lib
+    return _LIB
+
+
+def last_error():
+    e = load().onpu_last_error()
+    return e.decode() if e else None
+
+
+def check(rc, what="libonpu call"):
+    """Raise OnpuError with the library's message when rc < 0 (or rc is a NULL handle)."""
+    if rc is None or (isinstance(rc, int) and rc < 0):
+        raise OnpuError(f"{what}: {last_error() or 'failed'}")
+    return rc
+
+
+def require_device():
+    lib = load()
+    if not lib.onpu_ok():
+        raise OnpuError("libonpu: no usable B200 (onpu_ok() == 0); there is no CPU fallback")
+    return lib
+
+
+def fp(a):
+    return a.ctypes.data_as(F)
+
+
+def i32p(a):
+    return a.ctypes.data_as(I32P)

@@ -13,6 +13,21 @@ os.environ.setdefault("OPENNPU_GEMV_DIR", "/nonexistent-opennpu-gemv")
 os.environ.setdefault("OPENNPU_GEMM8_DIR", "/nonexistent-opennpu-gemm8")
 
 
+def _ensure_built():
+    """Build libonpu.so in-tree if this checkout has none yet (nvcc cross-compiles without a GPU)."""
+    lib = ROOT / "opennpu_b200" / "_lib" / "libonpu.so"
+    if not lib.exists():
+        from opennpu_b200 import build
+        build.build()
+    oracle_lib = ROOT / "oracle" / "_build" / "liboracle.so"
+    if not oracle_lib.exists():
+        import subprocess
+        subprocess.run(["make", "-s", "-C", str(ROOT / "oracle"), "all"], check=True)
+
+
+_ensure_built()
+
+
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (run with -m gpu on the GPU box)")
     config.addinivalue_line("markers", "slow: long CPU test")
