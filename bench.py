@@ -90,6 +90,18 @@ class DecodeStack:
         self.weight_bytes_per_step = sum(int4_param_bytes(N, K) for _, N, K, _ in qwen3_8b_matrices()) * layers
         self.launches_per_step = 3 * layers
 
+    def dominant(self):
+        """The dominant kernel of the step (gate_up GEMV + SwiGLU epilogue) alone, all layers:
+        (callable, algorithmic bytes per launch, launches)."""
+        d = self.dense
+        N, K = 2 * INTER, HIDDEN
+        nbytes = int4_param_bytes(N, K) + self.M * K * 2 + self.M * INTER * 2
+
+        def run():
+            for l, mats in enumerate(self.layers):
+                mats["gate_up"].mv(self.x[l], out=self.a, epi=d.EPI_SWIGLU)
+        return run, nbytes, len(self.layers)
+
     def step(self):
         d = self.dense
         for l, mats in enumerate(self.layers):
@@ -134,6 +146,10 @@ class GemvRotation:
         self.weight_bytes_per_step = copies * int4_param_bytes(N, K)
         self.launches_per_step = copies
 
+    def dominant(self):
+        nbytes = self.bytes_per_step // len(self.mats)
+        return self.step, nbytes, len(self.mats)
+
     def step(self):
         for m in self.mats:
             m.mv(self.x, out=self.y)
@@ -158,6 +174,10 @@ class ClockSampler:
                                          stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 3.0:   # first sample before the timed region
+                time.sleep(0.02)
+            self.lines.clear()
         except OSError:
             self.proc = None
 
@@ -256,7 +276,7 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     hbm, _, peak_kind = peaks()
     M = args.m
-    work = DecodeStack(M, seed=1000 + rank) if args.config == "qwen3-8b" else GemvRotation(M, seed=1000 + rank)
+    work = DecodeStack(M, seed=1000 + rank, layers=args.layers) if args.config == "qwen3-8b" else GemvRotation(M, seed=1000 + rank)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(max(args.warmup, 1)):
@@ -304,6 +324,25 @@ def run_ours(args):
         torch.distributed.barrier()
     ms_step = ms / args.steps
     gbs = work.bytes_per_step * world / (ms_step * 1e-3) / 1e9
+
+    # roofline of the dominant kernel alone: a graph of its launches, CUDA events on its stream
+    run_dom, dom_bytes, dom_n = work.dominant()
+    gdom = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gdom, stream=s):
+        run_dom()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            gdom.replay()
+    reps = max(5, min(200, int(2000 / max(ms_step, 1e-3))))
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(reps):
+            gdom.replay()
+    d1.record(s)
+    d1.synchronize()
+    dom_us = d0.elapsed_time(d1) * 1e3 / (reps * dom_n)
+    del gdom
     per_gpu_gbs = work.bytes_per_step / (ms_step * 1e-3) / 1e9
 
     # end to end through the reference ABI's host-pointer call (rank-local, not graph-replayed)
@@ -324,8 +363,8 @@ def run_ours(args):
             t = torch.tensor([dt], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             dt = float(t.item())
-        h2d = LAYERS * M * (HIDDEN * 4 * 2 + INTER * 4)
-        d2h = LAYERS * M * (QKV_N + 2 * INTER + HIDDEN) * 4
+        h2d = args.layers * M * (HIDDEN * 4 * 2 + INTER * 4)
+        d2h = args.layers * M * (QKV_N + 2 * INTER + HIDDEN) * 4
         e2e = {"value": round(work.bytes_per_step * world / dt / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3),
                "path": "onpu_dense_mv (host fp32 in/out, reference ABI)"}
@@ -341,7 +380,7 @@ def run_ours(args):
     if tp.exists():
         traffic = json.loads(tp.read_text()).get(args.config)
     if rank == 0:
-        achieved = per_gpu_gbs
+        achieved = dom_bytes / (dom_us * 1e-6) / 1e9
         line = {
             "metric": "int4 GEMV achieved HBM GB/s (Qwen3-8B decode projections, 36 layers)"
             if args.config == "qwen3-8b" else "int4 GEMV achieved HBM GB/s (4096x4096, M=1)",
@@ -349,14 +388,17 @@ def run_ours(args):
             "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "int4xbf16->fp32", "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1))",
             "config": {"workload": "qwen3-8b-decode-projections" if args.config == "qwen3-8b" else "gemv-4096x4096",
-                       "M": M, "layers": LAYERS if args.config == "qwen3-8b" else 1,
+                       "M": M, "layers": args.layers if args.config == "qwen3-8b" else 1,
                        "bytes_per_step_per_gpu": work.bytes_per_step,
                        "weight_bytes_per_step_per_gpu": work.weight_bytes_per_step,
                        "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (no flush needed)",
                        "cuda_graph": graph is not None},
             "tokens_per_s": round(M * world / (ms_step * 1e-3), 1) if args.config == "qwen3-8b" else None,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic},
+                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": "gemv_int4 gate_up 24576x4096 + SwiGLU" if args.config == "qwen3-8b"
+                         else "gemv_int4 4096x4096", "algorithmic_bytes_per_launch": dom_bytes,
+                         "us_per_launch": round(dom_us, 3)},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": work.launches_per_step * args.steps,
         }
@@ -394,7 +436,7 @@ def run_reference(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv"])
@@ -402,6 +444,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--layers", type=int, default=LAYERS,
+                    help="decoder layers in the stack (profiling captures use fewer; the metric is quoted at 36)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

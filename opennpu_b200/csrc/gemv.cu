@@ -6,24 +6,30 @@
 // fp32 accumulation; unlike the NPU it neither rounds the dequantised weight nor the K-slice
 // partial sums to bf16, so it is closer to the reference's CPU path (reference.py:24-28, :55-57).
 //
-// Design (HBM-bound; ~0.56 B of weights per MAC pair at M=1):
-//  * Work = the chunk sequence of all jobs ([job][row group][64-K chunk], 2304/2560 B each,
-//    contiguous per job). Every warp is an independent worker owning an equal contiguous range
-//    (split evenly over the grid, which is sized to whole waves of the 148 SMs).
-//  * Each warp streams its range HBM -> its own shared-memory ring with 1-D bulk copies
-//    (cp.async.bulk, mbarrier transaction counts, NS stages of CPS chunks) and consumes it with
-//    128-bit shared loads.
-//  * Codes become exact bf16 values 128+q with one LOP3 per code pair; the dot products run on
-//    the tensor cores (mma.sync m16n8k16, bf16 x bf16 -> fp32), tokens on the MMA's N axis. The
-//    offset is removed without per-code work: the accumulator of each 32-group starts at
-//    c * sum(x) (c = -136 for symmetric codes, -128 for q4nx) from one extra MMA against a
-//    constant A, so D = sum((q - 8) x) (or sum(q x)), then acc += scale * D in fp32 (+ min *
-//    sum(x) for q4nx). Only the 16-bit scale multiplies per group; the weights are never rounded.
-//  * A row group split between warps is finished by the last of its warps to arrive (atomic
-//    counter): partial sums go to a scratch slot per warp, the last arriver adds them in worker
-//    order, so the result is deterministic.
-//  * Programmatic dependent launch: the weight prefetch (which depends on nothing) is issued
-//    before griddepcontrol.wait, so a kernel's stream overlaps the previous kernel's tail.
+// Design (HBM-bound: 0.5625 B per weight, read once):
+//  * Work = the chunk sequence of all jobs ([job][row group][64-K chunk], 2304 or 2560 B each,
+//    contiguous per job). The grid is at most one resident wave of CTAs; CTA i owns an equal
+//    contiguous range of chunks.
+//  * Per CTA, one producer warp and four consumer warps. The producer streams the range
+//    HBM -> shared memory with 1-D bulk copies (cp.async.bulk, mbarrier transaction counts, no
+//    multicast), NS stages of CPS chunks, recycled through "empty" mbarriers.
+//  * Activations: a single-job launch whose tokens fit keeps them resident in shared memory
+//    (loaded once by the consumers after griddepcontrol.wait), so the copy engine only carries
+//    weights; otherwise each stage also carries one 128-B copy per token per chunk.
+//  * Consumer warp s owns strip s (16 rows) of every chunk. Codes become exact bf16 values
+//    (128 + q) with one LOP3 per code pair (the shifts run on the FMA pipe as mul.hi by opaque
+//    powers of two), minus the offset in one bf16x2 op, and the dot products run on the tensor
+//    cores (mma.sync m16n8k16, bf16 x bf16 -> fp32) with tokens on the MMA's N axis; then
+//    acc += scale * D per 32-group in fp32. Weights are never rounded.
+//  * A row group split between CTAs is the tail segment of its first contributor and the head
+//    segment of each later one. Later contributors store their head partial sums and raise a flag
+//    (release store, no waiting); the first contributor, at the end of its range, waits for those
+//    flags (bounded) and adds the partials to its registers in CTA order - deterministic. Waits
+//    only point at higher-numbered CTAs and the grid is one resident wave, so they terminate.
+//  * Programmatic dependent launch: the weight prefetch (constant data) is issued before
+//    griddepcontrol.wait, so a kernel's weight stream overlaps the previous kernel's tail.
+//  * Every wait is bounded (2 s of global time); a timed-out wait sets the error word and the
+//    warp keeps draining the pipeline without computing, so no copy is left in flight at exit.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -36,36 +42,51 @@ namespace onpu_b200 {
 
 namespace {
 
-constexpr int kWarps = 4;                         // warps (workers) per CTA
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: a bulk copy that never lands is a fault
+constexpr int kConsumers = 4;                      // one warp per 16-row strip
+constexpr int kThreads = (kConsumers + 1) * 32;    // + the producer warp
+constexpr int kCPS = 4, kNS = 8;                   // chunks per stage, stages
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // a copy that has not landed in 2 s is a fault
+constexpr int kSlotFloats = 4 * 8 * 2 * 16;        // [strip][r][h][token] head partial sums of a CTA
+constexpr int kXSlot = 192;                        // per-stage activation slot: 128 B + 64 B pad
 
-template <int FMT, int NT, int CPS, int NS>
-struct Cfg {
-    static constexpr int SB = strip_bytes(FMT);
-    static constexpr int CB = chunk_bytes(FMT);
-    static constexpr int STAGE = CPS * CB;
-    static constexpr int RING = NS * STAGE;
-    static constexpr int SMEM = kWarps * RING + kWarps * NS * 8;
-};
+__host__ __device__ constexpr int stage_w_bytes(int fmt) { return kCPS * chunk_bytes(fmt); }
 
-// two 16-bit scale/min values (strip rows r, r+8) -> fp32
+// two 16-bit scale/min values (strip rows r, r+8) -> fp32; mul[3] = 2^16 (an FMA-pipe shift)
 template <int FMT>
-__device__ __forceinline__ void decode_pair(uint32_t w, float &lo, float &hi) {
+__device__ __forceinline__ void decode_pair(uint32_t w, const uint32_t (&mul)[4], float &lo, float &hi) {
     if constexpr (FMT == kFmtQ4F16) {
         const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
         lo = f.x;
         hi = f.y;
     } else {
-        lo = __uint_as_float(w << 16);
+        lo = __uint_as_float(w * mul[3]);
         hi = __uint_as_float(w & 0xffff0000u);
     }
 }
 
-__device__ __forceinline__ void codes_to_a(uint32_t w, uint32_t (&a)[4]) {
+// Codes of one packed word -> the four bf16x2 A registers (128 + q). The right shifts are
+// mul.hi by 2^28 / 2^24 / 2^20 passed in as kernel parameters: they run on the FMA pipe instead
+// of the half-rate integer pipe, which the mask-and-OR (LOP3) already keeps busy.
+__device__ __forceinline__ void codes_to_a(uint32_t w, const uint32_t (&mul)[4], uint32_t (&a)[4]) {
     a[0] = (w & 0x000F000Fu) | 0x43004300u;
-    a[1] = ((w >> 4) & 0x000F000Fu) | 0x43004300u;
-    a[2] = ((w >> 8) & 0x000F000Fu) | 0x43004300u;
-    a[3] = ((w >> 12) & 0x000F000Fu) | 0x43004300u;
+    a[1] = (__umulhi(w, mul[0]) & 0x000F000Fu) | 0x43004300u;
+    a[2] = (__umulhi(w, mul[1]) & 0x000F000Fu) | 0x43004300u;
+    a[3] = (__umulhi(w, mul[2]) & 0x000F000Fu) | 0x43004300u;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                         const float (&c)[4]) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
 }
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
@@ -74,363 +95,516 @@ __device__ __forceinline__ int worker_of(int c, int W, int T) {
     return static_cast<int>((static_cast<int64_t>(c + 1) * W - 1) / T);
 }
 
-template <int NT>
-struct JobRegs {
-    const uint16_t *xp[NT];   // activation row of token (8*nt + r), or null
-    int yr[NT][2];            // output rows of tokens 8*nt + 2t, +1 (-1: none)
-    int m;
-};
-
-template <int NT>
-__device__ __forceinline__ void load_job(const GemvParams &p, int j, int r, int t, JobRegs<NT> &jr) {
-    const GemvJob &job = p.jobs[j];
-    jr.m = job.m;
+// One strip (16 rows) x one chunk (2 groups of 32 along K) into acc. wsb: the strip's bytes in
+// shared memory; xa[nt]: shared address of this lane's 8 activations of the chunk's first group
+// for n-tile nt (the second group is 64 B further; absent tokens read zeros).
+// Without a table (CI false): symmetric codes (128+q) - 136 = q - 8 exactly in bf16,
+// D = sum((q-8) x), acc += s * D; q4nx (128+q) - 128 = q, acc += s * sum(q x) + m * sum(x), with
+// sum(x) from an MMA against ones. With a table (CI true, resident activations): the MMA starts
+// from c * sum(x) read from shared memory at ca (+ gi * 8 * MT; c = -136 symmetric, -128 q4nx),
+// so the 128 + q codes go into the MMA as they are.
+template <int FMT, int NT, bool CI>
+__device__ __forceinline__ void strip_chunk(uint32_t wsb, const uint32_t (&xa)[NT], uint32_t ca, int lane, int r,
+                                            const uint32_t (&mul)[4], float (&acc)[NT][4]) {
+    const uint32_t off = FMT == kFmtQ4NX ? 0x43004300u : 0x43084308u;   // bf16x2 (128) / (136)
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t bx[2][NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        const int n = nt * 8 + r;
-        jr.xp[nt] = n < jr.m ? p.x + static_cast<int64_t>(job.xrow[n]) * p.ldx : nullptr;
-        const int t0 = nt * 8 + 2 * t;
-        jr.yr[nt][0] = t0 < jr.m ? job.yrow[t0] : -1;
-        jr.yr[nt][1] = t0 + 1 < jr.m ? job.yrow[t0 + 1] : -1;
-    }
-}
-
-// Write one row group's finished sums (vals[strip][ntile][frag]) through the epilogue.
-template <int EPI, int NT>
-__device__ __forceinline__ void epilogue(const GemvParams &p, int g, int r, const JobRegs<NT> &jr,
-                                         const float (&vals)[4][NT][4]) {
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
+    for (int gi = 0; gi < 2; ++gi)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            if constexpr (EPI == kEpiSwiGLU) {
-                const int i = g * (kRowGroup / 2) + s * 8 + r;   // strip rows r (gate), r+8 (up)
-                if (i < p.N / 2) {
+            const uint4 v = lds_v4(xa[nt] + gi * 64);
+            bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
+        }
+    const uint4 code = lds_v4(wsb + lane * 16);
+    const uint2 sc = lds_v2(wsb + kCodeBytes + r * 8);
+    uint2 mn = make_uint2(0, 0);
+    if constexpr (FMT == kFmtQ4NX) mn = lds_v2(wsb + kCodeBytes + kScaleBytes + r * 8);
+    constexpr int MT = 8 * NT;
+    float cinit[2][NT][4];
+    if constexpr (CI) {
 #pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int yr = jr.yr[nt][h];
-                        if (yr >= 0) {
-                            const float a = silu_f(vals[s][nt][h]) * vals[s][nt][2 + h];
-                            reinterpret_cast<__nv_bfloat16 *>(p.y)[static_cast<int64_t>(yr) * p.ldy + i] =
-                                __float2bfloat16_rn(a);
-                        }
-                    }
-                }
-            } else {
+        for (int gi = 0; gi < 2; ++gi)
 #pragma unroll
-                for (int f = 0; f < 4; ++f) {
-                    const int row = g * kRowGroup + s * kStripRows + r + 8 * (f >> 1);
-                    const int yr = jr.yr[nt][f & 1];
-                    if (row < p.N && yr >= 0) {
-                        const int col = p.row_map ? p.row_map[row] : row;
-                        const int64_t o = static_cast<int64_t>(yr) * p.ldy + col;
-                        if constexpr (EPI == kEpiF32) reinterpret_cast<float *>(p.y)[o] = vals[s][nt][f];
-                        else reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(vals[s][nt][f]);
-                    }
-                }
+            for (int nt = 0; nt < NT; ++nt) {
+                const uint2 c2 = lds_v2(ca + (gi * MT + nt * 8) * 4);
+                cinit[gi][nt][0] = cinit[gi][nt][2] = __uint_as_float(c2.x);
+                cinit[gi][nt][1] = cinit[gi][nt][3] = __uint_as_float(c2.y);
+            }
+    }
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+        uint32_t a0[4], a1[4];
+        codes_to_a(gi ? code.z : code.x, mul, a0);
+        codes_to_a(gi ? code.w : code.y, mul, a1);
+        if constexpr (!CI) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                a0[i] = bf16x2_sub(a0[i], off);
+                a1[i] = bf16x2_sub(a1[i], off);
+            }
+        }
+        float s_lo, s_hi;
+        decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            float d[4];
+            if constexpr (CI) mma16816(d, a0, bx[gi][nt][0], bx[gi][nt][1], cinit[gi][nt]);
+            else mma16816(d, a0, bx[gi][nt][0], bx[gi][nt][1], zero4);
+            mma16816(d, a1, bx[gi][nt][2], bx[gi][nt][3], d);
+            acc[nt][0] = fmaf(s_lo, d[0], acc[nt][0]);
+            acc[nt][1] = fmaf(s_lo, d[1], acc[nt][1]);
+            acc[nt][2] = fmaf(s_hi, d[2], acc[nt][2]);
+            acc[nt][3] = fmaf(s_hi, d[3], acc[nt][3]);
+            if constexpr (FMT == kFmtQ4NX && CI) {
+                float m_lo, m_hi;
+                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
+                m_lo *= -0.0078125f;                       // cinit = -128 sum(x): m * sum(x)
+                m_hi *= -0.0078125f;
+                acc[nt][0] = fmaf(m_lo, cinit[gi][nt][0], acc[nt][0]);
+                acc[nt][1] = fmaf(m_lo, cinit[gi][nt][1], acc[nt][1]);
+                acc[nt][2] = fmaf(m_hi, cinit[gi][nt][2], acc[nt][2]);
+                acc[nt][3] = fmaf(m_hi, cinit[gi][nt][3], acc[nt][3]);
+            }
+            if constexpr (FMT == kFmtQ4NX && !CI) {
+                float m_lo, m_hi, xs[4];
+                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
+                const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+                mma16816(xs, ones, bx[gi][nt][0], bx[gi][nt][1], zero4);
+                mma16816(xs, ones, bx[gi][nt][2], bx[gi][nt][3], xs);
+                acc[nt][0] = fmaf(m_lo, xs[0], acc[nt][0]);
+                acc[nt][1] = fmaf(m_lo, xs[1], acc[nt][1]);
+                acc[nt][2] = fmaf(m_hi, xs[2], acc[nt][2]);
+                acc[nt][3] = fmaf(m_hi, xs[3], acc[nt][3]);
             }
         }
     }
 }
 
-// partial-sum slot layout: [strip][ntile][token in tile (8)][strip row (16)] floats
-__device__ __forceinline__ int part_index(int s, int nt, int NT, int tok, int row) {
-    return ((s * NT + nt) * 8 + tok) * 16 + row;
+// Store the finished sums of strip rows r (v_lo) and r+8 (v_hi) of one token (output row yr).
+template <int EPI>
+__device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, int r, int yr, float v_lo, float v_hi) {
+    if (yr < 0) return;
+    if constexpr (EPI == kEpiSwiGLU) {
+        const int i = g * (kRowGroup / 2) + s * 8 + r;       // gate row r, up row r+8 of the strip
+        if (i < p.N / 2)
+            reinterpret_cast<__nv_bfloat16 *>(p.y)[static_cast<int64_t>(yr) * p.ldy + i] =
+                __float2bfloat16_rn(silu_f(v_lo) * v_hi);
+    } else {
+        const int row = g * kRowGroup + s * kStripRows + r;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int rr = row + 8 * h;
+            if (rr < p.N) {
+                const int col = p.row_map ? p.row_map[rr] : rr;
+                const int64_t o = static_cast<int64_t>(yr) * p.ldy + col;
+                const float v = h ? v_hi : v_lo;
+                if constexpr (EPI == kEpiF32) reinterpret_cast<float *>(p.y)[o] = v;
+                else reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(v);
+            }
+        }
+    }
 }
 
-template <int FMT, int NT, int EPI, int CPS, int NS>
-__global__ void __launch_bounds__(kWarps * 32) gemv_int4_kernel(const GemvParams p) {
-    using C = Cfg<FMT, NT, CPS, NS>;
+template <int FMT, int NT, int EPI, bool CI>
+__global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams p) {
+    constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT), STAGE_W = stage_w_bytes(FMT);
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r = lane >> 2, t = lane & 3;
-    const int wid = blockIdx.x * kWarps + warp;
-    const int W = p.workers, T = p.total_chunks;
-    const bool active = wid < W;
-    const int lo = active ? static_cast<int>(static_cast<int64_t>(wid) * T / W) : 0;
-    const int hi = active ? static_cast<int>(static_cast<int64_t>(wid + 1) * T / W) : 0;
-    const int nst = (hi - lo + CPS - 1) / CPS;
+    const int W = p.workers, T = p.total_chunks, cta = blockIdx.x;
+    const int lo = static_cast<int>(static_cast<int64_t>(cta) * T / W);
+    const int hi = static_cast<int>(static_cast<int64_t>(cta + 1) * T / W);
+    const int nst = (hi - lo + kCPS - 1) / kCPS;
     const int per_job = p.row_groups * p.chunks;
-    const uint32_t ring = smem_u32(smem + warp * C::RING);
-    const uint32_t bars = smem_u32(smem + kWarps * C::RING) + warp * NS * 8;
+    constexpr bool xres = CI;                         // resident activations carry the offset table
+    const int xchunk = p.xslots * kXSlot, stage_x = kCPS * xchunk;   // per-stage activation layout
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t wring = sbase, xregion = sbase + kNS * STAGE_W;
+    const uint32_t full = sbase + p.off_bar, empty = full + kNS * 8;
 
-    auto issue = [&](int st) {   // lane 0: bulk-copy the chunks of stage st into its ring slot
-        const int c0 = lo + st * CPS, c1 = min(hi, c0 + CPS);
-        const uint32_t bar = bars + (st % NS) * 8;
-        mbar_arrive_expect_tx(bar, static_cast<uint32_t>((c1 - c0) * C::CB));
-        uint32_t dst = ring + (st % NS) * C::STAGE;
-        for (int c = c0; c < c1; ++c) {
-            const int j = c / per_job;
-            const uint8_t *src = p.jobs[j].w + static_cast<int64_t>(c - j * per_job) * C::CB;
-            bulk_g2s(dst, src, C::CB, bar);
-            dst += C::CB;
+    if (!xres)   // the zero slot is never written; a chunk half past K gets a 64-B copy only
+        for (int e = threadIdx.x; e < kNS * stage_x / 16; e += blockDim.x)
+            *reinterpret_cast<uint4 *>(smem + kNS * STAGE_W + e * 16) = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kNS; ++s) {
+            mbar_init(full + s * 8, xres ? 1 : 2);   // weights arrival (+ activations arrival)
+            mbar_init(empty + s * 8, kConsumers);
         }
-    };
-
-    if (active && lane == 0) {
-        for (int s = 0; s < NS; ++s) mbar_init(bars + s * 8, 1);
         mbar_init_fence();
-        // Weights are written before any launch that reads them; when the job list is too
-        // (jobs_ready), the weight prefetch starts before the previous kernel has finished.
-        if (p.jobs_ready)
-            for (int st = 0; st < min(NS, nst); ++st) issue(st);
     }
-    __syncwarp();
-    pdl_launch_dependents();
-    pdl_wait_prerequisites();   // activations / outputs / scratch may belong to the previous kernel
-    if (!active) return;
-    if (!p.jobs_ready && lane == 0)
-        for (int st = 0; st < min(NS, nst); ++st) issue(st);
-    __syncwarp();
+    __syncthreads();
 
-    const uint32_t cA = FMT == kFmtQ4NX ? 0xC300C300u : 0xC308C308u;   // bf16x2 (-128) / (-136)
-    const uint32_t constA[4] = {cA, cA, cA, cA};
+    if (warp == kConsumers) {
+        // ============================================================ producer
+        int wj = lo / per_job;                        // weight cursor: job of the next chunk
+        const uint8_t *wbase = p.jobs_ready ? p.jobs[wj].w : nullptr;
+        auto issue_weights = [&](int st) {            // lane 0 only
+            const int c0 = lo + st * kCPS, c1 = min(hi, c0 + kCPS);
+            const uint32_t bar = full + (st % kNS) * 8;
+            mbar_arrive_expect_tx(bar, static_cast<uint32_t>((c1 - c0) * CB));
+            uint32_t dst = wring + (st % kNS) * STAGE_W;
+            int c = c0;
+            while (c < c1) {                          // one copy per run of chunks within a job
+                if (c >= (wj + 1) * per_job) wbase = p.jobs[++wj].w;
+                const int run_end = min(c1, (wj + 1) * per_job);
+                bulk_g2s(dst, wbase + static_cast<int64_t>(c - wj * per_job) * CB,
+                         static_cast<uint32_t>((run_end - c) * CB), bar);
+                dst += (run_end - c) * CB;
+                c = run_end;
+            }
+        };
+        const int npro = min(kNS, nst);
+        if (lane == 0 && p.jobs_ready)
+            for (int st = 0; st < npro; ++st) issue_weights(st);
+        pdl_launch_dependents();
+        pdl_wait_prerequisites();                     // activations may come from the previous kernel
+        if (lane == 0 && !p.jobs_ready) {
+            wbase = p.jobs[wj].w;
+            for (int st = 0; st < npro; ++st) issue_weights(st);
+        }
+        __syncwarp();
+
+        // activation cursor (per-stage mode): chunk -> (job, k chunk); lane holds xrow[lane & 15]
+        int cj = lo / per_job, ckc = (lo - cj * per_job) % p.chunks;
+        int xm = p.jobs[cj].m, xrow = p.jobs[cj].xrow[lane & 15];
+        bool failed = false;
+        for (int st = 0; st < nst; ++st) {
+            const int slot = st % kNS;
+            if (st >= kNS) {
+                if (!failed && !mbar_wait_bounded(empty + slot * 8, ((st / kNS) - 1) & 1, kWaitLimitNs)) {
+                    failed = true;
+                    if (lane == 0) atomicOr(p.err, 2);
+                }
+                __syncwarp();
+                if (lane == 0) issue_weights(st);
+            }
+            if (xres) continue;
+            // activations of this stage: per chunk one 128-B copy per token (64 B when the chunk's
+            // second group lies past K); the byte total is announced first
+            const int c0 = lo + st * kCPS, c1 = min(hi, c0 + kCPS);
+            uint32_t xbytes = 0;
+            {
+                int jj = cj, kk = ckc, mm = xm;
+                for (int c = c0; c < c1; ++c) {
+                    xbytes += static_cast<uint32_t>(mm * min(128, 2 * (p.K - kk * kChunkK)));
+                    if (++kk == p.chunks) {
+                        kk = 0;
+                        if ((c + 1) % per_job == 0 && c + 1 < hi) mm = p.jobs[++jj].m;
+                    }
+                }
+            }
+            if (lane == 0) mbar_arrive_expect_tx(full + slot * 8, xbytes);
+            __syncwarp();
+            for (int c = c0; c < c1; ++c) {
+                const int k0 = ckc * kChunkK;
+                const uint32_t nb = static_cast<uint32_t>(min(128, 2 * (p.K - k0)));
+                if (lane < xm)
+                    bulk_g2s(xregion + slot * stage_x + (c - c0) * xchunk + lane * kXSlot,
+                             p.x + static_cast<int64_t>(xrow) * p.ldx + k0, nb, full + slot * 8);
+                if (++ckc == p.chunks) {
+                    ckc = 0;
+                    if ((c + 1) % per_job == 0 && c + 1 < hi) {
+                        ++cj;
+                        xm = p.jobs[cj].m;
+                        xrow = p.jobs[cj].xrow[lane & 15];
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    // ================================================================ consumers (strip s = warp)
+    const int s = warp, r = lane >> 2, t = lane & 3;
+    volatile int *flag = reinterpret_cast<volatile int *>(smem + p.off_bar + 2 * kNS * 8);
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();                         // x / outputs / scratch may belong to the previous kernel
 
     int j = lo / per_job;
     int g = (lo - j * per_job) / p.chunks;
     int kc = lo - j * per_job - g * p.chunks;
-    int seg = lo;                                  // first chunk of the open segment
-    JobRegs<NT> jr;
-    load_job<NT>(p, j, r, t, jr);
+    int seg = lo;
+    int m = p.jobs[j].m;
 
-    float acc[4][NT][4];
+    if (xres) {
+        // resident activations: token rows of xstride bytes, then one zero block of 128 B
+        const int n16 = p.K / 8, row16 = p.xstride / 16;   // 16-B pieces: data, row incl. zero pad
+        for (int e = threadIdx.x; e < m * row16; e += kConsumers * 32) {
+            const int n = e / row16, q = e - n * row16;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (q < n16) v = ld_nc_v4(p.x + static_cast<int64_t>(p.jobs[j].xrow[n]) * p.ldx + q * 8);
+            *reinterpret_cast<uint4 *>(smem + kNS * STAGE_W + n * p.xstride + q * 16) = v;
+        }
+        if (threadIdx.x < 8)
+            *reinterpret_cast<uint4 *>(smem + kNS * STAGE_W + m * p.xstride + threadIdx.x * 16) = make_uint4(0, 0, 0, 0);
+        named_bar_sync(1, kConsumers * 32);
+        // offset table [k chunk][group][token slot] = c * sum of the token's 32 activations
+        constexpr int MT = 8 * NT;
+        const float c = FMT == kFmtQ4NX ? -128.0f : -136.0f;
+        float *tab = reinterpret_cast<float *>(smem + kNS * STAGE_W + p.ctab_off);
+        for (int e = threadIdx.x; e < p.chunks * 2 * MT; e += kConsumers * 32) {
+            const int tok = e % MT, grp = e / MT;             // grp = k chunk * 2 + group
+            float sum = 0.f;
+            if (tok < m && grp * 32 < p.K) {
+                const uint8_t *row = smem + kNS * STAGE_W + tok * p.xstride + grp * 64;
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
+                for (int q = 0; q < 4; ++q) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(row + q * 16);
+                    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int f = 0; f < 4; ++f) acc[s][nt][f] = 0.f;
+                    for (int i = 0; i < 4; ++i) sum += __uint_as_float(w4[i] << 16) + __uint_as_float(w4[i] & 0xffff0000u);
+                }
+            }
+            tab[e] = c * sum;
+        }
+        named_bar_sync(1, kConsumers * 32);
+    }
 
-    // Close segment [a, b) of row group (j, g): direct epilogue when this warp holds the whole
-    // row group, else a partial slot; the last of the row group's warps adds them up.
+    int yr[NT][2];
+    uint32_t xrb[NT], xkm[NT];                        // activation base and per-chunk stride of this lane
+    auto load_rows = [&]() {
+        m = p.jobs[j].m;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int tok = nt * 8 + r;
+            if (xres) {
+                xrb[nt] = xregion + (tok < m ? tok * p.xstride : m * p.xstride) + t * 16;
+                xkm[nt] = tok < m ? 128u : 0u;        // absent tokens stay on the zero block
+            } else {
+                xrb[nt] = xregion + (tok < m ? tok : p.xslots - 1) * kXSlot + t * 16;
+                xkm[nt] = 0u;
+            }
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int tk = nt * 8 + 2 * t + h;
+                yr[nt][h] = tk < m ? p.jobs[j].yrow[tk] : -1;
+            }
+        }
+    };
+    load_rows();
+
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int f = 0; f < 4; ++f) acc[nt][f] = 0.f;
+
+    // Close segment [a, b) of row group (j, g) for this strip.
     auto flush = [&](int a, int b) {
         const int gstart = (j * p.row_groups + g) * p.chunks;
-        if (a == gstart && b == gstart + p.chunks) {
-            epilogue<EPI, NT>(p, g, r, jr, acc);
+        if (a == gstart && b == gstart + p.chunks) {          // the whole row group is here
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) store_pair<EPI>(p, g, s, r, yr[nt][h], acc[nt][h], acc[nt][2 + h]);
             return;
         }
-        float *slot = p.part + static_cast<int64_t>(wid * 2 + (a == lo ? 0 : 1)) * (4 * NT * 8 * 16);
-#pragma unroll
-        for (int s = 0; s < 4; ++s)
+        const int cf = worker_of(gstart, W, T), cl = worker_of(gstart + p.chunks - 1, W, T);
+        if (cta != cf) {
+            // head segment of a later contributor: publish the partial sums
+            float *slot = p.part + static_cast<int64_t>(cta) * kSlotFloats;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
                 for (int f = 0; f < 4; ++f) {
-                    const int tok = 2 * t + (f & 1);
-                    if (nt * 8 + tok < jr.m) slot[part_index(s, nt, NT, tok, r + 8 * (f >> 1))] = acc[s][nt][f];
+                    const int tok = nt * 8 + 2 * t + (f & 1);
+                    if (tok < m) slot[((s * 8 + r) * 2 + (f >> 1)) * 16 + tok] = acc[nt][f];
                 }
-        __threadfence();
-        __syncwarp();
-        unsigned old = 0;
-        const int ctr = j * p.row_groups + g;
-        if (lane == 0) old = atomicAdd(p.counters + ctr, 1u);
-        old = __shfl_sync(0xffffffffu, old, 0);
-        const int wf = worker_of(gstart, W, T), wl = worker_of(gstart + p.chunks - 1, W, T);
-        if (old != static_cast<unsigned>(wl - wf)) return;
-        __threadfence();
-        float red[4][NT][4];
+            named_bar_sync(1, kConsumers * 32);
+            if (threadIdx.x == 0) st_release_gpu(p.counters + cta, 1u);
+            return;
+        }
+        // tail segment of the first contributor: collect cf+1 .. cl (bounded wait on their flags)
+        if (warp == 0) {
+            for (int w2 = cf + 1 + lane; w2 <= cl; w2 += 32) {
+                const uint64_t t0 = global_timer_ns();
+                while (ld_acquire_gpu(p.counters + w2) == 0u) {
+                    __nanosleep(256);
+                    if (global_timer_ns() - t0 > kWaitLimitNs) {
+                        atomicOr(p.err, 4);
+                        break;
+                    }
+                }
+                p.counters[w2] = 0u;                          // consumed: ready for the next launch
+            }
+        }
+        named_bar_sync(1, kConsumers * 32);
 #pragma unroll
-        for (int s = 0; s < 4; ++s)
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int f = 0; f < 4; ++f) {
+                const int tok = nt * 8 + 2 * t + (f & 1);
+                if (tok < m) {
+                    float v = acc[nt][f];
+                    const int e = ((s * 8 + r) * 2 + (f >> 1)) * 16 + tok;
+#pragma unroll 4
+                    for (int w2 = cf + 1; w2 <= cl; ++w2) v += __ldcg(p.part + static_cast<int64_t>(w2) * kSlotFloats + e);
+                    acc[nt][f] = v;
+                }
+            }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) store_pair<EPI>(p, g, s, r, yr[nt][h], acc[nt][h], acc[nt][2 + h]);
+    };
+    (void)flag;
+
+    const uint32_t mul[4] = {p.mul[0], p.mul[1], p.mul[2], p.mul[3]};
+    auto advance = [&](int c) {                       // chunk c finished: close its row group?
+        if (++kc == p.chunks) {
+            flush(seg, c + 1);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-                for (int f = 0; f < 4; ++f) red[s][nt][f] = 0.f;
-        for (int w2 = wf; w2 <= wl; ++w2) {
-            const int lo2 = static_cast<int>(static_cast<int64_t>(w2) * T / W);
-            const float *src = p.part + static_cast<int64_t>(w2 * 2 + (lo2 >= gstart ? 0 : 1)) * (4 * NT * 8 * 16);
-#pragma unroll
-            for (int s = 0; s < 4; ++s)
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                    for (int f = 0; f < 4; ++f) {
-                        const int tok = 2 * t + (f & 1);
-                        if (nt * 8 + tok < jr.m)
-                            red[s][nt][f] += __ldcg(src + part_index(s, nt, NT, tok, r + 8 * (f >> 1)));
-                    }
+                for (int f = 0; f < 4; ++f) acc[nt][f] = 0.f;
+            seg = c + 1;
+            kc = 0;
+            if (++g == p.row_groups) {
+                g = 0;
+                ++j;
+                if (c + 1 < hi) load_rows();
+            }
         }
-        epilogue<EPI, NT>(p, g, r, jr, red);
-        if (lane == 0) atomicExch(p.counters + ctr, 0u);
     };
+    // this lane's activation addresses for chunk ci of the current stage (k chunk kcc)
+    auto xaddr = [&](uint32_t (&xa)[NT], uint32_t xstage, int ci, int kcc) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) xa[nt] = xrb[nt] + (xres ? kcc * xkm[nt] : xstage + ci * xchunk);
+    };
+    // offset-table address of this lane's tokens 2t, 2t+1 for k chunk kcc (resident mode)
+    const uint32_t ctab = xregion + p.ctab_off + t * 8;
+    auto caddr = [&](int kcc) { return ctab + kcc * (2 * 8 * NT * 4); };
 
     bool failed = false;
-    int st = 0;
-    for (; st < nst; ++st) {
-        const int slot = st % NS;
-        if (!mbar_wait_bounded(bars + slot * 8, (st / NS) & 1, kWaitLimitNs)) {
+    for (int st = 0; st < nst; ++st) {
+        const int slot = st % kNS;
+        if (!failed && !mbar_wait_bounded(full + slot * 8, (st / kNS) & 1, kWaitLimitNs)) {
             failed = true;
-            break;
+            if (lane == 0) atomicOr(p.err, 1);
         }
-        const int c0 = lo + st * CPS, c1 = min(hi, c0 + CPS);
-        for (int c = c0; c < c1; ++c) {
-            const uint32_t cbase = ring + slot * C::STAGE + (c - c0) * C::CB;
-            // B fragments for both 32-groups of this chunk and the offset-carrying accumulators
-            uint32_t bx[2][NT][4];
-            float ci[2][NT][4];
+        const int c0 = lo + st * kCPS, n = min(hi - c0, kCPS);
+        const uint32_t wsb = wring + slot * STAGE_W + s * SB, xstage = slot * stage_x;
+        if (failed) {
+            // drain only: keep the barriers moving, skip the math and the outputs
+        } else if (n == kCPS && kc + kCPS < p.chunks) {
+            // the common case: a full stage inside one row group
 #pragma unroll
-            for (int gi = 0; gi < 2; ++gi) {
-                const int k0 = kc * kChunkK + gi * 32 + 8 * t;
-#pragma unroll
-                for (int nt = 0; nt < NT; ++nt) {
-                    uint4 v = make_uint4(0, 0, 0, 0);
-                    if (jr.xp[nt] != nullptr && k0 < p.K) v = ld_nc_v4(jr.xp[nt] + k0);
-                    bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
-                    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-                    mma_bf16_m16n8k16(ci[gi][nt], constA, v.x, v.y, zero);
-                    mma_bf16_m16n8k16(ci[gi][nt], constA, v.z, v.w, ci[gi][nt]);
-                }
+            for (int ci = 0; ci < kCPS; ++ci) {
+                uint32_t xa[NT];
+                xaddr(xa, xstage, ci, kc + ci);
+                strip_chunk<FMT, NT, CI>(wsb + ci * CB, xa, caddr(kc + ci), lane, r, mul, acc);
             }
-#pragma unroll
-            for (int s = 0; s < 4; ++s) {
-                const uint32_t sb = cbase + s * C::SB;
-                const uint4 code = lds_v4(sb + lane * 16);
-                const uint2 sc = lds_v2(sb + kCodeBytes + r * 8);
-                uint2 mn = make_uint2(0, 0);
-                if constexpr (FMT == kFmtQ4NX) mn = lds_v2(sb + kCodeBytes + kScaleBytes + r * 8);
-#pragma unroll
-                for (int gi = 0; gi < 2; ++gi) {
-                    uint32_t a0[4], a1[4];
-                    codes_to_a(gi ? code.z : code.x, a0);
-                    codes_to_a(gi ? code.w : code.y, a1);
-                    float s_lo, s_hi;
-                    decode_pair<FMT>(gi ? sc.y : sc.x, s_lo, s_hi);
-                    float m_lo = 0.f, m_hi = 0.f;
-                    if constexpr (FMT == kFmtQ4NX) {
-                        decode_pair<FMT>(gi ? mn.y : mn.x, m_lo, m_hi);
-                        m_lo *= -0.0078125f;   // the accumulator offset is -128 sum(x)
-                        m_hi *= -0.0078125f;
-                    }
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt) {
-                        float d[4];
-                        mma_bf16_m16n8k16(d, a0, bx[gi][nt][0], bx[gi][nt][1], ci[gi][nt]);
-                        mma_bf16_m16n8k16(d, a1, bx[gi][nt][2], bx[gi][nt][3], d);
-                        acc[s][nt][0] = fmaf(s_lo, d[0], acc[s][nt][0]);
-                        acc[s][nt][1] = fmaf(s_lo, d[1], acc[s][nt][1]);
-                        acc[s][nt][2] = fmaf(s_hi, d[2], acc[s][nt][2]);
-                        acc[s][nt][3] = fmaf(s_hi, d[3], acc[s][nt][3]);
-                        if constexpr (FMT == kFmtQ4NX) {
-                            acc[s][nt][0] = fmaf(m_lo, ci[gi][nt][0], acc[s][nt][0]);
-                            acc[s][nt][1] = fmaf(m_lo, ci[gi][nt][1], acc[s][nt][1]);
-                            acc[s][nt][2] = fmaf(m_hi, ci[gi][nt][2], acc[s][nt][2]);
-                            acc[s][nt][3] = fmaf(m_hi, ci[gi][nt][3], acc[s][nt][3]);
-                        }
-                    }
-                }
-            }
-            // advance to the next chunk; a finished row group closes its segment
-            if (++kc == p.chunks) {
-                flush(seg, c + 1);
-#pragma unroll
-                for (int s = 0; s < 4; ++s)
-#pragma unroll
-                    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                        for (int f = 0; f < 4; ++f) acc[s][nt][f] = 0.f;
-                seg = c + 1;
-                kc = 0;
-                if (++g == p.row_groups) {
-                    g = 0;
-                    ++j;
-                    if (c + 1 < hi) load_job<NT>(p, j, r, t, jr);
-                }
+            kc += kCPS;
+        } else {
+            for (int ci = 0; ci < n; ++ci) {
+                uint32_t xa[NT];
+                xaddr(xa, xstage, ci, kc);
+                strip_chunk<FMT, NT, CI>(wsb + ci * CB, xa, caddr(kc), lane, r, mul, acc);
+                advance(c0 + ci);
             }
         }
         __syncwarp();
-        if (lane == 0 && st + NS < nst) {
-            fence_proxy_async_smem();   // this stage's shared reads are done before it is refilled
-            issue(st + NS);
-        }
+        if (lane == 0) mbar_arrive(empty + slot * 8);
     }
-    if (failed) {
-        if (lane == 0) atomicOr(p.err, 1);
-        // copies still in flight must land before the CTA's shared memory is released
-        for (int s2 = st; s2 < min(nst, st + NS); ++s2)
-            (void)mbar_wait_bounded(bars + (s2 % NS) * 8, (s2 / NS) & 1, kWaitLimitNs);
-        return;
-    }
-    if (seg < hi) flush(seg, hi);
+    if (!failed && seg < hi) flush(seg, hi);
 }
 
-template <int FMT, int NT, int EPI>
+template <int FMT, int NT, int EPI, bool CI>
 struct GemvKernel {
-    static constexpr int CPS = 2, NS = 4;
-    using C = Cfg<FMT, NT, CPS, NS>;
-    static int occupancy() {
-        static int occ = -1;
-        if (occ < 0) {
-            auto k = gemv_int4_kernel<FMT, NT, EPI, CPS, NS>;
-            cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
-            int o = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, k, kWarps * 32, C::SMEM) != cudaSuccess) o = 1;
-            occ = o > 0 ? o : 1;
+    static void prepare() {
+        static bool done = false;
+        if (!done) {
+            done = true;
+            cudaFuncSetAttribute(gemv_int4_kernel<FMT, NT, EPI, CI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 227 * 1024);
         }
-        return occ;
     }
-    static cudaError_t launch(const GemvParams &p, cudaStream_t stream, bool pdl) {
-        auto k = gemv_int4_kernel<FMT, NT, EPI, CPS, NS>;
+    static int occupancy(int smem) {
+        prepare();
+        int o = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_int4_kernel<FMT, NT, EPI, CI>, kThreads, smem) !=
+            cudaSuccess)
+            o = 1;
+        return o > 0 ? o : 1;
+    }
+    static cudaError_t launch(const GemvParams &p, int smem, cudaStream_t stream, bool pdl) {
+        prepare();
         cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((p.workers + kWarps - 1) / kWarps);
-        cfg.blockDim = dim3(kWarps * 32);
-        cfg.dynamicSmemBytes = C::SMEM;
+        cfg.gridDim = dim3(p.workers);
+        cfg.blockDim = dim3(kThreads);
+        cfg.dynamicSmemBytes = smem;
         cfg.stream = stream;
         cudaLaunchAttribute attr[1];
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = pdl ? 1 : 0;
-        return cudaLaunchKernelEx(&cfg, k, p);
+        return cudaLaunchKernelEx(&cfg, gemv_int4_kernel<FMT, NT, EPI, CI>, p);
     }
 };
 
-template <int FMT, int NT>
-cudaError_t dispatch_epi(int epi, const GemvParams &p, cudaStream_t s, bool pdl) {
+template <int FMT, int NT, bool CI>
+cudaError_t dispatch_epi_ci(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
     switch (epi) {
-        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32>::launch(p, s, pdl);
-        case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16>::launch(p, s, pdl);
-        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU>::launch(p, s, pdl);
+        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, CI>::launch(p, smem, s, pdl);
+        case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16, CI>::launch(p, smem, s, pdl);
+        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, CI>::launch(p, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
 
+template <int FMT, int NT>
+cudaError_t dispatch_epi(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
+    return p.xres ? dispatch_epi_ci<FMT, NT, true>(epi, p, smem, s, pdl)
+                  : dispatch_epi_ci<FMT, NT, false>(epi, p, smem, s, pdl);
+}
+
 template <int FMT>
-cudaError_t dispatch_nt(int nt, int epi, const GemvParams &p, cudaStream_t s, bool pdl) {
-    return nt == 1 ? dispatch_epi<FMT, 1>(epi, p, s, pdl) : dispatch_epi<FMT, 2>(epi, p, s, pdl);
+cudaError_t dispatch_nt(int nt, int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
+    return nt == 1 ? dispatch_epi<FMT, 1>(epi, p, smem, s, pdl) : dispatch_epi<FMT, 2>(epi, p, smem, s, pdl);
+}
+
+template <int FMT>
+int occ_fmt(int nt, int smem) {
+    return nt == 1 ? GemvKernel<FMT, 1, kEpiF32, true>::occupancy(smem) : GemvKernel<FMT, 2, kEpiF32, true>::occupancy(smem);
 }
 
 }  // namespace
 
-int gemv_ctas_per_sm(int fmt, int ntiles) {
-    // occupancy does not depend on the epilogue (same shared memory); query one instantiation
-    if (fmt == kFmtQ4NX) return ntiles == 1 ? GemvKernel<kFmtQ4NX, 1, kEpiF32>::occupancy() : GemvKernel<kFmtQ4NX, 2, kEpiF32>::occupancy();
-    if (fmt == kFmtQ4S) return ntiles == 1 ? GemvKernel<kFmtQ4S, 1, kEpiF32>::occupancy() : GemvKernel<kFmtQ4S, 2, kEpiF32>::occupancy();
-    return ntiles == 1 ? GemvKernel<kFmtQ4F16, 1, kEpiF32>::occupancy() : GemvKernel<kFmtQ4F16, 2, kEpiF32>::occupancy();
+GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K) {
+    GemvLayout L{};
+    const int64_t xstride = (K * 2 + 127) / 128 * 128 + 64;   // rows 64 B off mod 128: conflict-free
+    const int64_t mt = mmax > 8 ? 16 : 8;
+    const int64_t chunks = (K + kChunkK - 1) / kChunkK;
+    const int64_t res_bytes = mmax * xstride + 128 + chunks * 2 * mt * 4;   // rows, zero block, offset table
+    L.xres = njobs == 1 && res_bytes <= kResidentXBudget;
+    L.xstride = static_cast<int>(xstride);
+    L.ctab_off = static_cast<int>(mmax * xstride + 128);
+    L.xslots = mmax + 1;
+    const int64_t xbytes = L.xres ? res_bytes : static_cast<int64_t>(kNS) * kCPS * L.xslots * kXSlot;
+    L.off_bar = static_cast<int>(kNS * stage_w_bytes(fmt) + (xbytes + 15) / 16 * 16);
+    L.smem = L.off_bar + 2 * kNS * 8 + 16;
+    return L;
 }
 
-int gemv_warps_per_cta() { return kWarps; }
+int gemv_ctas_per_sm(int fmt, int ntiles, int smem) {
+    if (fmt == kFmtQ4NX) return occ_fmt<kFmtQ4NX>(ntiles, smem);
+    if (fmt == kFmtQ4S) return occ_fmt<kFmtQ4S>(ntiles, smem);
+    return occ_fmt<kFmtQ4F16>(ntiles, smem);
+}
 
-int64_t gemv_part_floats_per_worker(int ntiles) { return 2LL * 4 * ntiles * 8 * 16; }
+int gemv_chunks_per_stage() { return kCPS; }
 
-cudaError_t gemv_launch(int fmt, int ntiles, int epi, const GemvParams &p, cudaStream_t stream, bool pdl) {
-    // every instantiation must have had its shared-memory limit raised before its first launch
-    (void)gemv_ctas_per_sm(fmt, ntiles);
-    auto raise = [](auto kern, int smem) { cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); };
-    static bool raised[3][2][3] = {};
-    if (!raised[fmt][ntiles - 1][epi]) {
-        raised[fmt][ntiles - 1][epi] = true;
-#define ONPU_RAISE(F, N, E) if (fmt == F && ntiles == N && epi == E) raise(gemv_int4_kernel<F, N, E, 2, 4>, Cfg<F, N, 2, 4>::SMEM)
-        ONPU_RAISE(kFmtQ4NX, 1, kEpiF32); ONPU_RAISE(kFmtQ4NX, 1, kEpiBF16); ONPU_RAISE(kFmtQ4NX, 1, kEpiSwiGLU);
-        ONPU_RAISE(kFmtQ4NX, 2, kEpiF32); ONPU_RAISE(kFmtQ4NX, 2, kEpiBF16); ONPU_RAISE(kFmtQ4NX, 2, kEpiSwiGLU);
-        ONPU_RAISE(kFmtQ4S, 1, kEpiF32); ONPU_RAISE(kFmtQ4S, 1, kEpiBF16); ONPU_RAISE(kFmtQ4S, 1, kEpiSwiGLU);
-        ONPU_RAISE(kFmtQ4S, 2, kEpiF32); ONPU_RAISE(kFmtQ4S, 2, kEpiBF16); ONPU_RAISE(kFmtQ4S, 2, kEpiSwiGLU);
-        ONPU_RAISE(kFmtQ4F16, 1, kEpiF32); ONPU_RAISE(kFmtQ4F16, 1, kEpiBF16); ONPU_RAISE(kFmtQ4F16, 1, kEpiSwiGLU);
-        ONPU_RAISE(kFmtQ4F16, 2, kEpiF32); ONPU_RAISE(kFmtQ4F16, 2, kEpiBF16); ONPU_RAISE(kFmtQ4F16, 2, kEpiSwiGLU);
-#undef ONPU_RAISE
-    }
+int64_t gemv_part_floats_per_worker(int ntiles) {
+    (void)ntiles;
+    return kSlotFloats;
+}
+
+cudaError_t gemv_launch(int fmt, int ntiles, int epi, const GemvParams &p, int smem, cudaStream_t stream, bool pdl) {
     switch (fmt) {
-        case kFmtQ4NX: return dispatch_nt<kFmtQ4NX>(ntiles, epi, p, stream, pdl);
-        case kFmtQ4S: return dispatch_nt<kFmtQ4S>(ntiles, epi, p, stream, pdl);
-        case kFmtQ4F16: return dispatch_nt<kFmtQ4F16>(ntiles, epi, p, stream, pdl);
+        case kFmtQ4NX: return dispatch_nt<kFmtQ4NX>(ntiles, epi, p, smem, stream, pdl);
+        case kFmtQ4S: return dispatch_nt<kFmtQ4S>(ntiles, epi, p, smem, stream, pdl);
+        case kFmtQ4F16: return dispatch_nt<kFmtQ4F16>(ntiles, epi, p, smem, stream, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -85,16 +85,22 @@ struct GemvParams {
     int N, K;                          // every job's matrix shape (logical)
     int row_groups, chunks;            // of one job
     int total_chunks;                  // njobs * row_groups * chunks
-    int workers;                       // warps sharing the chunk sequence
+    int workers;                       // CTAs sharing the chunk sequence (at most one resident wave)
     const uint16_t *x;                 // bf16 activations, row stride ldx (elements)
     int64_t ldx;
     void *y;                           // output rows, stride ldy (elements of the output type)
     int64_t ldy;
     const int *row_map;                // optional: GPU row -> output column (fp32/bf16 epilogues)
-    float *part;                       // split-row partial sums: [2 * workers][4][NT][32][4]
-    unsigned *counters;                // [njobs * row_groups], zero between launches
+    float *part;                       // split row groups: head partial sums, [workers][4][8][2][16]
+    unsigned *counters;                // [workers] partial-ready flags, zero between launches
     int *err;                          // set non-zero on a timed-out wait
     int jobs_ready;                    // job list not written by the previous kernel in the stream
+    uint32_t mul[4];                   // 2^28, 2^24, 2^20, 2^16: shift multipliers the compiler cannot fold
+    int xslots;                        // per-stage activations: slots per chunk (max tokens + 1 zero slot)
+    int xres;                          // activations resident in shared memory (single job)
+    int xstride;                       // resident: bytes per token row
+    int ctab_off;                      // resident: offset table position in the activation region
+    int off_bar;                       // shared-memory offset of the mbarriers
 };
 
 }  // namespace onpu_b200

@@ -9,10 +9,23 @@
 namespace onpu_b200 {
 
 // ---- GEMV (gemv.cu)
-int gemv_ctas_per_sm(int fmt, int ntiles);
-int gemv_warps_per_cta();
+// Activations of a single-job launch stay resident in shared memory when they take at most this
+// many bytes (tokens x padded K x 2 B); otherwise every stage carries its own slice.
+constexpr int64_t kResidentXBudget = 40 * 1024;
+
+struct GemvLayout {
+    int xres;          // activations resident
+    int xstride;       // resident: bytes per token row (padded)
+    int ctab_off;      // resident: offset of the per-group offset table in the activation region
+    int xslots;        // per-stage: token slots per chunk (max tokens + 1 zero slot)
+    int off_bar;       // byte offset of the mbarriers in shared memory
+    int smem;          // dynamic shared memory per CTA
+};
+GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K);
+int gemv_ctas_per_sm(int fmt, int ntiles, int smem);
+int gemv_chunks_per_stage();
 int64_t gemv_part_floats_per_worker(int ntiles);
-cudaError_t gemv_launch(int fmt, int ntiles, int epi, const GemvParams &p, cudaStream_t stream, bool pdl);
+cudaError_t gemv_launch(int fmt, int ntiles, int epi, const GemvParams &p, int smem, cudaStream_t stream, bool pdl);
 
 // ---- layout conversion (repack.cu)
 // Where the codes of the matrix come from.

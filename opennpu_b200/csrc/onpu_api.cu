@@ -191,11 +191,11 @@ bool set_gateup_interleave(GpuMat &m) {
 }
 
 // ------------------------------------------------------------------ GEMV driver
-int choose_workers(const Ctx &c, int fmt, int ntiles, int T) {
-    const int occ = gemv_ctas_per_sm(fmt, ntiles), per_wave = c.nsm * gemv_warps_per_cta();
-    if (T <= per_wave) return std::max(1, T);
-    const int k = std::min(occ, std::max(1, T / (per_wave * 2)));   // >= 2 chunks per warp, whole waves
-    return per_wave * k;
+int choose_workers(const Ctx &c, int fmt, int ntiles, int T, int smem) {
+    // at most one resident wave (every SM the same number of CTAs), each with >= 1 full stage
+    const int full = c.nsm * gemv_ctas_per_sm(fmt, ntiles, smem), cps = gemv_chunks_per_stage();
+    if (T >= full * cps) return full;
+    return std::max(1, std::min(full, (T + cps - 1) / cps));
 }
 
 bool ensure_scratch(Ctx &c, int workers, int ntiles, int counters) {
@@ -205,12 +205,14 @@ bool ensure_scratch(Ctx &c, int workers, int ntiles, int counters) {
     return true;
 }
 
-int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntiles, int epi, const uint16_t *x,
-             int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl) {
+// mmax: the largest token count of any job (the kernel sizes its activation slots by it)
+int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntiles, int mmax, int epi,
+             const uint16_t *x, int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl) {
     const int T = njobs * m.gm.row_groups * m.gm.chunks;
     if (T == 0) return 0;
-    const int W = choose_workers(c, m.gm.fmt, ntiles, T);
-    if (!ensure_scratch(c, W, ntiles, njobs * m.gm.row_groups)) return -1;
+    const GemvLayout lay = gemv_layout(m.gm.fmt, njobs, mmax, m.gm.K);
+    const int W = choose_workers(c, m.gm.fmt, ntiles, T, lay.smem);
+    if (!ensure_scratch(c, W, ntiles, W)) return -1;
     GemvParams p{};
     p.jobs = d_jobs;
     p.njobs = njobs;
@@ -229,7 +231,16 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     p.counters = c.d_cnt;
     p.err = c.d_err;
     p.jobs_ready = 1;
-    ONPU_CUDA(gemv_launch(m.gm.fmt, ntiles, epi, p, s, pdl), -1);
+    p.mul[0] = 1u << 28;
+    p.mul[1] = 1u << 24;
+    p.mul[2] = 1u << 20;
+    p.mul[3] = 1u << 16;
+    p.xslots = lay.xslots;
+    p.xres = lay.xres;
+    p.xstride = lay.xstride;
+    p.ctab_off = lay.ctab_off;
+    p.off_bar = lay.off_bar;
+    ONPU_CUDA(gemv_launch(m.gm.fmt, ntiles, epi, p, lay.smem, s, pdl), -1);
     ++c.calls;
     return 0;
 }
@@ -271,9 +282,10 @@ bool finish(Ctx &c) {
 
 // (token, slot) pairs grouped by expert (ascending id, then arrival order), <= 16 per job
 void build_expert_jobs(const GpuMat &m, const int32_t *ids, int64_t T, int k, bool x_per_slot, bool x_by_slot,
-                       std::vector<GemvJob> &jobs, int &ntiles) {
+                       std::vector<GemvJob> &jobs, int &ntiles, int &mmax) {
     jobs.clear();
     ntiles = 1;
+    mmax = 1;
     std::vector<int64_t> count(static_cast<size_t>(m.E) + 1, 0);
     for (int64_t i = 0; i < T * k; ++i) ++count[ids[i] + 1];
     for (int64_t e = 0; e < m.E; ++e) count[e + 1] += count[e];
@@ -291,6 +303,7 @@ void build_expert_jobs(const GpuMat &m, const int32_t *ids, int64_t T, int k, bo
                 jb.yrow[n] = static_cast<int>(slot);
             }
             if (jb.m > 8) ntiles = 2;
+            mmax = std::max(mmax, jb.m);
             jobs.push_back(jb);
         }
     }
@@ -305,7 +318,7 @@ bool upload_jobs(Ctx &c, const std::vector<GemvJob> &jobs) {
 // ------------------------------------------------------------------ handles
 struct JobSet {
     GemvJob *d = nullptr;
-    int n = 0, ntiles = 1;
+    int n = 0, ntiles = 1, mmax = 1;
 };
 
 struct DenseH {
@@ -353,6 +366,7 @@ JobSet *dense_jobs(DenseH *d, int64_t rows) {
         jb.m = static_cast<int>(std::min<int64_t>(kMaxTokensPerJob, rows - static_cast<int64_t>(j) * kMaxTokensPerJob));
         for (int n = 0; n < jb.m; ++n) jb.xrow[n] = jb.yrow[n] = j * kMaxTokensPerJob + n;
         if (jb.m > 8) js.ntiles = 2;
+        js.mmax = std::max(js.mmax, jb.m);
     }
     if (cudaMalloc(&js.d, sizeof(GemvJob) * js.n) != cudaSuccess ||
         cudaMemcpy(js.d, h.data(), sizeof(GemvJob) * js.n, cudaMemcpyHostToDevice) != cudaSuccess) {
@@ -457,9 +471,9 @@ bool moe_ffn_impl(BankH *gu, BankH *dn, const float *x, int64_t T, const int32_t
     }
     if (!stage_x(c, x, T, Kg, Kgp)) return false;
     std::vector<GemvJob> jg, jd;
-    int ntg = 1, ntd = 1;
-    build_expert_jobs(gu->mat, ids, T, k, false, false, jg, ntg);
-    build_expert_jobs(dn->mat, ids, T, k, false, true, jd, ntd);
+    int ntg = 1, ntd = 1, mg = 1, md = 1;
+    build_expert_jobs(gu->mat, ids, T, k, false, false, jg, ntg, mg);
+    build_expert_jobs(dn->mat, ids, T, k, false, true, jd, ntd, md);
     std::vector<GemvJob> all(jg);
     all.insert(all.end(), jd.begin(), jd.end());
     if (!upload_jobs(c, all)) return false;
@@ -481,17 +495,17 @@ bool moe_ffn_impl(BankH *gu, BankH *dn, const float *x, int64_t T, const int32_t
         d_db = c.d_db;
     }
     if (fused && act == 0 && !gu_bias) {
-        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, kEpiSwiGLU, c.d_x, Kgp, c.d_a, Kdp,
+        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, mg, kEpiSwiGLU, c.d_x, Kgp, c.d_a, Kdp,
                      c.stream, false))
             return false;
     } else {
         if (!grow(c.d_h, c.h_cap, TK * Ng)) return false;
-        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, kEpiF32, c.d_x, Kgp, c.d_h, Ng, c.stream,
+        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, mg, kEpiF32, c.d_x, Kgp, c.d_h, Ng, c.stream,
                      false))
             return false;
         ONPU_CUDA(moe_act_launch(c.d_h, Ng, TK, Ng, c.d_ids, d_gb, act, alpha, limit, c.d_a, Kdp, c.stream), false);
     }
-    if (run_gemv(c, dn->mat, c.d_jobs + jg.size(), static_cast<int>(jd.size()), ntd, kEpiF32, c.d_a, Kdp, c.d_o, Nd,
+    if (run_gemv(c, dn->mat, c.d_jobs + jg.size(), static_cast<int>(jd.size()), ntd, md, kEpiF32, c.d_a, Kdp, c.d_o, Nd,
                  c.stream, false))
         return false;
     ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, c.d_ids, c.d_w, d_db, c.d_y, Nd, c.stream), false);
@@ -587,7 +601,7 @@ void onpu_dense_mv(void *h, const float *x, int64_t rows, float *y) {
     const int64_t Kin = d->geo.ok ? d->geo.K : K;
     JobSet *js = dense_jobs(d, rows);
     if (!js || !stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
-    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
+    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * rows * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
 }
@@ -631,10 +645,10 @@ void onpu_bank_run(void *h, const float *x, int x_per_slot, int64_t T, const int
     const int64_t xrows = x_per_slot ? T * k : T;
     if (!stage_x(c, x, xrows, b->geo.K, Kp)) return;
     std::vector<GemvJob> jobs;
-    int nt = 1;
-    build_expert_jobs(b->mat, ids, T, k, x_per_slot != 0, false, jobs, nt);
+    int nt = 1, mm = 1;
+    build_expert_jobs(b->mat, ids, T, k, x_per_slot != 0, false, jobs, nt, mm);
     if (!upload_jobs(c, jobs) || !grow(c.d_y, c.y_cap, T * k * N)) return;
-    if (run_gemv(c, b->mat, c.d_jobs, static_cast<int>(jobs.size()), nt, kEpiF32, c.d_x, Kp, c.d_y, N, c.stream, false))
+    if (run_gemv(c, b->mat, c.d_jobs, static_cast<int>(jobs.size()), nt, mm, kEpiF32, c.d_x, Kp, c.d_y, N, c.stream, false))
         return;
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * T * k * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
@@ -848,8 +862,9 @@ int onpu_dense_prepare(void *h, int64_t rows) {
     JobSet *js = dense_jobs(d, rows);
     if (!js) return -1;
     const int T = js->n * d->mat.gm.row_groups * d->mat.gm.chunks;
-    const int W = choose_workers(c, d->mat.gm.fmt, js->ntiles, T);
-    return ensure_scratch(c, W, js->ntiles, js->n * d->mat.gm.row_groups) ? 0 : -1;
+    const GemvLayout lay = gemv_layout(d->mat.gm.fmt, js->n, js->mmax, d->mat.gm.K);
+    const int W = choose_workers(c, d->mat.gm.fmt, js->ntiles, T, lay.smem);
+    return ensure_scratch(c, W, js->ntiles, W) ? 0 : -1;
 }
 
 int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream) {
@@ -876,7 +891,7 @@ int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
     std::lock_guard<std::mutex> lk(g_mu);
     JobSet *js = dense_jobs(d, rows);
     if (!js) return -1;
-    return run_gemv(c, d->mat, js->d, js->n, js->ntiles, epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
+    return run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
                     static_cast<cudaStream_t>(stream), pdl_enabled());
 }
 

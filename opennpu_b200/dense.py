@@ -22,6 +22,7 @@ def _stream_ptr(stream=None):
 class DenseMatrix:
     def __init__(self, handle, N, K, fmt, gateup=False):
         self.h, self.N, self.K, self.fmt, self.gateup = handle, N, K, fmt, gateup
+        self.Kg = self.info()[2]          # K of the GPU layout (K rounded up to 32)
 
     # ---------------------------------------------------------------- construction
     @classmethod
@@ -65,9 +66,12 @@ class DenseMatrix:
         return cls(h, N, K, FMT_Q4S if sym else FMT_Q4NX)
 
     def __del__(self):
-        if getattr(self, "h", None):
-            L.load().onpu_dense_free(self.h)
-            self.h = None
+        try:
+            if getattr(self, "h", None):
+                L.load().onpu_dense_free(self.h)
+                self.h = None
+        except Exception:   # interpreter shutdown: the library may already be unloaded
+            pass
 
     # ---------------------------------------------------------------- use
     def info(self):
@@ -96,11 +100,11 @@ class DenseMatrix:
         return out
 
     def unpack(self):
-        """GPU layout -> (codes uint8 [N, K], scale bits int16 [N, K/32], min bits or None), in GPU
-        row order (a gate/up matrix is interleaved per 16 rows)."""
+        """GPU layout -> (codes uint8 [N, Kg], scale bits int16 [N, Kg/32], min bits or None), in GPU
+        row order (a gate/up matrix is interleaved per 16 rows); Kg = K rounded up to 32."""
         dev = torch.device("cuda")
-        q = torch.zeros(self.N, self.K, dtype=torch.uint8, device=dev)
-        s = torch.zeros(self.N, self.K // 32, dtype=torch.int16, device=dev)
+        q = torch.zeros(self.N, self.Kg, dtype=torch.uint8, device=dev)
+        s = torch.zeros(self.N, self.Kg // 32, dtype=torch.int16, device=dev)
         m = torch.zeros_like(s) if self.fmt == FMT_Q4NX else None
         rc = L.load().onpu_dense_unpack_dev(self.h, q.data_ptr(), s.data_ptr(), 0 if m is None else m.data_ptr(),
                                             _stream_ptr())

@@ -166,9 +166,12 @@ class NPULinearGroup:
         self._key, self._y = None, None
 
     def __del__(self):
-        if getattr(self, "ch", None):
-            L.load().onpu_dense_free(self.ch)
-            self.ch = None
+        try:
+            if getattr(self, "ch", None):
+                L.load().onpu_dense_free(self.ch)
+                self.ch = None
+        except Exception:
+            pass
 
     def compute(self, x, i):
         if self._key is None or self._key[0] is not x or self._key[1] != x._version:
@@ -274,10 +277,13 @@ class NPUExperts(nn.Module):
         return torch.from_numpy(y).to(hidden_states.dtype)
 
     def __del__(self):
-        lib = L.load()
-        if getattr(self, "cffn", None):
-            lib.onpu_ffn_free(self.cffn)
-        else:
-            for h in (getattr(self, "cgu", None), getattr(self, "cdn", None)):
-                if h:
-                    lib.onpu_bank_free(h)
+        try:
+            lib = L.load()
+            if getattr(self, "cffn", None):
+                lib.onpu_ffn_free(self.cffn)
+            else:
+                for h in (getattr(self, "cgu", None), getattr(self, "cdn", None)):
+                    if h:
+                        lib.onpu_bank_free(h)
+        except Exception:
+            pass
