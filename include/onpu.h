@@ -133,6 +133,15 @@ int onpu_dense_info(void *h, int64_t *out4);
 int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream);
 /* Prepare (allocate descriptors and scratch for) `rows`-row calls without running one. */
 int onpu_dense_prepare(void *h, int64_t rows);
+/* onpu_dense_mv_dev with no allocation in the call: no reference counterpart (the NPU library
+ * has no device scratch). Same arguments and result as onpu_dense_mv_dev, but the split-row
+ * scratch and descriptors live in one static device array shared by every call on a device, for
+ * callers that cannot let the library allocate (all free HBM handed to their own pool, or a fixed
+ * device footprint). rows <= 256 per call, else -1 with an error message. The first call on a
+ * device looks up the array (cudaGetSymbolAddress) and clears it; make that first call before any
+ * stream capture. Overlapping calls race: order them on one stream. */
+int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi,
+                              void *stream);
 /* GPU layout -> plain codes q[N][K] (0..15), scales[N][K/32] (and mins for q4nx), device pointers;
  * for bit-exact verification. */
 int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream);

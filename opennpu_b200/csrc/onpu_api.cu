@@ -905,3 +905,172 @@ int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins,
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ no-allocation entry point
+// onpu_dense_mv_dev_noalloc: onpu_dense_mv_dev whose split-row scratch (partial-sum slots, ready
+// flags) and GEMV descriptors live in one file-scope __device__ array instead of buffers that the
+// library grows with cudaMalloc on first use. For callers that cannot let a library allocate in
+// their decode loop: engines that hand all free HBM to their own pool at start-up (a serving
+// engine's KV-cache reservation leaves nothing for a lazy cudaMalloc, which then fails mid-run),
+// and callers with a fixed, pre-planned device footprint. The regular path's first call for a new
+// row count allocates descriptors, and its scratch growth synchronises the whole device first
+// (grow() above), a stall such callers cannot take inside a step either.
+//
+// Limits: rows <= kStaticMaxRows (descriptors for kStaticMaxRows / 16 jobs), at most
+// kStaticWorkers CTAs (the launch uses min(chosen, kStaticWorkers)). The array is
+// kStaticWorkers * 4 KB + 4 KB of flags + descriptors (~4.1 MB), device memory the driver
+// reserves when this translation unit's device image is loaded.
+//
+// Every call on a device shares the one array: calls must be ordered on one stream (overlapping
+// calls race on the flags, slots and descriptors). Each call clears the flags it uses on its
+// stream before the launch, so a call never reads state left by an earlier one.
+namespace {
+
+constexpr int kStaticWorkers = 1024;
+constexpr int kStaticSlotFloats = 1024;                       // gemv_part_floats_per_worker
+constexpr int kStaticMaxRows = 256;
+constexpr int kStaticMaxJobs = kStaticMaxRows / kMaxTokensPerJob;
+constexpr size_t kStaticPartBytes = size_t(kStaticWorkers) * kStaticSlotFloats * sizeof(float);
+constexpr size_t kStaticFlagBytes = size_t(kStaticWorkers) * sizeof(unsigned);
+constexpr size_t kStaticJobBytes = size_t(kStaticMaxJobs) * sizeof(GemvJob);
+constexpr size_t kStaticBytes = kStaticPartBytes + kStaticFlagBytes + kStaticJobBytes;
+static_assert(kStaticPartBytes % 256 == 0 && kStaticFlagBytes % 256 == 0, "scratch sections stay aligned");
+
+__device__ __align__(256) unsigned char g_static_scratch[kStaticBytes];
+
+constexpr int kMaxDevices = 64;
+unsigned char *g_static_ptr[kMaxDevices] = {};
+
+// once per device, with that device current; the first call on a device does it, so on each
+// device that first call should come before any stream capture. Caller holds g_mu.
+unsigned char *static_scratch(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) {
+        set_err("onpu_dense_mv_dev_noalloc: device ordinal %d out of range", dev);
+        return nullptr;
+    }
+    if (g_static_ptr[dev]) return g_static_ptr[dev];
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess || ptr == nullptr) {
+        set_err("onpu_dense_mv_dev_noalloc: cudaGetSymbolAddress of the static scratch failed: %s",
+                cudaGetErrorString(e));
+        return nullptr;
+    }
+    e = cudaMemset(static_cast<unsigned char *>(ptr) + kStaticPartBytes, 0, kStaticFlagBytes);
+    if (e == cudaSuccess) e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) {
+        set_err("onpu_dense_mv_dev_noalloc: clearing the static scratch failed: %s", cudaGetErrorString(e));
+        return nullptr;
+    }
+    g_static_ptr[dev] = static_cast<unsigned char *>(ptr);
+    return g_static_ptr[dev];
+}
+
+}  // namespace
+
+extern "C" {
+
+int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi,
+                              void *stream) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    if (!d) {
+        set_err("onpu_dense_mv_dev_noalloc: null matrix handle");
+        return -1;
+    }
+    if (rows <= 0) return 0;
+    if (rows > kStaticMaxRows) {
+        set_err("onpu_dense_mv_dev_noalloc: %lld rows exceed the static scratch limit of %d rows per call",
+                static_cast<long long>(rows), kStaticMaxRows);
+        return -1;
+    }
+    if (epi < kEpiF32 || epi > kEpiSwiGLU || (epi == kEpiSwiGLU && !d->gateup)) {
+        set_err("onpu_dense_mv_dev_noalloc: bad epilogue %d for this matrix", epi);
+        return -1;
+    }
+    if (d->geo.ok && d->geo.K != d->mat.gm.K) {
+        set_err("onpu_dense_mv_dev_noalloc: K must be a multiple of 32");
+        return -1;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < d->mat.gm.K) {
+        set_err("onpu_dense_mv_dev_noalloc: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+        return -1;
+    }
+    if (ldy < (epi == kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
+        set_err("onpu_dense_mv_dev_noalloc: y row stride %lld is shorter than the output row",
+                static_cast<long long>(ldy));
+        return -1;
+    }
+    if (gemv_part_floats_per_worker(2) > kStaticSlotFloats) {
+        set_err("onpu_dense_mv_dev_noalloc: GEMV slot size exceeds the static scratch layout");
+        return -1;
+    }
+    // the handle exists, so the library context (device, stream, status word) is already set up
+    Ctx &c = ctx();
+    int dev = -1;
+    ONPU_CUDA(cudaGetDevice(&dev), -1);
+    if (dev != c.device) {
+        set_err("onpu_dense_mv_dev_noalloc: current device %d is not the library's device %d", dev, c.device);
+        return -1;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    unsigned char *base = static_scratch(dev);
+    if (!base) return -1;
+    float *part = reinterpret_cast<float *>(base);
+    unsigned *flags = reinterpret_cast<unsigned *>(base + kStaticPartBytes);
+    GemvJob *d_jobs = reinterpret_cast<GemvJob *>(base + kStaticPartBytes + kStaticFlagBytes);
+
+    // descriptors built on the host stack, copied into the array on the caller's stream
+    GemvJob jobs[kStaticMaxJobs];
+    const int njobs = static_cast<int>((rows + kMaxTokensPerJob - 1) / kMaxTokensPerJob);
+    int ntiles = 1, mmax = 0;
+    for (int j = 0; j < njobs; ++j) {
+        GemvJob &jb = jobs[j];
+        std::memset(&jb, 0, sizeof jb);
+        jb.w = d->mat.d_w;
+        jb.m = static_cast<int>(std::min<int64_t>(kMaxTokensPerJob, rows - static_cast<int64_t>(j) * kMaxTokensPerJob));
+        for (int n = 0; n < jb.m; ++n) jb.xrow[n] = jb.yrow[n] = j * kMaxTokensPerJob + n;
+        if (jb.m > 8) ntiles = 2;
+        mmax = std::max(mmax, jb.m);
+    }
+    const int T = njobs * d->mat.gm.row_groups * d->mat.gm.chunks;
+    if (T == 0) return 0;
+    const GemvLayout lay = gemv_layout(d->mat.gm.fmt, njobs, mmax, d->mat.gm.K);
+    const int W = std::min(kStaticWorkers, choose_workers(c, d->mat.gm.fmt, ntiles, T, lay.smem));
+    auto s = static_cast<cudaStream_t>(stream);
+    ONPU_CUDA(cudaMemcpyAsync(d_jobs, jobs, sizeof(GemvJob) * njobs, cudaMemcpyHostToDevice, s), -1);
+    ONPU_CUDA(cudaMemsetAsync(flags, 0, sizeof(unsigned) * W, s), -1);
+
+    GemvParams p{};
+    p.jobs = d_jobs;
+    p.njobs = njobs;
+    p.N = static_cast<int>(d->mat.gm.N);
+    p.K = static_cast<int>(d->mat.gm.K);
+    p.row_groups = d->mat.gm.row_groups;
+    p.chunks = d->mat.gm.chunks;
+    p.total_chunks = T;
+    p.workers = W;
+    p.x = static_cast<const uint16_t *>(x);
+    p.ldx = ldx;
+    p.y = y;
+    p.ldy = ldy;
+    p.row_map = epi == kEpiSwiGLU ? nullptr : d->mat.d_row_map;
+    p.part = part;
+    p.counters = flags;
+    p.err = c.d_err;
+    p.jobs_ready = 1;
+    p.mul[0] = 1u << 28;
+    p.mul[1] = 1u << 24;
+    p.mul[2] = 1u << 20;
+    p.mul[3] = 1u << 16;
+    p.xslots = lay.xslots;
+    p.xres = lay.xres;
+    p.xstride = lay.xstride;
+    p.ctab_off = lay.ctab_off;
+    p.off_bar = lay.off_bar;
+    ONPU_CUDA(gemv_launch(d->mat.gm.fmt, ntiles, epi, p, lay.smem, s, false), -1);
+    ++c.calls;
+    return 0;
+}
+
+}  // extern "C"

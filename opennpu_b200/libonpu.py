@@ -58,6 +58,7 @@ SIGNATURES = {
     "onpu_dense_info": (I32, [P, I64P]),
     "onpu_dense_prepare": (I32, [P, I64]),
     "onpu_dense_mv_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
+    "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
 }
 
