@@ -61,12 +61,14 @@ def gen_int4_cuda(N, K, gen):
 
 
 class DecodeStack:
-    """The Qwen3-8B projection stack on one GPU (libonpu dense matrices)."""
+    """The Qwen3-8B projection stack on one GPU (libonpu dense matrices). mode "chain": the whole
+    step is one GEMV chain (onpu_chain_*), every link ordered after its predecessor as in a real
+    decode step; mode "launches": one onpu_dense_mv_dev launch per matrix."""
 
-    def __init__(self, M, seed, layers=LAYERS):
+    def __init__(self, M, seed, layers=LAYERS, mode="chain"):
         from opennpu_b200 import dense
         self.dense = dense
-        self.M = M
+        self.M, self.mode = M, mode
         gen = torch.Generator(device="cuda")
         gen.manual_seed(seed)
         self.layers = []
@@ -78,7 +80,8 @@ class DecodeStack:
                 del qk, s
             self.layers.append(mats)
         torch.cuda.synchronize()
-        self.x = [torch.randn(M, HIDDEN, device="cuda", generator=gen).to(torch.bfloat16) for _ in range(layers)]
+        self.x_all = torch.randn(layers, M, HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+        self.x = [self.x_all[l] for l in range(layers)]
         self.y_qkv = torch.empty(M, QKV_N, device="cuda")
         self.a = torch.empty(M, INTER, device="cuda", dtype=torch.bfloat16)
         self.y = torch.empty(M, HIDDEN, device="cuda")
@@ -88,26 +91,50 @@ class DecodeStack:
         per_layer += M * QKV_N * 4 + M * INTER * 2 + M * HIDDEN * 4
         self.bytes_per_step = per_layer * layers
         self.weight_bytes_per_step = sum(int4_param_bytes(N, K) for _, N, K, _ in qwen3_8b_matrices()) * layers
-        self.launches_per_step = 3 * layers
+        self.chain = None
+        if mode == "chain":
+            self.chain = dense.DenseChain()
+            prev = -1
+            for l, mats in enumerate(self.layers):
+                prev = self.chain.add(mats["qkv"], self.x[l], self.y_qkv, dep=prev)
+                prev = self.chain.add(mats["gate_up"], self.x[l], self.a, epi=dense.EPI_SWIGLU, dep=prev)
+                prev = self.chain.add(mats["down"], self.a, self.y, dep=prev)
+            self.chain.prepare()
+        self.launches_per_step = 1 if mode == "chain" else 3 * layers
 
     def dominant(self):
-        """The dominant kernel of the step (gate_up GEMV + SwiGLU epilogue) alone, all layers:
-        (callable, algorithmic bytes per launch, launches)."""
+        """The dominant kernel of the step alone: (callable, algorithmic bytes per launch,
+        launches per call, kernel name). Chain mode: the chain kernel is the step's only launch;
+        launches mode: gate_up GEMV + SwiGLU epilogue over all layers."""
         d = self.dense
+        if self.chain is not None:
+            return self.chain.run, self.bytes_per_step, 1, "gemv_chain_kernel (one launch = the whole step)"
         N, K = 2 * INTER, HIDDEN
         nbytes = int4_param_bytes(N, K) + self.M * K * 2 + self.M * INTER * 2
 
         def run():
             for l, mats in enumerate(self.layers):
                 mats["gate_up"].mv(self.x[l], out=self.a, epi=d.EPI_SWIGLU)
-        return run, nbytes, len(self.layers)
+        return run, nbytes, len(self.layers), "gemv_int4_kernel gate_up 24576x4096 + SwiGLU"
 
     def step(self):
+        if self.chain is not None:
+            self.chain.run()
+            return
         d = self.dense
         for l, mats in enumerate(self.layers):
             mats["qkv"].mv(self.x[l], out=self.y_qkv)
             mats["gate_up"].mv(self.x[l], out=self.a, epi=d.EPI_SWIGLU)
             mats["down"].mv(self.a, out=self.y)
+
+    def step_e2e(self, hx, hy_qkv, hy):
+        """One step through the public API with host buffers: pinned bf16 activations of every
+        layer -> device, the step, the last layer's q/k/v and down outputs -> pinned host."""
+        self.x_all.copy_(hx, non_blocking=True)
+        self.step()
+        hy_qkv.copy_(self.y_qkv, non_blocking=True)
+        hy.copy_(self.y, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
 
     def step_host(self, xs_host, ys_host):
         """The same pass through the reference ABI's host-pointer call (onpu_dense_mv): fp32 host
@@ -148,7 +175,7 @@ class GemvRotation:
 
     def dominant(self):
         nbytes = self.bytes_per_step // len(self.mats)
-        return self.step, nbytes, len(self.mats)
+        return self.step, nbytes, len(self.mats), "gemv_int4_kernel 4096x4096"
 
     def step(self):
         for m in self.mats:
@@ -276,7 +303,8 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     hbm, _, peak_kind = peaks()
     M = args.m
-    work = DecodeStack(M, seed=1000 + rank, layers=args.layers) if args.config == "qwen3-8b" else GemvRotation(M, seed=1000 + rank)
+    work = (DecodeStack(M, seed=1000 + rank, layers=args.layers, mode=args.mode) if args.config == "qwen3-8b"
+            else GemvRotation(M, seed=1000 + rank))
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(max(args.warmup, 1)):
@@ -326,7 +354,7 @@ def run_ours(args):
     gbs = work.bytes_per_step * world / (ms_step * 1e-3) / 1e9
 
     # roofline of the dominant kernel alone: a graph of its launches, CUDA events on its stream
-    run_dom, dom_bytes, dom_n = work.dominant()
+    run_dom, dom_bytes, dom_n, dom_name = work.dominant()
     gdom = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gdom, stream=s):
         run_dom()
@@ -345,29 +373,47 @@ def run_ours(args):
     del gdom
     per_gpu_gbs = work.bytes_per_step / (ms_step * 1e-3) / 1e9
 
-    # end to end through the reference ABI's host-pointer call (rank-local, not graph-replayed)
+    # end to end through the public API with host buffers (pinned): inputs in, step, outputs out
     e2e = None
     if isinstance(work, DecodeStack) and not args.no_e2e:
-        xs = [np.ascontiguousarray(xl.float().cpu().numpy()) for xl in work.x]
-        ys = {"qkv": np.empty((M, QKV_N), np.float32), "gate_up": np.empty((M, 2 * INTER), np.float32),
-              "down": np.empty((M, HIDDEN), np.float32)}
-        work.step_host(xs, ys)
-        e_steps = max(2, min(args.steps, 5))
-        if world > 1:
-            torch.distributed.barrier()
-        t0 = time.perf_counter()
-        for _ in range(e_steps):
-            work.step_host(xs, ys)
-        dt = (time.perf_counter() - t0) / e_steps
+        hx = torch.empty(work.x_all.shape, dtype=torch.bfloat16, pin_memory=True)
+        hx.copy_(work.x_all)
+        hq = torch.empty(work.y_qkv.shape, dtype=torch.float32, pin_memory=True)
+        hy = torch.empty(work.y.shape, dtype=torch.float32, pin_memory=True)
+        e_steps = max(3, min(args.steps, 50))
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                work.step_e2e(hx, hq, hy)
+            if world > 1:
+                torch.distributed.barrier()
+            t0 = time.perf_counter()
+            for _ in range(e_steps):
+                work.step_e2e(hx, hq, hy)
+            dt = (time.perf_counter() - t0) / e_steps
         if world > 1:
             t = torch.tensor([dt], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             dt = float(t.item())
-        h2d = args.layers * M * (HIDDEN * 4 * 2 + INTER * 4)
-        d2h = args.layers * M * (QKV_N + 2 * INTER + HIDDEN) * 4
         e2e = {"value": round(work.bytes_per_step * world / dt / 1e9, 2), "unit": "GB/s",
-               "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(dt * 1e3, 3),
-               "path": "onpu_dense_mv (host fp32 in/out, reference ABI)"}
+               "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": (hq.numel() + hy.numel()) * 4,
+               "ms_per_step": round(dt * 1e3, 3), "steps": e_steps,
+               "path": ("onpu_chain_run" if work.chain is not None else "onpu_dense_mv_dev")
+               + " with pinned host input/output copies and a host synchronisation per step (wall clock)"}
+        # the reference ABI's host-pointer call (onpu_dense_mv: fp32 host in/out, copies and a
+        # synchronisation inside every call, SwiGLU on the host), as a second end-to-end figure
+        xs = [np.ascontiguousarray(xl.float().cpu().numpy()) for xl in work.x]
+        ys = {"qkv": np.empty((M, QKV_N), np.float32), "gate_up": np.empty((M, 2 * INTER), np.float32),
+              "down": np.empty((M, HIDDEN), np.float32)}
+        work.step_host(xs, ys)
+        r_steps = max(2, min(args.steps, 5))
+        t0 = time.perf_counter()
+        for _ in range(r_steps):
+            work.step_host(xs, ys)
+        rt = (time.perf_counter() - t0) / r_steps
+        e2e["reference_abi"] = {"value": round(work.bytes_per_step / rt / 1e9, 2), "unit": "GB/s",
+                                "ms_per_step": round(rt * 1e3, 3), "path": "onpu_dense_mv per matrix (host fp32)",
+                                "h2d_bytes_per_step": args.layers * M * (HIDDEN * 4 * 2 + INTER * 4),
+                                "d2h_bytes_per_step": args.layers * M * (QKV_N + 2 * INTER + HIDDEN) * 4}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu and isinstance(work, DecodeStack):
@@ -378,7 +424,8 @@ def run_ours(args):
     traffic = None
     tp = ROOT / "profiles" / "traffic.json"
     if tp.exists():
-        traffic = json.loads(tp.read_text()).get(args.config)
+        mode = args.mode if args.config == "qwen3-8b" else "launches"
+        traffic = json.loads(tp.read_text()).get(f"{args.config}/{mode}")
     if rank == 0:
         achieved = dom_bytes / (dom_us * 1e-6) / 1e9
         line = {
@@ -392,12 +439,12 @@ def run_ours(args):
                        "bytes_per_step_per_gpu": work.bytes_per_step,
                        "weight_bytes_per_step_per_gpu": work.weight_bytes_per_step,
                        "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (no flush needed)",
-                       "cuda_graph": graph is not None},
+                       "cuda_graph": graph is not None,
+                       "mode": args.mode if args.config == "qwen3-8b" else "launches"},
             "tokens_per_s": round(M * world / (ms_step * 1e-3), 1) if args.config == "qwen3-8b" else None,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": "gemv_int4 gate_up 24576x4096 + SwiGLU" if args.config == "qwen3-8b"
-                         else "gemv_int4 4096x4096", "algorithmic_bytes_per_launch": dom_bytes,
+                         "kernel": dom_name, "algorithmic_bytes_per_launch": dom_bytes,
                          "us_per_launch": round(dom_us, 3)},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
             "gpu_launches": work.launches_per_step * args.steps,
@@ -444,6 +491,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--mode", default="chain", choices=["chain", "launches"],
+                    help="chain: the step as one persistent GEMV-chain launch; launches: one launch per matrix")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers in the stack (profiling captures use fewer; the metric is quoted at 36)")
     args = ap.parse_args()

@@ -133,6 +133,34 @@ int onpu_dense_info(void *h, int64_t *out4);
 int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream);
 /* Prepare (allocate descriptors and scratch for) `rows`-row calls without running one. */
 int onpu_dense_prepare(void *h, int64_t rows);
+/* ---- GEMV chains: a decode step's dense GEMVs recorded once on fixed device buffers and run as
+ * ONE persistent launch (the GPU analogue of the reference's instruction stream per call,
+ * llama/ggml-opennpu/opennpu_core.hpp:418-505, and of onpu_ffn_run's gate_up -> act -> down
+ * sequence, onpu_api.cpp:423-446). Links run in order; a link whose x or y overlaps the y (or,
+ * for y, the x) of an earlier link waits on the device until that link is finished everywhere.
+ * Runs of one chain must be ordered on one stream. */
+void *onpu_chain_new(void);
+/* Append y = x . W^T (dense handle h, 1..16 rows; pointer rules of onpu_dense_mv_dev). dep: an
+ * earlier link this one must also wait for (-1: data overlaps only). The link index, < 0 on
+ * error. All links of a chain share one weight format. */
+int onpu_chain_add(void *chain, void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi,
+                   int dep);
+/* links, CTAs, shared memory per CTA, MMA n-tiles (CTAs and shared memory after prepare) */
+int onpu_chain_info(void *chain, int64_t *out4);
+/* the link a link waits for (-1 none; -2 bad index) */
+int onpu_chain_link_dep(void *chain, int link);
+/* Allocate the chain's scratch and upload its links (the first run does it when needed: call
+ * this outside stream capture). 0 ok. */
+int onpu_chain_prepare(void *chain);
+/* One launch on `stream`, asynchronous. 0 ok. */
+int onpu_chain_run(void *chain, void *stream);
+/* Tracing: later runs write %globaltimer stamps (ns) to the device buffer `stamps`
+ * [CTAs][links][8]: consumer start, dependency met, activations staged, math done, link counted,
+ * producer first copy, producer last copy, then the nanoseconds consumer warp 0 waited for weights
+ * during the link. NULL turns it off. CTAs from onpu_chain_info. */
+int onpu_chain_trace(void *chain, uint64_t *stamps);
+void onpu_chain_free(void *chain);
+
 /* onpu_dense_mv_dev with no allocation in the call: no reference counterpart (the NPU library
  * has no device scratch). Same arguments and result as onpu_dense_mv_dev, but the split-row
  * scratch and descriptors live in one static device array shared by every call on a device, for

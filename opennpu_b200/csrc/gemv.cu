@@ -34,6 +34,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include "gemv_core.cuh"
 #include "gpu_layout.cuh"
 #include "kernels.h"
 #include "ptx.cuh"
@@ -42,144 +43,8 @@ namespace onpu_b200 {
 
 namespace {
 
-constexpr int kConsumers = 4;                      // one warp per 16-row strip
-constexpr int kThreads = (kConsumers + 1) * 32;    // + the producer warp
-constexpr int kCPS = 4, kNS = 8;                   // chunks per stage, stages
-constexpr uint64_t kWaitLimitNs = 2000000000ull;   // a copy that has not landed in 2 s is a fault
-constexpr int kSlotFloats = 4 * 8 * 2 * 16;        // [strip][r][h][token] head partial sums of a CTA
-constexpr int kXSlot = 192;                        // per-stage activation slot: 128 B + 64 B pad
+using namespace gemv_core;
 
-__host__ __device__ constexpr int stage_w_bytes(int fmt) { return kCPS * chunk_bytes(fmt); }
-
-// two 16-bit scale/min values (strip rows r, r+8) -> fp32; mul[3] = 2^16 (an FMA-pipe shift)
-template <int FMT>
-__device__ __forceinline__ void decode_pair(uint32_t w, const uint32_t (&mul)[4], float &lo, float &hi) {
-    if constexpr (FMT == kFmtQ4F16) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w));
-        lo = f.x;
-        hi = f.y;
-    } else {
-        lo = __uint_as_float(w * mul[3]);
-        hi = __uint_as_float(w & 0xffff0000u);
-    }
-}
-
-// Codes of one packed word -> the four bf16x2 A registers (128 + q). The right shifts are
-// mul.hi by 2^28 / 2^24 / 2^20 passed in as kernel parameters: they run on the FMA pipe instead
-// of the half-rate integer pipe, which the mask-and-OR (LOP3) already keeps busy.
-__device__ __forceinline__ void codes_to_a(uint32_t w, const uint32_t (&mul)[4], uint32_t (&a)[4]) {
-    a[0] = (w & 0x000F000Fu) | 0x43004300u;
-    a[1] = (__umulhi(w, mul[0]) & 0x000F000Fu) | 0x43004300u;
-    a[2] = (__umulhi(w, mul[1]) & 0x000F000Fu) | 0x43004300u;
-    a[3] = (__umulhi(w, mul[2]) & 0x000F000Fu) | 0x43004300u;
-}
-
-__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
-                                         const float (&c)[4]) {
-    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
-        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
-        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
-          "f"(c[3]));
-}
-
-__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-
-__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
-
-__device__ __forceinline__ int worker_of(int c, int W, int T) {
-    return static_cast<int>((static_cast<int64_t>(c + 1) * W - 1) / T);
-}
-
-// One strip (16 rows) x one chunk (2 groups of 32 along K) into acc. wsb: the strip's bytes in
-// shared memory; xa[nt]: shared address of this lane's 8 activations of the chunk's first group
-// for n-tile nt (the second group is 64 B further; absent tokens read zeros).
-// Without a table (CI false): symmetric codes (128+q) - 136 = q - 8 exactly in bf16,
-// D = sum((q-8) x), acc += s * D; q4nx (128+q) - 128 = q, acc += s * sum(q x) + m * sum(x), with
-// sum(x) from an MMA against ones. With a table (CI true, resident activations): the MMA starts
-// from c * sum(x) read from shared memory at ca (+ gi * 8 * MT; c = -136 symmetric, -128 q4nx),
-// so the 128 + q codes go into the MMA as they are.
-template <int FMT, int NT, bool CI>
-__device__ __forceinline__ void strip_chunk(uint32_t wsb, const uint32_t (&xa)[NT], uint32_t ca, int lane, int r,
-                                            const uint32_t (&mul)[4], float (&acc)[NT][4]) {
-    const uint32_t off = FMT == kFmtQ4NX ? 0x43004300u : 0x43084308u;   // bf16x2 (128) / (136)
-    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
-    uint32_t bx[2][NT][4];
-#pragma unroll
-    for (int gi = 0; gi < 2; ++gi)
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const uint4 v = lds_v4(xa[nt] + gi * 64);
-            bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
-        }
-    const uint4 code = lds_v4(wsb + lane * 16);
-    const uint2 sc = lds_v2(wsb + kCodeBytes + r * 8);
-    uint2 mn = make_uint2(0, 0);
-    if constexpr (FMT == kFmtQ4NX) mn = lds_v2(wsb + kCodeBytes + kScaleBytes + r * 8);
-    constexpr int MT = 8 * NT;
-    float cinit[2][NT][4];
-    if constexpr (CI) {
-#pragma unroll
-        for (int gi = 0; gi < 2; ++gi)
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                const uint2 c2 = lds_v2(ca + (gi * MT + nt * 8) * 4);
-                cinit[gi][nt][0] = cinit[gi][nt][2] = __uint_as_float(c2.x);
-                cinit[gi][nt][1] = cinit[gi][nt][3] = __uint_as_float(c2.y);
-            }
-    }
-#pragma unroll
-    for (int gi = 0; gi < 2; ++gi) {
-        uint32_t a0[4], a1[4];
-        codes_to_a(gi ? code.z : code.x, mul, a0);
-        codes_to_a(gi ? code.w : code.y, mul, a1);
-        if constexpr (!CI) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                a0[i] = bf16x2_sub(a0[i], off);
-                a1[i] = bf16x2_sub(a1[i], off);
-            }
-        }
-        float s_lo, s_hi;
-        decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            float d[4];
-            if constexpr (CI) mma16816(d, a0, bx[gi][nt][0], bx[gi][nt][1], cinit[gi][nt]);
-            else mma16816(d, a0, bx[gi][nt][0], bx[gi][nt][1], zero4);
-            mma16816(d, a1, bx[gi][nt][2], bx[gi][nt][3], d);
-            acc[nt][0] = fmaf(s_lo, d[0], acc[nt][0]);
-            acc[nt][1] = fmaf(s_lo, d[1], acc[nt][1]);
-            acc[nt][2] = fmaf(s_hi, d[2], acc[nt][2]);
-            acc[nt][3] = fmaf(s_hi, d[3], acc[nt][3]);
-            if constexpr (FMT == kFmtQ4NX && CI) {
-                float m_lo, m_hi;
-                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
-                m_lo *= -0.0078125f;                       // cinit = -128 sum(x): m * sum(x)
-                m_hi *= -0.0078125f;
-                acc[nt][0] = fmaf(m_lo, cinit[gi][nt][0], acc[nt][0]);
-                acc[nt][1] = fmaf(m_lo, cinit[gi][nt][1], acc[nt][1]);
-                acc[nt][2] = fmaf(m_hi, cinit[gi][nt][2], acc[nt][2]);
-                acc[nt][3] = fmaf(m_hi, cinit[gi][nt][3], acc[nt][3]);
-            }
-            if constexpr (FMT == kFmtQ4NX && !CI) {
-                float m_lo, m_hi, xs[4];
-                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
-                const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
-                mma16816(xs, ones, bx[gi][nt][0], bx[gi][nt][1], zero4);
-                mma16816(xs, ones, bx[gi][nt][2], bx[gi][nt][3], xs);
-                acc[nt][0] = fmaf(m_lo, xs[0], acc[nt][0]);
-                acc[nt][1] = fmaf(m_lo, xs[1], acc[nt][1]);
-                acc[nt][2] = fmaf(m_hi, xs[2], acc[nt][2]);
-                acc[nt][3] = fmaf(m_hi, xs[3], acc[nt][3]);
-            }
-        }
-    }
-}
 
 // Store the finished sums of strip rows r (v_lo) and r+8 (v_hi) of one token (output row yr).
 template <int EPI>
@@ -217,13 +82,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     const int nst = (hi - lo + kCPS - 1) / kCPS;
     const int per_job = p.row_groups * p.chunks;
     constexpr bool xres = CI;                         // resident activations carry the offset table
-    const int xchunk = p.xslots * kXSlot, stage_x = kCPS * xchunk;   // per-stage activation layout
+    const int xchunk = p.xslots * kXSlot, xstage_bytes = kCPS * xchunk;   // per-stage activation layout
     const uint32_t sbase = smem_u32(smem);
     const uint32_t wring = sbase, xregion = sbase + kNS * STAGE_W;
     const uint32_t full = sbase + p.off_bar, empty = full + kNS * 8;
 
     if (!xres)   // the zero slot is never written; a chunk half past K gets a 64-B copy only
-        for (int e = threadIdx.x; e < kNS * stage_x / 16; e += blockDim.x)
+        for (int e = threadIdx.x; e < kNS * xstage_bytes / 16; e += blockDim.x)
             *reinterpret_cast<uint4 *>(smem + kNS * STAGE_W + e * 16) = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
         for (int s = 0; s < kNS; ++s) {
@@ -299,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
                 const int k0 = ckc * kChunkK;
                 const uint32_t nb = static_cast<uint32_t>(min(128, 2 * (p.K - k0)));
                 if (lane < xm)
-                    bulk_g2s(xregion + slot * stage_x + (c - c0) * xchunk + lane * kXSlot,
+                    bulk_g2s(xregion + slot * xstage_bytes + (c - c0) * xchunk + lane * kXSlot,
                              p.x + static_cast<int64_t>(xrow) * p.ldx + k0, nb, full + slot * 8);
                 if (++ckc == p.chunks) {
                     ckc = 0;
@@ -327,38 +192,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     int m = p.jobs[j].m;
 
     if (xres) {
-        // resident activations: token rows of xstride bytes, then one zero block of 128 B
-        const int n16 = p.K / 8, row16 = p.xstride / 16;   // 16-B pieces: data, row incl. zero pad
-        for (int e = threadIdx.x; e < m * row16; e += kConsumers * 32) {
-            const int n = e / row16, q = e - n * row16;
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (q < n16) v = ld_nc_v4(p.x + static_cast<int64_t>(p.jobs[j].xrow[n]) * p.ldx + q * 8);
-            *reinterpret_cast<uint4 *>(smem + kNS * STAGE_W + n * p.xstride + q * 16) = v;
-        }
-        if (threadIdx.x < 8)
-            *reinterpret_cast<uint4 *>(smem + kNS * STAGE_W + m * p.xstride + threadIdx.x * 16) = make_uint4(0, 0, 0, 0);
-        named_bar_sync(1, kConsumers * 32);
-        // offset table [k chunk][group][token slot] = c * sum of the token's 32 activations
-        constexpr int MT = 8 * NT;
-        const float c = FMT == kFmtQ4NX ? -128.0f : -136.0f;
-        float *tab = reinterpret_cast<float *>(smem + kNS * STAGE_W + p.ctab_off);
-        for (int e = threadIdx.x; e < p.chunks * 2 * MT; e += kConsumers * 32) {
-            const int tok = e % MT, grp = e / MT;             // grp = k chunk * 2 + group
-            float sum = 0.f;
-            if (tok < m && grp * 32 < p.K) {
-                const uint8_t *row = smem + kNS * STAGE_W + tok * p.xstride + grp * 64;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint4 v = *reinterpret_cast<const uint4 *>(row + q * 16);
-                    const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) sum += __uint_as_float(w4[i] << 16) + __uint_as_float(w4[i] & 0xffff0000u);
-                }
-            }
-            tab[e] = c * sum;
-        }
-        named_bar_sync(1, kConsumers * 32);
+        // resident activations: fp16 rows, a zero block, the offset table, token scales
+        const GemvJob *jb = p.jobs + j;
+        stage_activations<FMT, NT, false>(p.x, p.ldx, [jb](int n) { return jb->xrow[n]; }, m, p.K, p.xstride,
+                                smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
     }
+    const float *tscale = reinterpret_cast<const float *>(smem + kNS * STAGE_W + p.ctab_off +
+                                                          p.chunks * tab_chunk_bytes(NT));
 
     int yr[NT][2];
     uint32_t xrb[NT], xkm[NT];                        // activation base and per-chunk stride of this lane
@@ -391,6 +231,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
 
     // Close segment [a, b) of row group (j, g) for this strip.
     auto flush = [&](int a, int b) {
+        if (xres) finish_rows<NT>(acc, tscale, t);
         const int gstart = (j * p.row_groups + g) * p.chunks;
         if (a == gstart && b == gstart + p.chunks) {          // the whole row group is here
 #pragma unroll
@@ -473,7 +314,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     };
     // offset-table address of this lane's tokens 2t, 2t+1 for k chunk kcc (resident mode)
     const uint32_t ctab = xregion + p.ctab_off + t * 8;
-    auto caddr = [&](int kcc) { return ctab + kcc * (2 * 8 * NT * 4); };
+    auto caddr = [&](int kcc) { return ctab + kcc * tab_chunk_bytes(NT); };
+    const Unpack u{p.unpk[0], p.unpk[1], p.unpk[2]};
+    // resident activations take the fp16 path, per-stage slices the bf16 one
+    auto chunk_math = [&](uint32_t wsc, const uint32_t (&xa)[NT], int kcc) {
+        if constexpr (CI) strip_chunk_h<FMT, NT>(wsc, xa, caddr(kcc), lane, r, mul, u, acc);
+        else strip_chunk<FMT, NT, false>(wsc, xa, 0u, lane, r, mul, acc);
+    };
 
     bool failed = false;
     for (int st = 0; st < nst; ++st) {
@@ -483,30 +330,34 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
             if (lane == 0) atomicOr(p.err, 1);
         }
         const int c0 = lo + st * kCPS, n = min(hi - c0, kCPS);
-        const uint32_t wsb = wring + slot * STAGE_W + s * SB, xstage = slot * stage_x;
-        if (failed) {
-            // drain only: keep the barriers moving, skip the math and the outputs
-        } else if (n == kCPS && kc + kCPS < p.chunks) {
+        const uint32_t wsb = wring + slot * STAGE_W + s * SB, xstage = slot * xstage_bytes;
+        // after a timed-out wait (failed is per thread) only the math is skipped: the bookkeeping
+        // and every named barrier in flush() stay the same in all consumer threads
+        if (n == kCPS && kc + kCPS < p.chunks) {
             // the common case: a full stage inside one row group
+            if (!failed) {
 #pragma unroll
-            for (int ci = 0; ci < kCPS; ++ci) {
-                uint32_t xa[NT];
-                xaddr(xa, xstage, ci, kc + ci);
-                strip_chunk<FMT, NT, CI>(wsb + ci * CB, xa, caddr(kc + ci), lane, r, mul, acc);
+                for (int ci = 0; ci < kCPS; ++ci) {
+                    uint32_t xa[NT];
+                    xaddr(xa, xstage, ci, kc + ci);
+                    chunk_math(wsb + ci * CB, xa, kc + ci);
+                }
             }
             kc += kCPS;
         } else {
             for (int ci = 0; ci < n; ++ci) {
-                uint32_t xa[NT];
-                xaddr(xa, xstage, ci, kc);
-                strip_chunk<FMT, NT, CI>(wsb + ci * CB, xa, caddr(kc), lane, r, mul, acc);
+                if (!failed) {
+                    uint32_t xa[NT];
+                    xaddr(xa, xstage, ci, kc);
+                    chunk_math(wsb + ci * CB, xa, kc);
+                }
                 advance(c0 + ci);
             }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + slot * 8);
     }
-    if (!failed && seg < hi) flush(seg, hi);
+    if (seg < hi) flush(seg, hi);
 }
 
 template <int FMT, int NT, int EPI, bool CI>
@@ -573,10 +424,8 @@ int occ_fmt(int nt, int smem) {
 
 GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K) {
     GemvLayout L{};
-    const int64_t xstride = (K * 2 + 127) / 128 * 128 + 64;   // rows 64 B off mod 128: conflict-free
-    const int64_t mt = mmax > 8 ? 16 : 8;
-    const int64_t chunks = (K + kChunkK - 1) / kChunkK;
-    const int64_t res_bytes = mmax * xstride + 128 + chunks * 2 * mt * 4;   // rows, zero block, offset table
+    const int64_t xstride = xres_stride(K);
+    const int64_t res_bytes = xres_bytes(mmax, K, mmax > 8 ? 2 : 1, xstride);   // rows, zero block, table, scales
     L.xres = njobs == 1 && res_bytes <= kResidentXBudget;
     L.xstride = static_cast<int>(xstride);
     L.ctab_off = static_cast<int>(mmax * xstride + 128);

@@ -1,0 +1,428 @@
+// Device building blocks shared by the int4 GEMV kernels (gemv.cu: one matrix per launch;
+// chain.cu: a sequence of matrices per launch): pipeline constants, code unpacking, the
+// tensor-core strip x chunk product.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include "gpu_layout.cuh"
+#include "ptx.cuh"
+
+namespace onpu_b200 {
+namespace gemv_core {
+
+constexpr int kConsumers = 4;                      // one warp per 16-row strip
+constexpr int kThreads = (kConsumers + 1) * 32;    // + the producer warp
+constexpr int kCPS = 4, kNS = 8;                   // chunks per stage, stages
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // a copy that has not landed in 2 s is a fault
+constexpr int kSlotFloats = 4 * 8 * 2 * 16;        // [strip][r][h][token] head partial sums of a CTA
+constexpr int kXSlot = 192;                        // per-stage activation slot: 128 B + 64 B pad
+
+__host__ __device__ constexpr int stage_w_bytes(int fmt) { return kCPS * chunk_bytes(fmt); }
+
+// two 16-bit scale/min values (strip rows r, r+8) -> fp32; mul[3] = 2^16 (an FMA-pipe shift)
+template <int FMT>
+__device__ __forceinline__ void decode_pair(uint32_t w, const uint32_t (&mul)[4], float &lo, float &hi) {
+    if constexpr (FMT == kFmtQ4F16) {
+        lo = __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu)));
+        hi = __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+    } else {
+        lo = __uint_as_float(w * mul[3]);
+        hi = __uint_as_float(w & 0xffff0000u);
+    }
+}
+
+// Codes of one packed word -> the four bf16x2 A registers (128 + q). The right shifts are
+// mul.hi by 2^28 / 2^24 / 2^20 passed in as kernel parameters: they run on the FMA pipe instead
+// of the half-rate integer pipe, which the mask-and-OR (LOP3) already keeps busy.
+__device__ __forceinline__ void codes_to_a(uint32_t w, const uint32_t (&mul)[4], uint32_t (&a)[4]) {
+    a[0] = (w & 0x000F000Fu) | 0x43004300u;
+    a[1] = (__umulhi(w, mul[0]) & 0x000F000Fu) | 0x43004300u;
+    a[2] = (__umulhi(w, mul[1]) & 0x000F000Fu) | 0x43004300u;
+    a[3] = (__umulhi(w, mul[2]) & 0x000F000Fu) | 0x43004300u;
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                         const float (&c)[4]) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]), "f"(c[2]),
+          "f"(c[3]));
+}
+
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.0f + __expf(-g)); }
+
+__device__ __forceinline__ int worker_of(int c, int W, int T) {
+    return static_cast<int>((static_cast<int64_t>(c + 1) * W - 1) / T);
+}
+
+// One strip (16 rows) x one chunk (2 groups of 32 along K) into acc. wsb: the strip's bytes in
+// shared memory; xa[nt]: shared address of this lane's 8 activations of the chunk's first group
+// for n-tile nt (the second group is 64 B further; absent tokens read zeros).
+// Without a table (CI false): symmetric codes (128+q) - 136 = q - 8 exactly in bf16,
+// D = sum((q-8) x), acc += s * D; q4nx (128+q) - 128 = q, acc += s * sum(q x) + m * sum(x), with
+// sum(x) from an MMA against ones. With a table (CI true, resident activations): the MMA starts
+// from c * sum(x) read from shared memory at ca (+ gi * 8 * MT; c = -136 symmetric, -128 q4nx),
+// so the 128 + q codes go into the MMA as they are.
+template <int FMT, int NT, bool CI>
+__device__ __forceinline__ void strip_chunk(uint32_t wsb, const uint32_t (&xa)[NT], uint32_t ca, int lane, int r,
+                                            const uint32_t (&mul)[4], float (&acc)[NT][4]) {
+    const uint32_t off = FMT == kFmtQ4NX ? 0x43004300u : 0x43084308u;   // bf16x2 (128) / (136)
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t bx[2][NT][4];
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint4 v = lds_v4(xa[nt] + gi * 64);
+            bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
+        }
+    const uint4 code = lds_v4(wsb + lane * 16);
+    const uint2 sc = lds_v2(wsb + kCodeBytes + r * 8);
+    uint2 mn = make_uint2(0, 0);
+    if constexpr (FMT == kFmtQ4NX) mn = lds_v2(wsb + kCodeBytes + kScaleBytes + r * 8);
+    constexpr int MT = 8 * NT;
+    float cinit[2][NT][4];
+    if constexpr (CI) {
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const uint2 c2 = lds_v2(ca + (gi * MT + nt * 8) * 4);
+                cinit[gi][nt][0] = cinit[gi][nt][2] = __uint_as_float(c2.x);
+                cinit[gi][nt][1] = cinit[gi][nt][3] = __uint_as_float(c2.y);
+            }
+    }
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+        uint32_t a0[4], a1[4];
+        codes_to_a(gi ? code.z : code.x, mul, a0);
+        codes_to_a(gi ? code.w : code.y, mul, a1);
+        if constexpr (!CI) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                a0[i] = bf16x2_sub(a0[i], off);
+                a1[i] = bf16x2_sub(a1[i], off);
+            }
+        }
+        float s_lo, s_hi;
+        decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            float d[4];
+            if constexpr (CI) mma16816(d, a0, bx[gi][nt][0], bx[gi][nt][1], cinit[gi][nt]);
+            else mma16816(d, a0, bx[gi][nt][0], bx[gi][nt][1], zero4);
+            mma16816(d, a1, bx[gi][nt][2], bx[gi][nt][3], d);
+            acc[nt][0] = fmaf(s_lo, d[0], acc[nt][0]);
+            acc[nt][1] = fmaf(s_lo, d[1], acc[nt][1]);
+            acc[nt][2] = fmaf(s_hi, d[2], acc[nt][2]);
+            acc[nt][3] = fmaf(s_hi, d[3], acc[nt][3]);
+            if constexpr (FMT == kFmtQ4NX && CI) {
+                float m_lo, m_hi;
+                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
+                m_lo *= -0.0078125f;                       // cinit = -128 sum(x): m * sum(x)
+                m_hi *= -0.0078125f;
+                acc[nt][0] = fmaf(m_lo, cinit[gi][nt][0], acc[nt][0]);
+                acc[nt][1] = fmaf(m_lo, cinit[gi][nt][1], acc[nt][1]);
+                acc[nt][2] = fmaf(m_hi, cinit[gi][nt][2], acc[nt][2]);
+                acc[nt][3] = fmaf(m_hi, cinit[gi][nt][3], acc[nt][3]);
+            }
+            if constexpr (FMT == kFmtQ4NX && !CI) {
+                float m_lo, m_hi, xs[4];
+                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
+                const uint32_t ones[4] = {0x3F803F80u, 0x3F803F80u, 0x3F803F80u, 0x3F803F80u};
+                mma16816(xs, ones, bx[gi][nt][0], bx[gi][nt][1], zero4);
+                mma16816(xs, ones, bx[gi][nt][2], bx[gi][nt][3], xs);
+                acc[nt][0] = fmaf(m_lo, xs[0], acc[nt][0]);
+                acc[nt][1] = fmaf(m_lo, xs[1], acc[nt][1]);
+                acc[nt][2] = fmaf(m_hi, xs[2], acc[nt][2]);
+                acc[nt][3] = fmaf(m_hi, xs[3], acc[nt][3]);
+            }
+        }
+    }
+}
+
+// ================================================================ fp16 path (resident activations)
+// The resident kernels feed the tensor cores fp16: A = 1024 + q for strip rows r (mask 0x000F000F)
+// and 1024 + 16 q for rows r+8 (mask 0x00F000F0), one three-register LOP3 each from the packed
+// word or the word >> 8 (fp16's 10-bit mantissa holds both nibbles of a byte), 5 instructions per
+// 8 codes. Rows r+8 carry a factor 16, removed exactly at the end of a segment (finish_rows). The
+// activations are staged as fp16 (scaled per token by a power of two when |x| would leave the
+// fp16 range); the MMA starts from c * sum(x) per 32-group and token (sums from a table):
+// symmetric c = -1032 (rows r) and -1152 (rows r+8, = -(1024 + 16 * 8)); q4nx c = -1024 both.
+// Products (1024 + 16 q) * x are exact in fp32; the weights are never rounded.
+struct Unpack {
+    uint32_t mlo, mhi, magic;      // 0x000F000F, 0x00F000F0, 0x64006400 (kernel parameters: kept in registers)
+};
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));   // (a & b) | c
+    return d;
+}
+
+__device__ __forceinline__ void codes_to_a_h(uint32_t w, const Unpack &u, uint32_t (&a)[4]) {
+    const uint32_t s = w >> 8;
+    a[0] = lop3_and_or(w, u.mlo, u.magic);
+    a[1] = lop3_and_or(w, u.mhi, u.magic);
+    a[2] = lop3_and_or(s, u.mlo, u.magic);
+    a[3] = lop3_and_or(s, u.mhi, u.magic);
+}
+
+__device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// offset table bytes per 64-K chunk: [group][n-tile][t][2 floats] = sum(x) of tokens 2t, 2t+1
+__host__ __device__ constexpr int tab_chunk_bytes(int nt) { return 2 * nt * 4 * 8; }
+
+// One strip x one chunk, fp16 path. xa[nt]: this lane's fp16 activations of the chunk's first
+// group (second group 64 B further); ca: this lane's offset-table entry of the chunk (t * 8 in).
+template <int FMT, int NT>
+__device__ __forceinline__ void strip_chunk_h(uint32_t wsb, const uint32_t (&xa)[NT], uint32_t ca, int lane, int r,
+                                              const uint32_t (&mul)[4], const Unpack &u, float (&acc)[NT][4]) {
+    uint32_t bx[2][NT][4];
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint4 v = lds_v4(xa[nt] + gi * 64);
+            bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
+        }
+    const uint4 code = lds_v4(wsb + lane * 16);
+    const uint2 sc = lds_v2(wsb + kCodeBytes + r * 8);
+    uint2 mn = make_uint2(0, 0);
+    if constexpr (FMT == kFmtQ4NX) mn = lds_v2(wsb + kCodeBytes + kScaleBytes + r * 8);
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+        uint32_t a0[4], a1[4];
+        codes_to_a_h(gi ? code.z : code.x, u, a0);
+        codes_to_a_h(gi ? code.w : code.y, u, a1);
+        float s_lo, s_hi;
+        decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
+        constexpr float c_lo = FMT == kFmtQ4NX ? -1024.0f : -1032.0f, c_hi = FMT == kFmtQ4NX ? -1024.0f : -1152.0f;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
+            const float x0 = __uint_as_float(c2.x), x1 = __uint_as_float(c2.y);
+            float d[4] = {c_lo * x0, c_lo * x1, c_hi * x0, c_hi * x1};
+            mma16816_f16(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+            mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
+            acc[nt][0] = fmaf(s_lo, d[0], acc[nt][0]);
+            acc[nt][1] = fmaf(s_lo, d[1], acc[nt][1]);
+            acc[nt][2] = fmaf(s_hi, d[2], acc[nt][2]);
+            acc[nt][3] = fmaf(s_hi, d[3], acc[nt][3]);
+            if constexpr (FMT == kFmtQ4NX) {
+                // + m * sum(x) on rows r, 16 m * sum(x) on rows r+8
+                float m_lo, m_hi;
+                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
+                m_hi *= 16.0f;
+                acc[nt][0] = fmaf(m_lo, x0, acc[nt][0]);
+                acc[nt][1] = fmaf(m_lo, x1, acc[nt][1]);
+                acc[nt][2] = fmaf(m_hi, x0, acc[nt][2]);
+                acc[nt][3] = fmaf(m_hi, x1, acc[nt][3]);
+            }
+        }
+    }
+}
+
+// One whole chunk (all 4 strips) by one warp, fp16 path: the activations, the offset constants and
+// their table entries are read once per chunk and shared by the strips. wcb: the chunk in shared
+// memory; xa/ca as in strip_chunk_h; acc[strip][n-tile][4].
+template <int FMT, int NT>
+__device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], uint32_t ca, int lane, int r,
+                                        const uint32_t (&mul)[4], const Unpack &u, float (&acc)[4][NT][4]) {
+    constexpr int SB = strip_bytes(FMT);
+    constexpr float c_lo = FMT == kFmtQ4NX ? -1024.0f : -1032.0f, c_hi = FMT == kFmtQ4NX ? -1024.0f : -1152.0f;
+    uint32_t bx[2][NT][4];
+    float xs[2][NT][2];
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi)
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const uint4 v = lds_v4(xa[nt] + gi * 64);
+            bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
+            const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
+            xs[gi][nt][0] = __uint_as_float(c2.x);
+            xs[gi][nt][1] = __uint_as_float(c2.y);
+        }
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+        const uint4 code = lds_v4(wcb + s * SB + lane * 16);
+        const uint2 sc = lds_v2(wcb + s * SB + kCodeBytes + r * 8);
+        uint2 mn = make_uint2(0, 0);
+        if constexpr (FMT == kFmtQ4NX) mn = lds_v2(wcb + s * SB + kCodeBytes + kScaleBytes + r * 8);
+#pragma unroll
+        for (int gi = 0; gi < 2; ++gi) {
+            uint32_t a0[4], a1[4];
+            codes_to_a_h(gi ? code.z : code.x, u, a0);
+            codes_to_a_h(gi ? code.w : code.y, u, a1);
+            float s_lo, s_hi;
+            decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
+            float m_lo = 0.f, m_hi = 0.f;
+            if constexpr (FMT == kFmtQ4NX) {
+                decode_pair<FMT>(gi ? mn.y : mn.x, mul, m_lo, m_hi);
+                m_hi *= 16.0f;
+            }
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+                const float x0 = xs[gi][nt][0], x1 = xs[gi][nt][1];
+                float d[4] = {c_lo * x0, c_lo * x1, c_hi * x0, c_hi * x1};
+                mma16816_f16(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+                mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
+                acc[s][nt][0] = fmaf(s_lo, d[0], acc[s][nt][0]);
+                acc[s][nt][1] = fmaf(s_lo, d[1], acc[s][nt][1]);
+                acc[s][nt][2] = fmaf(s_hi, d[2], acc[s][nt][2]);
+                acc[s][nt][3] = fmaf(s_hi, d[3], acc[s][nt][3]);
+                if constexpr (FMT == kFmtQ4NX) {
+                    acc[s][nt][0] = fmaf(m_lo, x0, acc[s][nt][0]);
+                    acc[s][nt][1] = fmaf(m_lo, x1, acc[s][nt][1]);
+                    acc[s][nt][2] = fmaf(m_hi, x0, acc[s][nt][2]);
+                    acc[s][nt][3] = fmaf(m_hi, x1, acc[s][nt][3]);
+                }
+            }
+        }
+    }
+}
+
+// Bytes of the buffer in which the 4 consumer warps combine their per-strip partial sums:
+// [warp][strip][lane][n-tile * 4 floats]
+__host__ __device__ constexpr int combine_bytes(int nt) { return 4 * 4 * 32 * nt * 16; }
+
+// Resident activation region: m rows of xstride bytes (fp16), a 128-B zero block, the offset table
+// (chunks * tab_chunk_bytes), then 16 token scales (float) and 16 token maxima (uint).
+__host__ __device__ inline int64_t xres_bytes(int64_t m, int64_t K, int nt, int64_t xstride) {
+    const int64_t chunks = (K + kChunkK - 1) / kChunkK;
+    return m * xstride + 128 + chunks * tab_chunk_bytes(nt) + 128;
+}
+__host__ __device__ inline int64_t xres_stride(int64_t K) { return (K * 2 + 127) / 128 * 128 + 64; }   // 64 B off mod 128
+
+// Convert 32 bf16 activations (4 x 16 B) to fp16, returning their fp16-rounded sum and max |x|
+// (as fp32 bits); inv scales them first (a power of two).
+__device__ __forceinline__ float group_to_f16(uint4 (&v)[4], float inv, uint32_t &mx) {
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        uint32_t w4[4] = {v[q].x, v[q].y, v[q].z, v[q].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float lo = __uint_as_float(w4[k] << 16) * inv, hi = __uint_as_float(w4[k] & 0xffff0000u) * inv;
+            mx = max(mx, max(__float_as_uint(fabsf(lo)), __float_as_uint(fabsf(hi))));
+            const __half hl = __float2half_rn(lo), hh = __float2half_rn(hi);
+            sum += __half2float(hl) + __half2float(hh);
+            w4[k] = static_cast<uint32_t>(__half_as_ushort(hl)) | (static_cast<uint32_t>(__half_as_ushort(hh)) << 16);
+        }
+        v[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+    return sum;
+}
+
+// Stage m activation rows as fp16 + the offset table, by the nthr consumer threads (every one
+// must call this; named barrier 1 synchronises them). Row n is x + row_of(n) * ldx (bf16,
+// 16-byte aligned). CG: load through L2 only (rows written earlier in the same launch).
+// One pass: the (token, 32-group) items are spread evenly over the threads, each thread issues
+// all its loads (up to kSU groups) before converting, stores fp16 and writes the group's sum.
+// A token whose |x| exceeds 2^15 is redone scaled by 2^-e (rare) and tscale[n] = 2^e.
+template <int FMT, int NT, bool CG, typename RowOf>
+__device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, int m, int K, int xstride, uint8_t *xs, int tid,
+                        int nthr) {
+    constexpr int MT = 8 * NT, kSU = 4;
+    const int chunks = (K + kChunkK - 1) / kChunkK, G = K / 32;
+    float *tab = reinterpret_cast<float *>(xs + m * xstride + 128);
+    float *tscale = reinterpret_cast<float *>(xs + m * xstride + 128 + chunks * tab_chunk_bytes(NT));
+    unsigned *tmax = reinterpret_cast<unsigned *>(tscale + 16);
+    auto tab_at = [&](int grp, int tok) -> float & {
+        return tab[((grp * NT + tok / 8) * 4 + (tok % 8) / 2) * 2 + (tok & 1)];
+    };
+    // zeros: row tails, the zero block, table entries of absent tokens and of a group past K
+    const int rowb = K * 2, tail16 = (xstride - rowb) / 16;
+    for (int e = tid; e < m * tail16; e += nthr) {
+        const int n = e / tail16, q = e - n * tail16;
+        *reinterpret_cast<uint4 *>(xs + n * xstride + rowb + q * 16) = make_uint4(0, 0, 0, 0);
+    }
+    if (tid < 8) *reinterpret_cast<uint4 *>(xs + m * xstride + tid * 16) = make_uint4(0, 0, 0, 0);
+    for (int e = tid; e < chunks * 2 * MT; e += nthr) {
+        const int tok = e % MT, grp = e / MT;
+        if (tok >= m || grp >= G) tab_at(grp, tok) = 0.f;
+    }
+    if (tid < 16) tmax[tid] = 0u;
+    named_bar_sync(1, nthr);
+    const int items = m * G;
+    for (int e0 = 0; e0 < items; e0 += nthr * kSU) {
+        uint4 v[kSU][4];
+#pragma unroll
+        for (int u = 0; u < kSU; ++u) {
+            const int e = e0 + u * nthr + tid;
+            if (e < items) {
+                const int n = e / G, grp = e - n * G;
+                const uint16_t *src = x + static_cast<int64_t>(row_of(n)) * ldx + grp * 32;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[u][q] = CG ? ld_cg_v4(src + q * 8) : ld_nc_v4(src + q * 8);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kSU; ++u) {
+            const int e = e0 + u * nthr + tid;
+            if (e < items) {
+                const int n = e / G, grp = e - n * G;
+                uint32_t mx = 0;
+                const float sum = group_to_f16(v[u], 1.0f, mx);
+                uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) row[q] = v[u][q];
+                tab_at(grp, n) = sum;
+                if (mx > 0x47000000u) atomicMax(tmax + n, mx);      // only values above 2^15 matter
+            }
+        }
+    }
+    named_bar_sync(1, nthr);
+    bool big = false;
+#pragma unroll 1
+    for (int n = 0; n < m; ++n) big |= tmax[n] != 0u;
+    if (big) {   // rare: redo the tokens beyond the fp16 range, scaled by 2^-e
+        for (int e = tid; e < items; e += nthr) {
+            const int n = e / G, grp = e - n * G;
+            if (tmax[n] == 0u) continue;
+            const float inv = exp2f(-ceilf(log2f(__uint_as_float(tmax[n]) * (1.0f / 32768.0f))));
+            const uint16_t *src = x + static_cast<int64_t>(row_of(n)) * ldx + grp * 32;
+            uint4 v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = CG ? ld_cg_v4(src + q * 8) : ld_nc_v4(src + q * 8);
+            uint32_t mx = 0;
+            const float sum = group_to_f16(v, inv, mx);
+            uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) row[q] = v[q];
+            tab_at(grp, n) = sum;
+        }
+    }
+    if (tid < 16)
+        tscale[tid] = tid < m && tmax[tid] ? exp2f(ceilf(log2f(__uint_as_float(tmax[tid]) * (1.0f / 32768.0f)))) : 1.0f;
+    named_bar_sync(1, nthr);
+}
+
+// End of a segment (fp16 path): rows r+8 lose their factor 16, tokens their staging scale.
+template <int NT>
+__device__ __forceinline__ void finish_rows(float (&acc)[NT][4], const float *tscale, int t) {
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int f = 0; f < 4; ++f) {
+            const float sc = tscale[nt * 8 + 2 * t + (f & 1)];
+            acc[nt][f] *= f >= 2 ? sc * 0.0625f : sc;
+        }
+}
+
+}  // namespace gemv_core
+}  // namespace onpu_b200

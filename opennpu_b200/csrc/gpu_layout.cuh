@@ -96,11 +96,53 @@ struct GemvParams {
     int *err;                          // set non-zero on a timed-out wait
     int jobs_ready;                    // job list not written by the previous kernel in the stream
     uint32_t mul[4];                   // 2^28, 2^24, 2^20, 2^16: shift multipliers the compiler cannot fold
+    uint32_t unpk[3];                  // 0x000F000F, 0x00F000F0, 0x64006400 (fp16 code unpacking)
     int xslots;                        // per-stage activations: slots per chunk (max tokens + 1 zero slot)
     int xres;                          // activations resident in shared memory (single job)
     int xstride;                       // resident: bytes per token row
     int ctab_off;                      // resident: offset table position in the activation region
     int off_bar;                       // shared-memory offset of the mbarriers
 };
+
+// One link of a GEMV chain: y = x . W^T for m consecutive activation rows, run inside one
+// persistent launch together with the other links (chain.cu).
+struct ChainOp {
+    const uint8_t *w;                  // GPU-layout matrix
+    const uint16_t *x;                 // bf16 activations, rows 0..m-1, stride ldx (elements)
+    void *y;                           // output rows 0..m-1, stride ldy (elements of the output type)
+    const int *row_map;                // optional: GPU row -> output column (fp32/bf16 epilogues)
+    int64_t ldx, ldy;
+    int N, K;                          // logical shape
+    int row_groups, chunks;            // GPU layout
+    int epi;                           // GemvEpilogue
+    int dep;                           // last earlier link whose outputs/inputs overlap this one (-1: none)
+    int m;                             // tokens (1..16)
+    int xstride;                       // bytes per resident activation row in shared memory
+    int ctab_off;                      // offset table position in the activation region
+    int pad_;
+};
+
+struct ChainParams {
+    const ChainOp *ops;
+    int nops;
+    int workers;                       // CTAs (one resident wave); every link is split over all of them
+    float *part;                       // [kChainRing][workers][2][slot] partial sums of split row groups
+    unsigned *flags;                   // [kChainRing][workers][2] slot in use (zero at rest)
+    unsigned *rgcnt;                   // [nops][workers] arrivals per split row group (by first contributor)
+    unsigned *done;                    // [nops] workers finished per link, then one exit counter
+    int *err;
+    uint32_t mul[4];
+    uint32_t unpk[3];                  // 0x000F000F, 0x00F000F0, 0x64006400 (fp16 code unpacking)
+    int ns;                            // ring stages
+    int off_x, off_comb, off_bar;      // shared memory: activation region, combine buffer, mbarriers
+    unsigned long long *trace;         // optional: [workers][nops][kChainTrace] global-timer stamps
+    ChainOp op0;                       // the link when ops is null (a single GEMV, no descriptor upload)
+};
+
+constexpr int kChainRing = 4;          // links whose split-row partials may be outstanding at once
+// trace stamps per (CTA, link): consumer start, dependency met, activations staged, math done,
+// link counted; producer first copy issued, last copy issued; then the nanoseconds consumer
+// warp 0 spent waiting for weight stages during the link
+constexpr int kChainTrace = 8;
 
 }  // namespace onpu_b200

@@ -27,6 +27,24 @@ int gemv_chunks_per_stage();
 int64_t gemv_part_floats_per_worker(int ntiles);
 cudaError_t gemv_launch(int fmt, int ntiles, int epi, const GemvParams &p, int smem, cudaStream_t stream, bool pdl);
 
+// ---- GEMV chain (chain.cu): a sequence of dense GEMVs in one persistent launch
+// Rows per link: up to two MMA n-tiles of 8 tokens.
+constexpr int kChainMaxRows = 16;
+struct ChainLayout {
+    int ns;            // ring stages
+    int off_x;         // activation region
+    int off_comb;      // buffer in which the consumer warps combine a row group's partial sums
+    int off_bar;       // mbarriers
+    int smem;          // dynamic shared memory per CTA
+};
+// shared memory for a chain whose largest activation region (rows, offset table) is xregion_bytes
+ChainLayout chain_layout(int fmt, int ntiles, int64_t xregion_bytes, int ns);
+// activation region of one link (m rows of K), its row stride and offset-table position
+int64_t chain_xregion_bytes(int64_t m, int64_t K, int ntiles, int *xstride, int *ctab_off);
+int chain_ctas_per_sm(int fmt, int ntiles, int smem);        // 0: does not fit
+int64_t chain_part_floats_per_slot();
+cudaError_t chain_launch(int fmt, int ntiles, const ChainParams &p, int smem, cudaStream_t stream);
+
 // ---- layout conversion (repack.cu)
 // Where the codes of the matrix come from.
 enum RepackSource : int {

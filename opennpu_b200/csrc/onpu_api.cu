@@ -17,6 +17,7 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -110,6 +111,13 @@ struct Ctx {
     float *d_db = nullptr;
     int64_t db_cap = 0;
     std::vector<GemvJob> h_jobs;
+    // single dense GEMVs through the chain kernel (one link): split-row scratch and counters
+    float *d_c1part = nullptr;
+    int64_t c1part_cap = 0;
+    unsigned *d_c1flags = nullptr;
+    int64_t c1flags_cap = 0;
+    unsigned *d_c1cnt = nullptr;      // [W] row-group arrivals, then [2] link/exit counters
+    int64_t c1cnt_cap = 0;
     int64_t calls = 0;
     double wait_s = 0;
 };
@@ -235,6 +243,9 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     p.mul[1] = 1u << 24;
     p.mul[2] = 1u << 20;
     p.mul[3] = 1u << 16;
+    p.unpk[0] = 0x000F000Fu;
+    p.unpk[1] = 0x00F000F0u;
+    p.unpk[2] = 0x64006400u;
     p.xslots = lay.xslots;
     p.xres = lay.xres;
     p.xstride = lay.xstride;
@@ -244,6 +255,77 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     ++c.calls;
     return 0;
 }
+
+// The deepest ring (8 .. 4 stages) that still gives two CTAs per SM, else one CTA per SM; false if
+// the activation region does not fit at all.
+bool choose_chain_layout(int fmt, int ntiles, int64_t xregion, ChainLayout &lay, int &occ) {
+    occ = 0;
+    for (int want = 2; want >= 1; --want)
+        for (int ns = 8; ns >= 4; --ns) {
+            lay = chain_layout(fmt, ntiles, xregion, ns);
+            occ = lay.smem <= 227 * 1024 ? chain_ctas_per_sm(fmt, ntiles, lay.smem) : 0;
+            if (occ >= want) return true;
+        }
+    return false;
+}
+
+// One dense GEMV (1..kChainMaxRows rows, rows 0..rows-1 of x and y) as a one-link chain: the chain kernel's
+// fp16 chunk-per-warp math and last-arrival reduction, the link descriptor passed by value.
+// Returns 1 when the activations do not fit in shared memory (caller uses the job kernel).
+int run_chain1(Ctx &c, const GpuMat &m, int rows, int epi, const uint16_t *x, int64_t ldx, void *y, int64_t ldy,
+               cudaStream_t s) {
+    const int ntiles = rows > 8 ? 2 : 1;
+    ChainOp op{};
+    const int64_t xregion = chain_xregion_bytes(rows, m.gm.K, ntiles, &op.xstride, &op.ctab_off);
+    ChainLayout lay{};
+    int occ = 0;
+    if (!choose_chain_layout(m.gm.fmt, ntiles, xregion, lay, occ)) return 1;
+    const int W = c.nsm * occ;
+    if (!grow(c.d_c1part, c.c1part_cap, static_cast<int64_t>(kChainRing) * W * 2 * chain_part_floats_per_slot()) ||
+        !grow(c.d_c1flags, c.c1flags_cap, static_cast<int64_t>(kChainRing) * W * 2, true) ||
+        !grow(c.d_c1cnt, c.c1cnt_cap, static_cast<int64_t>(W) + 2, true))
+        return -1;
+    op.w = m.d_w;
+    op.x = x;
+    op.y = y;
+    op.row_map = epi == kEpiSwiGLU ? nullptr : m.d_row_map;
+    op.ldx = ldx;
+    op.ldy = ldy;
+    op.N = static_cast<int>(m.gm.N);
+    op.K = static_cast<int>(m.gm.K);
+    op.row_groups = m.gm.row_groups;
+    op.chunks = m.gm.chunks;
+    op.epi = epi;
+    op.dep = -1;
+    op.m = rows;
+    ChainParams p{};
+    p.ops = nullptr;
+    p.op0 = op;
+    p.nops = 1;
+    p.workers = W;
+    p.part = c.d_c1part;
+    p.flags = c.d_c1flags;
+    p.rgcnt = c.d_c1cnt;
+    p.done = c.d_c1cnt + W;
+    p.err = c.d_err;
+    p.mul[0] = 1u << 28;
+    p.mul[1] = 1u << 24;
+    p.mul[2] = 1u << 20;
+    p.mul[3] = 1u << 16;
+    p.unpk[0] = 0x000F000Fu;
+    p.unpk[1] = 0x00F000F0u;
+    p.unpk[2] = 0x64006400u;
+    p.ns = lay.ns;
+    p.off_x = lay.off_x;
+    p.off_comb = lay.off_comb;
+    p.off_bar = lay.off_bar;
+    p.trace = nullptr;
+    ONPU_CUDA(chain_launch(m.gm.fmt, ntiles, p, lay.smem, s), -1);
+    ++c.calls;
+    return 0;
+}
+
+void reset_chains_after_error();   // GEMV chains: clear their counters (defined with the chains)
 
 // after a synchronising host call: surface device-side timeouts and reset the split-row counters
 int check_device_err(Ctx &c) {
@@ -255,6 +337,9 @@ int check_device_err(Ctx &c) {
     if (h) {
         cudaMemset(c.d_err, 0, sizeof(int));
         if (c.d_cnt) cudaMemset(c.d_cnt, 0, sizeof(unsigned) * c.cnt_cap);
+        if (c.d_c1flags) cudaMemset(c.d_c1flags, 0, sizeof(unsigned) * c.c1flags_cap);
+        if (c.d_c1cnt) cudaMemset(c.d_c1cnt, 0, sizeof(unsigned) * c.c1cnt_cap);
+        reset_chains_after_error();
         set_err("a GEMV kernel timed out waiting for its weight copies (device status %d)", h);
         return -2;
     }
@@ -599,9 +684,16 @@ void onpu_dense_mv(void *h, const float *x, int64_t rows, float *y) {
     std::lock_guard<std::mutex> lk(g_mu);
     const int64_t K = d->mat.gm.K, N = d->mat.gm.N;
     const int64_t Kin = d->geo.ok ? d->geo.K : K;
-    JobSet *js = dense_jobs(d, rows);
-    if (!js || !stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
-    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
+    if (!stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
+    int rc = rows <= kChainMaxRows ? run_chain1(c, d->mat, static_cast<int>(rows), kEpiF32, c.d_x, K, c.d_y, N,
+                                                c.stream)
+                                   : 1;
+    if (rc < 0) return;
+    if (rc > 0) {
+        JobSet *js = dense_jobs(d, rows);
+        if (!js || run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false))
+            return;
+    }
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * rows * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
 }
@@ -889,6 +981,11 @@ int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
     }
     Ctx &c = ctx();
     std::lock_guard<std::mutex> lk(g_mu);
+    if (rows <= kChainMaxRows) {
+        const int rc = run_chain1(c, d->mat, static_cast<int>(rows), epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
+                                  static_cast<cudaStream_t>(stream));
+        if (rc <= 0) return rc;
+    }
     JobSet *js = dense_jobs(d, rows);
     if (!js) return -1;
     return run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
@@ -1063,6 +1160,9 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
     p.mul[1] = 1u << 24;
     p.mul[2] = 1u << 20;
     p.mul[3] = 1u << 16;
+    p.unpk[0] = 0x000F000Fu;
+    p.unpk[1] = 0x00F000F0u;
+    p.unpk[2] = 0x64006400u;
     p.xslots = lay.xslots;
     p.xres = lay.xres;
     p.xstride = lay.xstride;
@@ -1071,6 +1171,250 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
     ONPU_CUDA(gemv_launch(d->mat.gm.fmt, ntiles, epi, p, lay.smem, s, false), -1);
     ++c.calls;
     return 0;
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ GEMV chains
+// A decode step's dense GEMVs recorded once on fixed device buffers and run as one persistent
+// launch (chain.cu). Links keep their order; a link that reads or overwrites memory an earlier
+// link writes (or reads, for an overwrite) waits on the device until every CTA has finished the
+// latest such link. Runs of one chain must be ordered on one stream (its counters and partial
+// slots are shared by its runs).
+namespace {
+
+struct ChainH {
+    std::vector<ChainOp> ops;
+    std::vector<uintptr_t> xr, yr;    // per link: [x0, x1), [y0, y1) byte ranges
+    int fmt = -1, ntiles = 1;
+    bool ready = false;
+    ChainOp *d_ops = nullptr;
+    float *d_part = nullptr;
+    unsigned *d_flags = nullptr, *d_done = nullptr, *d_rgcnt = nullptr;
+    int W = 0, smem = 0;
+    ChainLayout lay{};
+    unsigned long long *trace = nullptr;   // caller's device buffer, or null
+    void release() {
+        if (d_ops) cudaFree(d_ops);
+        if (d_part) cudaFree(d_part);
+        if (d_flags) cudaFree(d_flags);
+        if (d_done) cudaFree(d_done);
+        if (d_rgcnt) cudaFree(d_rgcnt);
+        d_ops = nullptr;
+        d_part = nullptr;
+        d_flags = d_done = d_rgcnt = nullptr;
+        ready = false;
+    }
+    ChainH();
+    ~ChainH();
+};
+
+std::set<ChainH *> g_chains;           // live chains (guarded by g_mu)
+ChainH::ChainH() { g_chains.insert(this); }
+ChainH::~ChainH() {
+    g_chains.erase(this);
+    release();
+}
+
+// a timed-out wait can leave a chain's counters or flags raised: clear them (device is idle here)
+void reset_chains_after_error() {
+    for (ChainH *ch : g_chains) {
+        if (ch->d_flags) cudaMemset(ch->d_flags, 0, sizeof(unsigned) * kChainRing * ch->W * 2);
+        if (ch->d_rgcnt) cudaMemset(ch->d_rgcnt, 0, sizeof(unsigned) * ch->ops.size() * ch->W);
+        if (ch->d_done) cudaMemset(ch->d_done, 0, sizeof(unsigned) * (ch->ops.size() + 1));
+    }
+}
+
+bool overlap(uintptr_t a0, uintptr_t a1, uintptr_t b0, uintptr_t b1) { return a0 < b1 && b0 < a1; }
+
+int chain_prepare(Ctx &c, ChainH *ch) {
+    if (ch->ready) return 0;
+    if (ch->ops.empty()) {
+        set_err("onpu_chain: the chain has no links");
+        return -1;
+    }
+    cudaDeviceSynchronize();              // a previous run may still use the old buffers
+    ch->release();
+    int64_t xregion = 0;
+    for (auto &op : ch->ops) {
+        const int64_t b = chain_xregion_bytes(op.m, op.K, ch->ntiles, &op.xstride, &op.ctab_off);
+        xregion = std::max(xregion, b);
+    }
+    ChainLayout lay{};
+    int occ = 0;
+    if (!choose_chain_layout(ch->fmt, ch->ntiles, xregion, lay, occ)) {
+        set_err("onpu_chain: the largest link's activations (%lld bytes) do not fit in shared memory",
+                static_cast<long long>(xregion));
+        return -1;
+    }
+    ch->W = c.nsm * occ;
+    ch->smem = lay.smem;
+    ch->lay = lay;
+    const size_t nops = ch->ops.size();
+    const size_t part = static_cast<size_t>(kChainRing) * ch->W * 2 * chain_part_floats_per_slot();
+    const size_t nflags = static_cast<size_t>(kChainRing) * ch->W * 2, nrg = nops * ch->W;
+    ONPU_CUDA(cudaMalloc(&ch->d_ops, sizeof(ChainOp) * nops), -1);
+    ONPU_CUDA(cudaMalloc(&ch->d_part, sizeof(float) * part), -1);
+    ONPU_CUDA(cudaMalloc(&ch->d_flags, sizeof(unsigned) * nflags), -1);
+    ONPU_CUDA(cudaMalloc(&ch->d_rgcnt, sizeof(unsigned) * nrg), -1);
+    ONPU_CUDA(cudaMalloc(&ch->d_done, sizeof(unsigned) * (nops + 1)), -1);
+    ONPU_CUDA(cudaMemset(ch->d_flags, 0, sizeof(unsigned) * nflags), -1);
+    ONPU_CUDA(cudaMemset(ch->d_rgcnt, 0, sizeof(unsigned) * nrg), -1);
+    ONPU_CUDA(cudaMemset(ch->d_done, 0, sizeof(unsigned) * (nops + 1)), -1);
+    ONPU_CUDA(cudaMemcpy(ch->d_ops, ch->ops.data(), sizeof(ChainOp) * nops, cudaMemcpyHostToDevice), -1);
+    ch->ready = true;
+    return 0;
+}
+
+}  // namespace
+
+extern "C" {
+
+void *onpu_chain_new(void) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    return new ChainH();
+}
+
+int onpu_chain_add(void *chain, void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi,
+                   int dep) {
+    clear_err();
+    auto *ch = static_cast<ChainH *>(chain);
+    auto *d = static_cast<DenseH *>(h);
+    if (!ch || !d) {
+        set_err("onpu_chain_add: null handle");
+        return -1;
+    }
+    if (rows < 1 || rows > kChainMaxRows) {
+        set_err("onpu_chain_add: rows must be 1..%d (got %lld)", kChainMaxRows, static_cast<long long>(rows));
+        return -1;
+    }
+    if (epi < kEpiF32 || epi > kEpiSwiGLU || (epi == kEpiSwiGLU && !d->gateup)) {
+        set_err("onpu_chain_add: bad epilogue %d for this matrix", epi);
+        return -1;
+    }
+    if (d->geo.ok && d->geo.K != d->mat.gm.K) {
+        set_err("onpu_chain_add: K must be a multiple of 32");
+        return -1;
+    }
+    const int64_t K = d->mat.gm.K, ncol = epi == kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < K) {
+        set_err("onpu_chain_add: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+        return -1;
+    }
+    if (ldy < ncol || (reinterpret_cast<uintptr_t>(y) & 3)) {
+        set_err("onpu_chain_add: y row stride %lld is shorter than the output row", static_cast<long long>(ldy));
+        return -1;
+    }
+    if (ch->fmt >= 0 && ch->fmt != d->mat.gm.fmt) {
+        set_err("onpu_chain_add: every link of a chain must use the same weight format");
+        return -1;
+    }
+    const int idx = static_cast<int>(ch->ops.size());
+    if (dep >= idx) {
+        set_err("onpu_chain_add: dep %d does not name an earlier link", dep);
+        return -1;
+    }
+    const int esz = epi == kEpiF32 ? 4 : 2;
+    const uintptr_t x0 = reinterpret_cast<uintptr_t>(x), x1 = x0 + ((rows - 1) * ldx + K) * 2;
+    const uintptr_t y0 = reinterpret_cast<uintptr_t>(y), y1 = y0 + ((rows - 1) * ldy + ncol) * esz;
+    int d_auto = -1;
+    for (int i = idx - 1; i >= 0 && d_auto < 0; --i)
+        if (overlap(x0, x1, ch->yr[2 * i], ch->yr[2 * i + 1]) || overlap(y0, y1, ch->xr[2 * i], ch->xr[2 * i + 1]) ||
+            overlap(y0, y1, ch->yr[2 * i], ch->yr[2 * i + 1]))
+            d_auto = i;
+    ChainOp op{};
+    op.w = d->mat.d_w;
+    op.x = static_cast<const uint16_t *>(x);
+    op.y = y;
+    op.row_map = epi == kEpiSwiGLU ? nullptr : d->mat.d_row_map;
+    op.ldx = ldx;
+    op.ldy = ldy;
+    op.N = static_cast<int>(d->mat.gm.N);
+    op.K = static_cast<int>(K);
+    op.row_groups = d->mat.gm.row_groups;
+    op.chunks = d->mat.gm.chunks;
+    op.epi = epi;
+    op.dep = std::max(dep, d_auto);
+    op.m = static_cast<int>(rows);
+    ch->ops.push_back(op);
+    ch->xr.push_back(x0);
+    ch->xr.push_back(x1);
+    ch->yr.push_back(y0);
+    ch->yr.push_back(y1);
+    ch->fmt = d->mat.gm.fmt;
+    if (rows > 8) ch->ntiles = 2;
+    ch->ready = false;
+    return idx;
+}
+
+int onpu_chain_info(void *chain, int64_t *out4) {
+    auto *ch = static_cast<ChainH *>(chain);
+    out4[0] = static_cast<int64_t>(ch->ops.size());
+    out4[1] = ch->W;
+    out4[2] = ch->smem;
+    out4[3] = ch->ntiles;
+    return 0;
+}
+
+int onpu_chain_link_dep(void *chain, int link) {
+    auto *ch = static_cast<ChainH *>(chain);
+    if (link < 0 || link >= static_cast<int>(ch->ops.size())) return -2;
+    return ch->ops[link].dep;
+}
+
+int onpu_chain_prepare(void *chain) {
+    clear_err();
+    std::lock_guard<std::mutex> lk(g_mu);
+    return chain_prepare(ctx(), static_cast<ChainH *>(chain));
+}
+
+int onpu_chain_run(void *chain, void *stream) {
+    clear_err();
+    auto *ch = static_cast<ChainH *>(chain);
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (chain_prepare(c, ch)) return -1;
+    ChainParams p{};
+    p.ops = ch->d_ops;
+    p.nops = static_cast<int>(ch->ops.size());
+    p.workers = ch->W;
+    p.part = ch->d_part;
+    p.flags = ch->d_flags;
+    p.rgcnt = ch->d_rgcnt;
+    p.done = ch->d_done;
+    p.err = c.d_err;
+    p.mul[0] = 1u << 28;
+    p.mul[1] = 1u << 24;
+    p.mul[2] = 1u << 20;
+    p.mul[3] = 1u << 16;
+    p.unpk[0] = 0x000F000Fu;
+    p.unpk[1] = 0x00F000F0u;
+    p.unpk[2] = 0x64006400u;
+    p.ns = ch->lay.ns;
+    p.off_x = ch->lay.off_x;
+    p.off_comb = ch->lay.off_comb;
+    p.off_bar = ch->lay.off_bar;
+    p.trace = ch->trace;
+    ONPU_CUDA(chain_launch(ch->fmt, ch->ntiles, p, ch->smem, static_cast<cudaStream_t>(stream)), -1);
+    ++c.calls;
+    return 0;
+}
+
+int onpu_chain_trace(void *chain, uint64_t *stamps) {
+    auto *ch = static_cast<ChainH *>(chain);
+    ch->trace = reinterpret_cast<unsigned long long *>(stamps);
+    return 0;
+}
+
+void onpu_chain_free(void *chain) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    delete static_cast<ChainH *>(chain);
 }
 
 }  // extern "C"

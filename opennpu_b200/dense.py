@@ -113,6 +113,62 @@ class DenseMatrix:
         return q, s, m
 
 
+class DenseChain:
+    """A sequence of ``DenseMatrix`` GEMVs on fixed CUDA buffers, run as one persistent launch
+    (``onpu_chain_*``). Keep the tensors passed to ``add`` alive while the chain is used."""
+
+    def __init__(self):
+        lib = L.require_device()
+        self.h = lib.onpu_chain_new()
+        if not self.h:
+            raise L.OnpuError(f"onpu_chain_new: {L.last_error()}")
+        self._keep = []
+
+    def add(self, m, x, y, epi=EPI_F32, dep=-1):
+        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+        assert y.is_cuda and y.dim() == 2 and y.stride(1) == 1
+        idx = L.load().onpu_chain_add(self.h, m.h, x.data_ptr(), x.stride(0), x.shape[0], y.data_ptr(), y.stride(0),
+                                      epi, dep)
+        L.check(idx, "onpu_chain_add")
+        self._keep += [m, x, y]
+        return idx
+
+    def dep(self, link):
+        return L.load().onpu_chain_link_dep(self.h, link)
+
+    def info(self):
+        out = (L.C.c_int64 * 4)()
+        L.load().onpu_chain_info(self.h, out)
+        return tuple(out)
+
+    def prepare(self):
+        L.check(L.load().onpu_chain_prepare(self.h), "onpu_chain_prepare")
+
+    def run(self, stream=None):
+        L.check(L.load().onpu_chain_run(self.h, _stream_ptr(stream)), "onpu_chain_run")
+
+    def trace(self, on=True):
+        """Record %globaltimer stamps of later runs: returns the int64 CUDA tensor
+        [CTAs, links, 8] they go to (see onpu_chain_trace), or None when turned off."""
+        if not on:
+            L.load().onpu_chain_trace(self.h, None)
+            self._trace = None
+            return None
+        self.prepare()
+        ctas, links = self.info()[1], self.info()[0]
+        self._trace = torch.zeros(ctas, links, 8, dtype=torch.int64, device="cuda")
+        L.load().onpu_chain_trace(self.h, self._trace.data_ptr())
+        return self._trace
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                L.load().onpu_chain_free(self.h)
+                self.h = None
+        except Exception:
+            pass
+
+
 def check_device():
     """Synchronise and raise if a kernel reported a timed-out wait."""
     L.check(L.load().onpu_check_device(), "device status")

@@ -60,6 +60,14 @@ SIGNATURES = {
     "onpu_dense_mv_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
+    "onpu_chain_new": (P, []),
+    "onpu_chain_add": (I32, [P, P, P, I64, I64, P, I64, I32, I32]),
+    "onpu_chain_info": (I32, [P, I64P]),
+    "onpu_chain_link_dep": (I32, [P, I32]),
+    "onpu_chain_prepare": (I32, [P]),
+    "onpu_chain_run": (I32, [P, P]),
+    "onpu_chain_trace": (I32, [P, P]),
+    "onpu_chain_free": (None, [P]),
 }
 
 _LIB = None
