@@ -65,7 +65,7 @@ class DecodeStack:
     step is one GEMV chain (onpu_chain_*), every link ordered after its predecessor as in a real
     decode step; mode "launches": one onpu_dense_mv_dev launch per matrix."""
 
-    def __init__(self, M, seed, layers=LAYERS, mode="chain"):
+    def __init__(self, M, seed, layers=LAYERS, mode="launches"):
         from opennpu_b200 import dense
         self.dense = dense
         self.M, self.mode = M, mode
@@ -491,7 +491,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
-    ap.add_argument("--mode", default="chain", choices=["chain", "launches"],
+    ap.add_argument("--mode", default="launches", choices=["chain", "launches"],
                     help="chain: the step as one persistent GEMV-chain launch; launches: one launch per matrix")
     ap.add_argument("--layers", type=int, default=LAYERS,
                     help="decoder layers in the stack (profiling captures use fewer; the metric is quoted at 36)")

@@ -137,7 +137,6 @@ __device__ __noinline__ bool chain_flush(const ChainParams &p, const ChainOp *op
             const int tok = nt * 8 + 2 * t + (f & 1);
             if (tok < m) pslot[((s * 8 + r) * 2 + (f >> 1)) * 16 + tok] = sa[nt][f];
         }
-    __threadfence();                       // each thread's partials, before the arrival below
     named_bar_sync(1, kConsumers * 32);
     if (threadIdx.x == 0) {
         __threadfence();
@@ -202,7 +201,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
         int slot = 0, round = 0;                      // ring position of the next stage
         bool failed = false;
         for (int i = 0; i < p.nops; ++i) {
-            const ChainOp *opp = p.ops ? p.ops + i : &p.op0;
+            const ChainOp *opp = p.ops + i;
             const uint8_t *wb = opp->w;
             const int T = opp->row_groups * opp->chunks;
             const int lo = static_cast<int>(static_cast<int64_t>(w) * T / W);
@@ -244,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
     bool failed = false;
 
     for (int i = 0; i < p.nops; ++i) {
-        const ChainOp *opp = p.ops ? p.ops + i : &p.op0;
+        const ChainOp *opp = p.ops + i;
         const int chunks = opp->chunks, T = opp->row_groups * chunks;
         const int lo = static_cast<int>(static_cast<int64_t>(w) * T / W);
         const int hi = static_cast<int>(static_cast<int64_t>(w + 1) * T / W);
@@ -383,7 +382,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
             if (seg < hi) flush(seg, hi);
         }
         // ---- link i is finished here (outputs stored): count this CTA
-        __threadfence();                      // each thread's outputs, before the count below
         named_bar_sync(1, kConsumers * 32);
         if (threadIdx.x == 0) {
             __threadfence();

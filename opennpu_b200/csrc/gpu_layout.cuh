@@ -136,7 +136,6 @@ struct ChainParams {
     int ns;                            // ring stages
     int off_x, off_comb, off_bar;      // shared memory: activation region, combine buffer, mbarriers
     unsigned long long *trace;         // optional: [workers][nops][kChainTrace] global-timer stamps
-    ChainOp op0;                       // the link when ops is null (a single GEMV, no descriptor upload)
 };
 
 constexpr int kChainRing = 4;          // links whose split-row partials may be outstanding at once

@@ -111,13 +111,6 @@ struct Ctx {
     float *d_db = nullptr;
     int64_t db_cap = 0;
     std::vector<GemvJob> h_jobs;
-    // single dense GEMVs through the chain kernel (one link): split-row scratch and counters
-    float *d_c1part = nullptr;
-    int64_t c1part_cap = 0;
-    unsigned *d_c1flags = nullptr;
-    int64_t c1flags_cap = 0;
-    unsigned *d_c1cnt = nullptr;      // [W] row-group arrivals, then [2] link/exit counters
-    int64_t c1cnt_cap = 0;
     int64_t calls = 0;
     double wait_s = 0;
 };
@@ -269,62 +262,6 @@ bool choose_chain_layout(int fmt, int ntiles, int64_t xregion, ChainLayout &lay,
     return false;
 }
 
-// One dense GEMV (1..kChainMaxRows rows, rows 0..rows-1 of x and y) as a one-link chain: the chain kernel's
-// fp16 chunk-per-warp math and last-arrival reduction, the link descriptor passed by value.
-// Returns 1 when the activations do not fit in shared memory (caller uses the job kernel).
-int run_chain1(Ctx &c, const GpuMat &m, int rows, int epi, const uint16_t *x, int64_t ldx, void *y, int64_t ldy,
-               cudaStream_t s) {
-    const int ntiles = rows > 8 ? 2 : 1;
-    ChainOp op{};
-    const int64_t xregion = chain_xregion_bytes(rows, m.gm.K, ntiles, &op.xstride, &op.ctab_off);
-    ChainLayout lay{};
-    int occ = 0;
-    if (!choose_chain_layout(m.gm.fmt, ntiles, xregion, lay, occ)) return 1;
-    const int W = c.nsm * occ;
-    if (!grow(c.d_c1part, c.c1part_cap, static_cast<int64_t>(kChainRing) * W * 2 * chain_part_floats_per_slot()) ||
-        !grow(c.d_c1flags, c.c1flags_cap, static_cast<int64_t>(kChainRing) * W * 2, true) ||
-        !grow(c.d_c1cnt, c.c1cnt_cap, static_cast<int64_t>(W) + 2, true))
-        return -1;
-    op.w = m.d_w;
-    op.x = x;
-    op.y = y;
-    op.row_map = epi == kEpiSwiGLU ? nullptr : m.d_row_map;
-    op.ldx = ldx;
-    op.ldy = ldy;
-    op.N = static_cast<int>(m.gm.N);
-    op.K = static_cast<int>(m.gm.K);
-    op.row_groups = m.gm.row_groups;
-    op.chunks = m.gm.chunks;
-    op.epi = epi;
-    op.dep = -1;
-    op.m = rows;
-    ChainParams p{};
-    p.ops = nullptr;
-    p.op0 = op;
-    p.nops = 1;
-    p.workers = W;
-    p.part = c.d_c1part;
-    p.flags = c.d_c1flags;
-    p.rgcnt = c.d_c1cnt;
-    p.done = c.d_c1cnt + W;
-    p.err = c.d_err;
-    p.mul[0] = 1u << 28;
-    p.mul[1] = 1u << 24;
-    p.mul[2] = 1u << 20;
-    p.mul[3] = 1u << 16;
-    p.unpk[0] = 0x000F000Fu;
-    p.unpk[1] = 0x00F000F0u;
-    p.unpk[2] = 0x64006400u;
-    p.ns = lay.ns;
-    p.off_x = lay.off_x;
-    p.off_comb = lay.off_comb;
-    p.off_bar = lay.off_bar;
-    p.trace = nullptr;
-    ONPU_CUDA(chain_launch(m.gm.fmt, ntiles, p, lay.smem, s), -1);
-    ++c.calls;
-    return 0;
-}
-
 void reset_chains_after_error();   // GEMV chains: clear their counters (defined with the chains)
 
 // after a synchronising host call: surface device-side timeouts and reset the split-row counters
@@ -337,8 +274,6 @@ int check_device_err(Ctx &c) {
     if (h) {
         cudaMemset(c.d_err, 0, sizeof(int));
         if (c.d_cnt) cudaMemset(c.d_cnt, 0, sizeof(unsigned) * c.cnt_cap);
-        if (c.d_c1flags) cudaMemset(c.d_c1flags, 0, sizeof(unsigned) * c.c1flags_cap);
-        if (c.d_c1cnt) cudaMemset(c.d_c1cnt, 0, sizeof(unsigned) * c.c1cnt_cap);
         reset_chains_after_error();
         set_err("a GEMV kernel timed out waiting for its weight copies (device status %d)", h);
         return -2;
@@ -684,16 +619,9 @@ void onpu_dense_mv(void *h, const float *x, int64_t rows, float *y) {
     std::lock_guard<std::mutex> lk(g_mu);
     const int64_t K = d->mat.gm.K, N = d->mat.gm.N;
     const int64_t Kin = d->geo.ok ? d->geo.K : K;
-    if (!stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
-    int rc = rows <= kChainMaxRows ? run_chain1(c, d->mat, static_cast<int>(rows), kEpiF32, c.d_x, K, c.d_y, N,
-                                                c.stream)
-                                   : 1;
-    if (rc < 0) return;
-    if (rc > 0) {
-        JobSet *js = dense_jobs(d, rows);
-        if (!js || run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false))
-            return;
-    }
+    JobSet *js = dense_jobs(d, rows);
+    if (!js || !stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
+    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * rows * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
 }
@@ -981,11 +909,6 @@ int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
     }
     Ctx &c = ctx();
     std::lock_guard<std::mutex> lk(g_mu);
-    if (rows <= kChainMaxRows) {
-        const int rc = run_chain1(c, d->mat, static_cast<int>(rows), epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
-                                  static_cast<cudaStream_t>(stream));
-        if (rc <= 0) return rc;
-    }
     JobSet *js = dense_jobs(d, rows);
     if (!js) return -1;
     return run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, epi, static_cast<const uint16_t *>(x), ldx, y, ldy,

@@ -38,10 +38,12 @@ def _call(fn, m, x, rows, epi):
 
 
 def _close(a, b):
+    # two bf16 outputs may round one bf16 ulp apart (2^-8 relative) on top of the fp32 tolerance
+    ulp = b.float().abs().max().item() * 2.0 ** -8 if b.dtype == torch.bfloat16 else 0.0
     a, b = a.float(), b.float()
     err = (a - b).norm() / b.norm().clamp_min(1e-30)
     assert err.item() <= REL_L2, err.item()
-    assert (a - b).abs().max().item() <= MAX_ABS
+    assert (a - b).abs().max().item() <= MAX_ABS + ulp
 
 
 # (N, K, gateup, epilogue, (rows of call 1, rows of call 2))
