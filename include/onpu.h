@@ -131,6 +131,13 @@ int onpu_dense_info(void *h, int64_t *out4);
  * device (by epi). A first call for a given row count allocates (call it outside stream capture);
  * later calls with that row count allocate nothing. 0 ok, < 0 error. */
 int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream);
+/* Y = X . W^T for many tokens (prefill) on the tensor cores (tcgen05, fp32 accumulators in tensor
+ * memory); same arguments as onpu_dense_mv_dev, any rows >= 1. The weights are dequantised to
+ * fp16 (one rounding per weight) and the activations copied to fp16 first (a token beyond the fp16
+ * range is scaled by a power of two). Replaces the reference's multi-token device path
+ * (opennpu/native/npu4/kernels/gemm8.cc:33-139, one 8-token pass per 8 tokens). Asynchronous;
+ * allocates its fp16 activation copy on first use of a larger row count. 0 ok, < 0 error. */
+int onpu_dense_mm_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream);
 /* Prepare (allocate descriptors and scratch for) `rows`-row calls without running one. */
 int onpu_dense_prepare(void *h, int64_t rows);
 /* ---- GEMV chains: a decode step's dense GEMVs recorded once on fixed device buffers and run as

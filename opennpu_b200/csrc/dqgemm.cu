@@ -1,0 +1,452 @@
+// int4 group-32 dequant-GEMM for prefill (many tokens per weight pass) on the 5th-generation
+// tensor cores: Y[M][N] = X[M][K] . W^T, W in the GPU layout (int4 codes + per-32 scales).
+//
+// Replaces the reference's multi-token NPU path (the 8-token GEMM opennpu/native/npu4/kernels/
+// gemm8.cc:33-139 run ceil(M/8) times, and the MLIR-AIR prefill devices cited in
+// opennpu/native/prefill.py:107-256 for shapes only). Arithmetic contract as the reference's
+// dequantise-then-matmul (reference.py:24-28): W dequantised per 32 along K, fp32 accumulation.
+// Here the dequantised weight is rounded once to fp16 and the activations are fp16 (exact for
+// bf16 inputs in the fp16 range; a token beyond it is scaled by a power of two and unscaled in
+// the epilogue): both tensor-core operands must have one type, and bf16 weights would round
+// 8x coarser.
+//
+// One CTA computes a 128 (tokens) x 256 (weight rows) tile; the fp32 accumulator lives in tensor
+// memory (256 columns). Warp roles:
+//  * warp 0: one thread issues the copies: the fp16 activation tile of each 64-K stage through a
+//    128-byte-swizzled tensor map (TMA, no multicast), and the int4 chunks of the tile's four row
+//    groups as 1-D bulk copies into a raw ring.
+//  * warp 1: allocates tensor memory; one thread issues tcgen05.mma kind::f16 (M128 N256 K16,
+//    four per stage) from shared-memory descriptors and commits each stage's completion to the
+//    mbarrier that frees the stage.
+//  * warps 2-5: dequantise each raw chunk into the stage's fp16 B tile in the canonical K-major
+//    128-byte-swizzled layout (a lane's 16 bytes of codes are two 8-K runs of two rows: one LOP3,
+//    one f16x2 subtract and one f16x2 multiply per pair of weights, 16-byte stores), then after
+//    the last stage read the accumulator with tcgen05.ld (each warp its 32 lanes) and store.
+// Every wait is bounded (2 s of global time) and reports through the error word.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "gpu_layout.cuh"
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace onpu_b200 {
+
+namespace {
+
+constexpr int kTM = 128, kTN = 256, kTK = 64;           // CTA tile: tokens, weight rows, K per stage
+constexpr int kOpStages = 3, kRawStages = 4;
+constexpr int kXTile = kTM * kTK * 2;                   // 16 KB fp16 activations
+constexpr int kWTile = kTN * kTK * 2;                   // 32 KB fp16 weights
+constexpr int kRawMax = 4 * 2560;                       // four row groups' chunk (q4nx is largest)
+constexpr int kGThreads = 192;                          // 6 warps
+constexpr int kTmemCols = 256;
+constexpr uint64_t kWaitNs = 2000000000ull;
+
+constexpr int smem_bytes() {
+    return 1024 /* alignment slack */ + kOpStages * (kXTile + kWTile) + kRawStages * kRawMax +
+           (2 * kOpStages + 2 * kRawStages + 1) * 8 + 16;
+}
+
+// ---------------------------------------------------------------- tcgen05 / TMA
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        ::"r"(dst), "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_alloc(uint32_t slot, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot), "r"(ncols));
+}
+__device__ __forceinline__ void tmem_relinquish() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, rows of 128 B in 8-row atoms 1024 B
+// apart (stride byte offset), start address in 16-byte units; version 1 (Blackwell). The tile
+// base is 1024-aligned, so the base offset is 0.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+    uint64_t d = static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>(1) << 16;                  // leading byte offset (unused when swizzled)
+    d |= static_cast<uint64_t>(1024 >> 4) << 32;          // stride byte offset
+    d |= static_cast<uint64_t>(1) << 46;                  // descriptor version
+    d |= static_cast<uint64_t>(2) << 61;                  // SWIZZLE_128B
+    return d;
+}
+
+// Instruction descriptor for kind::f16: fp32 accumulator, fp16 A and B, both K-major, N and M.
+constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
+                            (static_cast<uint32_t>(kTM >> 4) << 24);
+
+// byte offset of 16-byte chunk c (0..7, 8 fp16 along K) of row n in a K-major 128-byte-swizzled tile
+__device__ __forceinline__ uint32_t swz(int n, int c) {
+    return static_cast<uint32_t>((n >> 3) * 1024 + (n & 7) * 128 + ((c ^ (n & 7)) << 4));
+}
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// 16-bit scale (fp16, or bf16 for the reference formats) -> fp16 bits
+template <int FMT>
+__device__ __forceinline__ uint32_t to_f16_bits(uint32_t v16) {
+    if constexpr (FMT == kFmtQ4F16) return v16;
+    return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(__uint_as_float(v16 << 16))));
+}
+
+template <int FMT, int EPI>
+__global__ void __launch_bounds__(kGThreads, 1)
+    dqgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ DqGemmParams p) {
+    constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT);
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t s0 = smem_u32(smem_raw), sb = (s0 + 1023u) & ~1023u;
+    uint8_t *base = smem_raw + (sb - s0);
+    const uint32_t xs = sb, ws = xs + kOpStages * kXTile, raw = ws + kOpStages * kWTile;
+    const uint32_t bars = raw + kRawStages * kRawMax;
+    const uint32_t op_full = bars, op_empty = op_full + kOpStages * 8, raw_full = op_empty + kOpStages * 8,
+                   raw_empty = raw_full + kRawStages * 8, acc_full = raw_empty + kRawStages * 8;
+    const uint32_t tmem_slot = acc_full + 8;
+    volatile uint32_t *tmem_slot_p = reinterpret_cast<volatile uint32_t *>(base + (tmem_slot - sb));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n0 = blockIdx.x * kTN, m0 = blockIdx.y * kTM, g0 = n0 / kRowGroup;
+    const int nk = p.chunks;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kOpStages; ++s) {
+            mbar_init(op_full + s * 8, 1 + 4);             // producer (with the copy bytes) + 4 dequant warps
+            mbar_init(op_empty + s * 8, 1);                // tcgen05.commit
+        }
+        for (int r = 0; r < kRawStages; ++r) {
+            mbar_init(raw_full + r * 8, 1);
+            mbar_init(raw_empty + r * 8, 4);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init_fence();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot_p;
+    bool failed = false;
+
+    if (warp == 0) {
+        // ============================================================ copies
+        if (lane == 0) {
+            int nvalid = 0;
+            for (int gg = 0; gg < 4; ++gg) nvalid += g0 + gg < p.row_groups;
+            for (int kt = 0; kt < nk && !failed; ++kt) {
+                const int r = kt % kRawStages, rr = kt / kRawStages;
+                if (rr > 0 && !mbar_wait_bounded(raw_empty + r * 8, (rr - 1) & 1, kWaitNs)) {
+                    failed = true;
+                    break;
+                }
+                mbar_arrive_expect_tx(raw_full + r * 8, static_cast<uint32_t>(nvalid * CB));
+                for (int gg = 0; gg < 4; ++gg)
+                    if (g0 + gg < p.row_groups)
+                        bulk_g2s(raw + r * kRawMax + gg * CB,
+                                 p.w + (static_cast<int64_t>(g0 + gg) * p.chunks + kt) * CB, CB, raw_full + r * 8);
+                const int s = kt % kOpStages, sr = kt / kOpStages;
+                if (sr > 0 && !mbar_wait_bounded(op_empty + s * 8, (sr - 1) & 1, kWaitNs)) {
+                    failed = true;
+                    break;
+                }
+                mbar_arrive_expect_tx(op_full + s * 8, kXTile);
+                tma_load_2d(xs + s * kXTile, &tmap_x, kt * kTK, m0, op_full + s * 8);
+            }
+            if (failed) atomicOr(p.err, 64);
+        }
+    } else if (warp == 1) {
+        // ============================================================ tensor-core issue
+        if (lane == 0) {
+            for (int kt = 0; kt < nk; ++kt) {
+                const int s = kt % kOpStages, sr = kt / kOpStages;
+                if (!mbar_wait_bounded(op_full + s * 8, sr & 1, kWaitNs)) {
+                    atomicOr(p.err, 128);
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int kk = 0; kk < kTK / 16; ++kk)
+                    tc_mma_f16(tmem, sw128_desc(xs + s * kXTile + kk * 32), sw128_desc(ws + s * kWTile + kk * 32), kIdesc,
+                               (kt | kk) != 0 ? 1u : 0u);
+                tc_commit(op_empty + s * 8);
+            }
+            tc_commit(acc_full);                           // arrives once every issued MMA has completed
+        }
+    } else {
+        // ============================================================ dequantise, then epilogue
+        const int dt = threadIdx.x - 64, dw = warp - 2;
+        const uint32_t mlo = p.unpk[0], magic = p.unpk[2];
+        const uint32_t c_off = FMT == kFmtQ4NX ? 0x64006400u : 0x64086408u;   // 1024 / 1032 in f16x2
+        for (int kt = 0; kt < nk; ++kt) {
+            const int r = kt % kRawStages, rr = kt / kRawStages, s = kt % kOpStages, sr = kt / kOpStages;
+            if (!failed && !mbar_wait_bounded(raw_full + r * 8, rr & 1, kWaitNs)) failed = true;
+            if (!failed && sr > 0 && !mbar_wait_bounded(op_empty + s * 8, (sr - 1) & 1, kWaitNs)) failed = true;
+            if (!failed) {
+                const uint32_t rbase = raw + r * kRawMax, wbase = ws + s * kWTile;
+                uint8_t *wtile = base + (wbase - sb);
+#pragma unroll 1
+                for (int b = 0; b < 4; ++b) {
+                    const int blk = dt + b * 128, gg = blk >> 7, st = (blk >> 5) & 3, L = blk & 31;
+                    if (g0 + gg >= p.row_groups) continue;
+                    const int rq = L >> 2, t = L & 3;
+                    const uint32_t sbase = rbase + gg * CB + st * SB;
+                    const uint4 code = lds_v4(sbase + L * 16);
+                    const uint2 sc = lds_v2(sbase + kCodeBytes + rq * 8);
+                    uint2 mn = make_uint2(0, 0);
+                    if constexpr (FMT == kFmtQ4NX) mn = lds_v2(sbase + kCodeBytes + kScaleBytes + rq * 8);
+                    const int nlo = gg * kRowGroup + st * kStripRows + rq, nhi = nlo + 8;
+#pragma unroll
+                    for (int gi = 0; gi < 2; ++gi) {
+                        const uint32_t sp = gi ? sc.y : sc.x;
+                        const uint32_t slo = to_f16_bits<FMT>(sp & 0xffffu), shi = to_f16_bits<FMT>(sp >> 16);
+                        const uint32_t slo2 = slo | (slo << 16), shi2 = shi | (shi << 16);
+                        uint32_t mlo2 = 0, mhi2 = 0;
+                        if constexpr (FMT == kFmtQ4NX) {
+                            const uint32_t mp = gi ? mn.y : mn.x;
+                            const uint32_t a = to_f16_bits<FMT>(mp & 0xffffu), b2 = to_f16_bits<FMT>(mp >> 16);
+                            mlo2 = a | (a << 16);
+                            mhi2 = b2 | (b2 << 16);
+                        }
+                        uint32_t rlo[4], rhi[4];
+#pragma unroll
+                        for (int j = 0; j < 2; ++j) {
+                            const uint32_t w = gi ? (j ? code.w : code.z) : (j ? code.y : code.x);
+                            uint32_t a[4];
+                            a[0] = lop3_and_or(w, mlo, magic);
+                            a[1] = lop3_and_or(w >> 4, mlo, magic);
+                            a[2] = lop3_and_or(w >> 8, mlo, magic);
+                            a[3] = lop3_and_or(w >> 12, mlo, magic);
+#pragma unroll
+                            for (int i = 0; i < 4; ++i) {
+                                const uint32_t q = hsub2(a[i], c_off);          // exact: q - 8 (q4nx: q)
+                                if constexpr (FMT == kFmtQ4NX) a[i] = hfma2(q, (i & 1) ? shi2 : slo2, (i & 1) ? mhi2 : mlo2);
+                                else a[i] = hmul2(q, (i & 1) ? shi2 : slo2);
+                            }
+                            rlo[2 * j] = a[0];
+                            rlo[2 * j + 1] = a[2];
+                            rhi[2 * j] = a[1];
+                            rhi[2 * j + 1] = a[3];
+                        }
+                        *reinterpret_cast<uint4 *>(wtile + swz(nlo, gi * 4 + t)) = make_uint4(rlo[0], rlo[1], rlo[2], rlo[3]);
+                        *reinterpret_cast<uint4 *>(wtile + swz(nhi, gi * 4 + t)) = make_uint4(rhi[0], rhi[1], rhi[2], rhi[3]);
+                    }
+                }
+                fence_proxy_async_smem();                  // generic stores -> tensor-core reads
+            }
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(op_full + s * 8);
+                mbar_arrive(raw_empty + r * 8);
+            }
+        }
+        if (failed && lane == 0) atomicOr(p.err, 256);
+        (void)dw;
+
+        // ---- epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. +31 = tokens of the tile
+        const bool acc_ok = mbar_wait_bounded(acc_full, 0, kWaitNs);
+        tc_fence_after();
+        const int quarter = warp & 3, row = m0 + quarter * 32 + lane;
+        const float tsc = row < p.M ? p.tscale[row] : 0.f;
+        const bool do_store = acc_ok && row < p.M;
+        for (int c = 0; c < kTN / 32; ++c) {
+            uint32_t v[32];
+            __syncwarp();                                  // tcgen05.ld is warp-collective
+            tc_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, v);
+            if (!do_store) continue;
+            const int nb = n0 + c * 32;
+            if constexpr (EPI == kEpiSwiGLU) {
+                // columns are GPU rows: strip rows 0-7 gate, 8-15 up of output 8 * strip + r
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int strip = (nb >> 4) + h;
+                    if (strip * 16 >= p.N) continue;
+                    __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(row) * p.ldy + strip * 8;
+#pragma unroll
+                    for (int r8 = 0; r8 < 8; ++r8) {
+                        const float gte = __uint_as_float(v[h * 16 + r8]) * tsc, up = __uint_as_float(v[h * 16 + 8 + r8]) * tsc;
+                        if (strip * 8 + r8 < p.N / 2) out[r8] = __float2bfloat16_rn(gte / (1.0f + __expf(-gte)) * up);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int n = nb + j;
+                    if (n >= p.N) break;
+                    const int col = p.row_map ? p.row_map[n] : n;
+                    const float val = __uint_as_float(v[j]) * tsc;
+                    const int64_t o = static_cast<int64_t>(row) * p.ldy + col;
+                    if constexpr (EPI == kEpiF32) reinterpret_cast<float *>(p.y)[o] = val;
+                    else reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(val);
+                }
+            }
+        }
+        if (!acc_ok && lane == 0) atomicOr(p.err, 512);
+    }
+
+    // ---- teardown: every MMA has completed (acc_full) before the tensor memory is freed
+    if (warp == 1) mbar_wait_bounded(acc_full, 0, kWaitNs);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) tmem_dealloc(tmem, kTmemCols);
+}
+
+// One CTA per token row: fp16 copy of the row, scaled by 2^-e when max |x| > 2^15 (tscale = 2^e).
+__global__ void __launch_bounds__(256) x_to_f16_kernel(const uint16_t *x, int64_t ldx, int K, uint16_t *xh,
+                                                       float *tscale) {
+    __shared__ float red[8];
+    const int row = blockIdx.x;
+    const uint16_t *src = x + static_cast<int64_t>(row) * ldx;
+    uint16_t *dst = xh + static_cast<int64_t>(row) * K;
+    float mx = 0.f;
+    for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+        const uint4 v = ld_nc_v4(src + k);
+        const uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            mx = fmaxf(mx, fmaxf(fabsf(__uint_as_float(w4[i] << 16)), fabsf(__uint_as_float(w4[i] & 0xffff0000u))));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, red[i]);
+    const float e = mx > 32768.0f ? ceilf(log2f(mx * (1.0f / 32768.0f))) : 0.0f;
+    const float inv = exp2f(-e);
+    for (int k = threadIdx.x * 8; k < K; k += 256 * 8) {
+        const uint4 v = ld_nc_v4(src + k);
+        uint32_t w4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float lo = __uint_as_float(w4[i] << 16) * inv, hi = __uint_as_float(w4[i] & 0xffff0000u) * inv;
+            w4[i] = static_cast<uint32_t>(__half_as_ushort(__float2half_rn(lo))) |
+                    (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(hi))) << 16);
+        }
+        *reinterpret_cast<uint4 *>(dst + k) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+    }
+    if (threadIdx.x == 0) tscale[row] = exp2f(e);
+}
+
+template <int FMT, int EPI>
+cudaError_t launch_t(const CUtensorMap &map, const DqGemmParams &p, cudaStream_t s) {
+    static bool attr = false;
+    if (!attr) {
+        attr = true;
+        cudaFuncSetAttribute(dqgemm_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes());
+    }
+    const dim3 grid((p.N + kTN - 1) / kTN, (p.M + kTM - 1) / kTM);
+    dqgemm_kernel<FMT, EPI><<<grid, kGThreads, smem_bytes(), s>>>(map, p);
+    return cudaGetLastError();
+}
+
+template <int FMT>
+cudaError_t launch_fmt(int epi, const CUtensorMap &map, const DqGemmParams &p, cudaStream_t s) {
+    switch (epi) {
+        case kEpiF32: return launch_t<FMT, kEpiF32>(map, p, s);
+        case kEpiBF16: return launch_t<FMT, kEpiBF16>(map, p, s);
+        case kEpiSwiGLU: return launch_t<FMT, kEpiSwiGLU>(map, p, s);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }
+    return fn;
+}
+
+}  // namespace
+
+int dqgemm_tile_tokens() { return kTM; }
+
+cudaError_t x_to_f16_launch(const uint16_t *x, int64_t ldx, int M, int K, uint16_t *xh, float *tscale,
+                            cudaStream_t stream) {
+    if (M <= 0) return cudaSuccess;
+    x_to_f16_kernel<<<M, 256, 0, stream>>>(x, ldx, K, xh, tscale);
+    return cudaGetLastError();
+}
+
+cudaError_t dqgemm_launch(int fmt, int epi, const uint16_t *xh, const DqGemmParams &p, cudaStream_t stream) {
+    auto fn = encode_fn();
+    if (!fn) return cudaErrorNotSupported;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(p.K), static_cast<cuuint64_t>(p.M)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(p.K) * 2};
+    const cuuint32_t box[2] = {kTK, kTM}, estr[2] = {1, 1};
+    if (fn(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<uint16_t *>(xh), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    switch (fmt) {
+        case kFmtQ4NX: return launch_fmt<kFmtQ4NX>(epi, map, p, stream);
+        case kFmtQ4S: return launch_fmt<kFmtQ4S>(epi, map, p, stream);
+        case kFmtQ4F16: return launch_fmt<kFmtQ4F16>(epi, map, p, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace onpu_b200

@@ -138,6 +138,20 @@ struct ChainParams {
     unsigned long long *trace;         // optional: [workers][nops][kChainTrace] global-timer stamps
 };
 
+// Prefill dequant-GEMM (dqgemm.cu): Y[M][N] = X[M][K] . W^T for many tokens.
+struct DqGemmParams {
+    const uint8_t *w;                  // GPU-layout matrix
+    int N, K;                          // logical shape (K a multiple of 32)
+    int row_groups, chunks;            // GPU layout
+    int M;                             // tokens
+    void *y;                           // [M][ldy] fp32 / bf16 (or bf16 [M][N/2] for SwiGLU)
+    int64_t ldy;
+    const int *row_map;                // optional: GPU row -> output column (fp32/bf16 epilogues)
+    const float *tscale;               // [M] per-token scale of the fp16 activation copy
+    int *err;
+    uint32_t unpk[3];                  // 0x000F000F, 0x00F000F0, 0x64006400
+};
+
 constexpr int kChainRing = 4;          // links whose split-row partials may be outstanding at once
 // trace stamps per (CTA, link): consumer start, dependency met, activations staged, math done,
 // link counted; producer first copy issued, last copy issued; then the nanoseconds consumer

@@ -45,6 +45,14 @@ int chain_ctas_per_sm(int fmt, int ntiles, int smem);        // 0: does not fit
 int64_t chain_part_floats_per_slot();
 cudaError_t chain_launch(int fmt, int ntiles, const ChainParams &p, int smem, cudaStream_t stream);
 
+// ---- prefill dequant-GEMM (dqgemm.cu): tcgen05 tensor cores, fp16 operands, fp32 accumulators
+// x (bf16 [M][ldx]) -> xh (fp16 [M][K], scaled per token when |x| > 2^15) and tscale[M]
+cudaError_t x_to_f16_launch(const uint16_t *x, int64_t ldx, int M, int K, uint16_t *xh, float *tscale,
+                            cudaStream_t stream);
+// Y = Xh . W^T with the dequantised weights; grid of 128-token x 256-row tiles
+cudaError_t dqgemm_launch(int fmt, int epi, const uint16_t *xh, const DqGemmParams &p, cudaStream_t stream);
+int dqgemm_tile_tokens();
+
 // ---- layout conversion (repack.cu)
 // Where the codes of the matrix come from.
 enum RepackSource : int {

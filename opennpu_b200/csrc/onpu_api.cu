@@ -111,6 +111,10 @@ struct Ctx {
     float *d_db = nullptr;
     int64_t db_cap = 0;
     std::vector<GemvJob> h_jobs;
+    uint16_t *d_xh = nullptr;           // prefill GEMM: fp16 copy of the activations
+    int64_t xh_cap = 0;
+    float *d_ts = nullptr;              // and their per-token scales
+    int64_t ts_cap = 0;
     int64_t calls = 0;
     double wait_s = 0;
 };
@@ -913,6 +917,58 @@ int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
     if (!js) return -1;
     return run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
                     static_cast<cudaStream_t>(stream), pdl_enabled());
+}
+
+int onpu_dense_mm_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    if (rows <= 0) return 0;
+    if (rows > (int64_t{1} << 30)) {
+        set_err("onpu_dense_mm_dev: %lld rows is too many", static_cast<long long>(rows));
+        return -1;
+    }
+    if (epi < kEpiF32 || epi > kEpiSwiGLU || (epi == kEpiSwiGLU && !d->gateup)) {
+        set_err("onpu_dense_mm_dev: bad epilogue %d for this matrix", epi);
+        return -1;
+    }
+    if (d->geo.ok && d->geo.K != d->mat.gm.K) {
+        set_err("onpu_dense_mm_dev: K must be a multiple of 32");
+        return -1;
+    }
+    const int64_t K = d->mat.gm.K, N = d->mat.gm.N;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < K) {
+        set_err("onpu_dense_mm_dev: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+        return -1;
+    }
+    if (ldy < (epi == kEpiSwiGLU ? N / 2 : N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
+        set_err("onpu_dense_mm_dev: y row stride %lld is shorter than the output row", static_cast<long long>(ldy));
+        return -1;
+    }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!grow(c.d_xh, c.xh_cap, rows * K) || !grow(c.d_ts, c.ts_cap, rows)) return -1;
+    auto s = static_cast<cudaStream_t>(stream);
+    ONPU_CUDA(x_to_f16_launch(static_cast<const uint16_t *>(x), ldx, static_cast<int>(rows), static_cast<int>(K), c.d_xh,
+                              c.d_ts, s),
+              -1);
+    DqGemmParams p{};
+    p.w = d->mat.d_w;
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.row_groups = d->mat.gm.row_groups;
+    p.chunks = d->mat.gm.chunks;
+    p.M = static_cast<int>(rows);
+    p.y = y;
+    p.ldy = ldy;
+    p.row_map = epi == kEpiSwiGLU ? nullptr : d->mat.d_row_map;
+    p.tscale = c.d_ts;
+    p.err = c.d_err;
+    p.unpk[0] = 0x000F000Fu;
+    p.unpk[1] = 0x00F000F0u;
+    p.unpk[2] = 0x64006400u;
+    ONPU_CUDA(dqgemm_launch(d->mat.gm.fmt, epi, c.d_xh, p, s), -1);
+    ++c.calls;
+    return 0;
 }
 
 int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream) {

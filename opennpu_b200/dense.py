@@ -99,6 +99,19 @@ class DenseMatrix:
         L.check(rc, "onpu_dense_mv_dev")
         return out
 
+    def mm(self, x, out=None, epi=EPI_F32, stream=None):
+        """Many tokens (prefill) on the tensor cores: like ``mv`` for any number of rows, with the
+        weights dequantised to fp16."""
+        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+        M = x.shape[0]
+        if out is None:
+            ncol = self.N // 2 if epi == EPI_SWIGLU else self.N
+            out = torch.empty(M, ncol, device=x.device, dtype=torch.float32 if epi == EPI_F32 else torch.bfloat16)
+        rc = L.load().onpu_dense_mm_dev(self.h, x.data_ptr(), x.stride(0), M, out.data_ptr(), out.stride(0), epi,
+                                        _stream_ptr(stream))
+        L.check(rc, "onpu_dense_mm_dev")
+        return out
+
     def unpack(self):
         """GPU layout -> (codes uint8 [N, Kg], scale bits int16 [N, Kg/32], min bits or None), in GPU
         row order (a gate/up matrix is interleaved per 16 rows); Kg = K rounded up to 32."""

@@ -59,6 +59,7 @@ SIGNATURES = {
     "onpu_dense_prepare": (I32, [P, I64]),
     "onpu_dense_mv_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),
+    "onpu_dense_mm_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
     "onpu_chain_new": (P, []),
     "onpu_chain_add": (I32, [P, P, P, I64, I64, P, I64, I32, I32]),
