@@ -154,6 +154,186 @@ class DecodeStack:
             raise RuntimeError(err)
 
 
+# Qwen3-14B: prefill dequant-GEMMs
+P_HIDDEN, P_INTER = 5120, 17408
+
+
+class PrefillStack:
+    """Qwen3-14B MLP projections for M prefill tokens on the tensor cores (gate_up with
+    the SwiGLU epilogue, then down), `layers` layers of synthetic int4 weights."""
+
+    def __init__(self, M, seed, layers=2):
+        from opennpu_b200 import dense
+        self.dense = dense
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+        self.layers = []
+        for _ in range(layers):
+            qk, s = gen_int4_cuda(2 * P_INTER, P_HIDDEN, gen)
+            gu = dense.DenseMatrix.from_int4(qk, s, gateup=True)
+            del qk, s
+            qk, s = gen_int4_cuda(P_HIDDEN, P_INTER, gen)
+            dn = dense.DenseMatrix.from_int4(qk, s)
+            del qk, s
+            self.layers.append((gu, dn))
+        torch.cuda.synchronize()
+        self.M = M
+        self.x = torch.randn(M, P_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+        self.a = torch.empty(M, P_INTER, device="cuda", dtype=torch.bfloat16)
+        self.y = torch.empty(M, P_HIDDEN, device="cuda")
+        self.flops_gu = 2 * M * (2 * P_INTER) * P_HIDDEN
+        self.flops_per_step = layers * (self.flops_gu + 2 * M * P_HIDDEN * P_INTER)
+        self.launches_per_step = 4 * layers            # activation copy + GEMM, per matrix
+
+    def step(self):
+        d = self.dense
+        for gu, dn in self.layers:
+            gu.mm(self.x, out=self.a, epi=d.EPI_SWIGLU)
+            dn.mm(self.a, out=self.y)
+
+    def dominant(self):
+        d = self.dense
+
+        def run():
+            for gu, _ in self.layers:
+                gu.mm(self.x, out=self.a, epi=d.EPI_SWIGLU)
+        return run, self.flops_gu, len(self.layers)
+
+
+def cpu_prefill_sample(M_cpu=128, seconds=10.0, seed=0):
+    """The reference's CPU path on the prefill shapes: dequantise per 32 (w = v * s) then fp32
+    matmul with all host threads, on M_cpu tokens; TFLOP/s."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    mats = []
+    for N, K in ((2 * P_INTER, P_HIDDEN), (P_HIDDEN, P_INTER)):
+        v = torch.randint(-8, 8, (N, K), generator=g, dtype=torch.int8)
+        sc = (torch.randn(N, K // 32, generator=g).abs() * 0.02 + 1e-4).half()
+        mats.append((v, sc))
+    x = torch.randn(M_cpu, P_HIDDEN, generator=g).bfloat16().float()
+    flops, t0, n = 0, time.perf_counter(), 0
+    while True:
+        h = x
+        for (v, sc), act in zip(mats, (True, False)):
+            w = (v.float().view(v.shape[0], -1, 32) * sc.float().unsqueeze(-1)).view(v.shape[0], -1)
+            h = h @ w.T
+            flops += 2 * h.shape[0] * w.shape[0] * w.shape[1]
+            if act:
+                gte, up = h[:, :P_INTER], h[:, P_INTER:]
+                h = gte * torch.sigmoid(gte) * up
+        n += 1
+        if time.perf_counter() - t0 > seconds:
+            break
+    dt = time.perf_counter() - t0
+    return flops / dt / 1e12, torch.get_num_threads(), f"{n} x one Qwen3-14B MLP (gate_up + SwiGLU + down, dequant + fp32 matmul) on {M_cpu} tokens"
+
+
+def run_prefill(args):
+    rank, world, local = dist_setup(args.gpus)
+    _, tflops_peak, peak_kind = peaks()
+    M = args.m if args.m > 1 else 2048
+    work = PrefillStack(M, seed=2000 + rank, layers=2)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(max(args.warmup, 1)):
+            work.step()
+    s.synchronize()
+    from opennpu_b200 import dense
+    dense.check_device()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        work.step()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            graph.replay()
+    s.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(args.steps):
+            graph.replay()
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    dense.check_device()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    tflops = work.flops_per_step * world / (ms_step * 1e-3) / 1e12
+
+    run_dom, dom_flops, dom_n = work.dominant()
+    gdom = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gdom, stream=s):
+        run_dom()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            gdom.replay()
+    reps = 20
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(reps):
+            gdom.replay()
+    d1.record(s)
+    d1.synchronize()
+    dom_us = d0.elapsed_time(d1) * 1e3 / (reps * dom_n)
+    del gdom
+
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(work.x.shape, dtype=torch.bfloat16, pin_memory=True)
+        hx.copy_(work.x)
+        hy = torch.empty(work.y.shape, dtype=torch.float32, pin_memory=True)
+        with torch.cuda.stream(s):
+            for i in range(3 + 10):
+                if i == 3:
+                    t0 = time.perf_counter()
+                work.x.copy_(hx, non_blocking=True)
+                work.step()
+                hy.copy_(work.y, non_blocking=True)
+                s.synchronize()
+        dt = (time.perf_counter() - t0) / 10
+        e2e = {"value": round(work.flops_per_step / dt / 1e12, 2), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 4,
+               "ms_per_step": round(dt * 1e3, 3),
+               "path": "onpu_dense_mm_dev with pinned host input/output copies and a host synchronisation per step"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, sample = cpu_prefill_sample(seconds=args.cpu_seconds)
+        cpu = {"value": round(v, 4), "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        achieved = dom_flops / (dom_us * 1e-6) / 1e12
+        line = {
+            "metric": "int4 prefill dequant-GEMM TFLOP/s (Qwen3-14B MLP, tcgen05)", "value": round(tflops, 2),
+            "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4 weights dequantised to fp16, fp16 x fp16 -> fp32",
+            "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1))",
+            "config": {"workload": "qwen3-14b-prefill-mlp", "M": M, "layers": len(work.layers),
+                       "matrices": "gate_up 34816x5120 + SwiGLU, down 5120x17408",
+                       "parallelism": f"replicas{world}", "l2": "weights larger than L2 (no flush needed)",
+                       "cuda_graph": True},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tflops_peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / tflops_peak, 4), "peak_kind": peak_kind + " (bf16 dense, burst)",
+                         "traffic": None, "kernel": "dqgemm_kernel gate_up 34816x5120 + SwiGLU",
+                         "flops_per_launch": dom_flops, "us_per_launch": round(dom_us, 3)},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": work.launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 class GemvRotation:
     """one 4096x4096 int4 GEMV, M=1; the step rotates over 32 weight copies (302 MB
     > L2) so every launch reads HBM."""
@@ -486,7 +666,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv"])
+    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill"])
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -500,6 +680,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "prefill":
+        run_prefill(args)
     else:
         run_ours(args)
 

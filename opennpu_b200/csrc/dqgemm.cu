@@ -18,7 +18,7 @@
 //  * warp 1: allocates tensor memory; one thread issues tcgen05.mma kind::f16 (M128 N256 K16,
 //    four per stage) from shared-memory descriptors and commits each stage's completion to the
 //    mbarrier that frees the stage.
-//  * warps 2-5: dequantise each raw chunk into the stage's fp16 B tile in the canonical K-major
+//  * warps 2-17: dequantise each raw chunk into the stage's fp16 B tile in the canonical K-major
 //    128-byte-swizzled layout (a lane's 16 bytes of codes are two 8-K runs of two rows: one LOP3,
 //    one f16x2 subtract and one f16x2 multiply per pair of weights, 16-byte stores), then after
 //    the last stage read the accumulator with tcgen05.ld (each warp its 32 lanes) and store.
@@ -44,7 +44,8 @@ constexpr int kOpStages = 3, kRawStages = 4;
 constexpr int kXTile = kTM * kTK * 2;                   // 16 KB fp16 activations
 constexpr int kWTile = kTN * kTK * 2;                   // 32 KB fp16 weights
 constexpr int kRawMax = 4 * 2560;                       // four row groups' chunk (q4nx is largest)
-constexpr int kGThreads = 192;                          // 6 warps
+constexpr int kGThreads = 576;                          // 18 warps
+constexpr int kDqWarps = 16;                            // warps 2..17: dequantise, then the epilogue
 constexpr int kTmemCols = 256;
 constexpr uint64_t kWaitNs = 2000000000ull;
 
@@ -158,17 +159,18 @@ __global__ void __launch_bounds__(kGThreads, 1)
     volatile uint32_t *tmem_slot_p = reinterpret_cast<volatile uint32_t *>(base + (tmem_slot - sb));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kTN, m0 = blockIdx.y * kTM, g0 = n0 / kRowGroup;
+    // raster: the token tile varies fastest, so the CTAs that share a weight tile run together
+    const int m0 = blockIdx.x * kTM, n0 = blockIdx.y * kTN, g0 = n0 / kRowGroup;
     const int nk = p.chunks;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kOpStages; ++s) {
-            mbar_init(op_full + s * 8, 1 + 4);             // producer (with the copy bytes) + 4 dequant warps
+            mbar_init(op_full + s * 8, 1 + kDqWarps);      // producer (with the copy bytes) + the dequant warps
             mbar_init(op_empty + s * 8, 1);                // tcgen05.commit
         }
         for (int r = 0; r < kRawStages; ++r) {
             mbar_init(raw_full + r * 8, 1);
-            mbar_init(raw_empty + r * 8, 4);
+            mbar_init(raw_empty + r * 8, kDqWarps);
         }
         mbar_init(acc_full, 1);
         mbar_init_fence();
@@ -239,9 +241,9 @@ __global__ void __launch_bounds__(kGThreads, 1)
             if (!failed) {
                 const uint32_t rbase = raw + r * kRawMax, wbase = ws + s * kWTile;
                 uint8_t *wtile = base + (wbase - sb);
-#pragma unroll 1
-                for (int b = 0; b < 4; ++b) {
-                    const int blk = dt + b * 128, gg = blk >> 7, st = (blk >> 5) & 3, L = blk & 31;
+#pragma unroll
+                for (int b = 0; b < 512 / (kDqWarps * 32); ++b) {
+                    const int blk = dt + b * kDqWarps * 32, gg = blk >> 7, st = (blk >> 5) & 3, L = blk & 31;
                     if (g0 + gg >= p.row_groups) continue;
                     const int rq = L >> 2, t = L & 3;
                     const uint32_t sbase = rbase + gg * CB + st * SB;
@@ -297,29 +299,70 @@ __global__ void __launch_bounds__(kGThreads, 1)
         if (failed && lane == 0) atomicOr(p.err, 256);
         (void)dw;
 
-        // ---- epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. +31 = tokens of the tile
+        // ---- epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. +31 (tokens of the tile) and
+        // the 64 columns (w - 2) / 4
         const bool acc_ok = mbar_wait_bounded(acc_full, 0, kWaitNs);
         tc_fence_after();
-        const int quarter = warp & 3, row = m0 + quarter * 32 + lane;
+        const int quarter = warp & 3, part = (warp - 2) >> 2, row = m0 + quarter * 32 + lane;
         const float tsc = row < p.M ? p.tscale[row] : 0.f;
         const bool do_store = acc_ok && row < p.M;
-        for (int c = 0; c < kTN / 32; ++c) {
+        // 16-byte stores need a 16-byte aligned output and a row stride of 16 bytes
+        constexpr int kOutBytes = EPI == kEpiF32 ? 4 : 2;
+        const bool vec_ok = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && (p.ldy * kOutBytes) % 16 == 0;
+        for (int c = part * (kTN / 32 / (kDqWarps / 4)); c < (part + 1) * (kTN / 32 / (kDqWarps / 4)); ++c) {
             uint32_t v[32];
             __syncwarp();                                  // tcgen05.ld is warp-collective
             tc_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, v);
             if (!do_store) continue;
             const int nb = n0 + c * 32;
             if constexpr (EPI == kEpiSwiGLU) {
-                // columns are GPU rows: strip rows 0-7 gate, 8-15 up of output 8 * strip + r
+                // columns are GPU rows: strip rows 0-7 gate, 8-15 up of output 8 * strip + r; a full
+                // strip's 8 outputs go out as one 16-byte store when the row allows it
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                     const int strip = (nb >> 4) + h;
                     if (strip * 16 >= p.N) continue;
                     __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(row) * p.ldy + strip * 8;
+                    uint32_t pk[4];
 #pragma unroll
-                    for (int r8 = 0; r8 < 8; ++r8) {
-                        const float gte = __uint_as_float(v[h * 16 + r8]) * tsc, up = __uint_as_float(v[h * 16 + 8 + r8]) * tsc;
-                        if (strip * 8 + r8 < p.N / 2) out[r8] = __float2bfloat16_rn(gte / (1.0f + __expf(-gte)) * up);
+                    for (int r8 = 0; r8 < 8; r8 += 2) {
+                        float o2[2];
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const float gte = __uint_as_float(v[h * 16 + r8 + e]) * tsc;
+                            const float up = __uint_as_float(v[h * 16 + 8 + r8 + e]) * tsc;
+                            o2[e] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
+                        }
+                        pk[r8 / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(o2[0]))) |
+                                     (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(o2[1]))) << 16);
+                    }
+                    if (vec_ok && strip * 8 + 8 <= p.N / 2) {
+                        *reinterpret_cast<uint4 *>(out) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    } else {
+#pragma unroll
+                        for (int r8 = 0; r8 < 8; ++r8)
+                            if (strip * 8 + r8 < p.N / 2)
+                                reinterpret_cast<uint16_t *>(out)[r8] = static_cast<uint16_t>(pk[r8 / 2] >> (16 * (r8 & 1)));
+                    }
+                }
+            } else if (vec_ok && !p.row_map && nb + 32 <= p.N) {
+                // 32 consecutive outputs of this token: 16-byte stores
+                if constexpr (EPI == kEpiF32) {
+                    float4 *out = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.y) + static_cast<int64_t>(row) * p.ldy + nb);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        out[j] = make_float4(__uint_as_float(v[4 * j]) * tsc, __uint_as_float(v[4 * j + 1]) * tsc,
+                                             __uint_as_float(v[4 * j + 2]) * tsc, __uint_as_float(v[4 * j + 3]) * tsc);
+                } else {
+                    uint4 *out = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(row) * p.ldy + nb);
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        uint32_t pk[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            pk[e] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[8 * j + 2 * e]) * tsc))) |
+                                    (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[8 * j + 2 * e + 1]) * tsc))) << 16);
+                        out[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     }
                 }
             } else {
@@ -390,7 +433,7 @@ cudaError_t launch_t(const CUtensorMap &map, const DqGemmParams &p, cudaStream_t
         attr = true;
         cudaFuncSetAttribute(dqgemm_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes());
     }
-    const dim3 grid((p.N + kTN - 1) / kTN, (p.M + kTM - 1) / kTM);
+    const dim3 grid((p.M + kTM - 1) / kTM, (p.N + kTN - 1) / kTN);
     dqgemm_kernel<FMT, EPI><<<grid, kGThreads, smem_bytes(), s>>>(map, p);
     return cudaGetLastError();
 }
