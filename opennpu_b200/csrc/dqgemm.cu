@@ -10,18 +10,20 @@
 // the epilogue): both tensor-core operands must have one type, and bf16 weights would round
 // 8x coarser.
 //
-// One CTA computes a 128 (tokens) x 256 (weight rows) tile; the fp32 accumulator lives in tensor
-// memory (256 columns). Warp roles:
+// Persistent CTAs (one per SM) walk 256 (tokens) x 128 (weight rows) tiles; the fp32 accumulators
+// of a tile (two 128-token halves sharing each dequantised weight tile) live in tensor memory,
+// double-buffered so that one tile's epilogue overlaps the next tile's main loop. Warp roles:
 //  * warp 0: one thread issues the copies: the fp16 activation tile of each 64-K stage through a
-//    128-byte-swizzled tensor map (TMA, no multicast), and the int4 chunks of the tile's four row
+//    128-byte-swizzled tensor map (TMA, no multicast), and the int4 chunks of the tile's two row
 //    groups as 1-D bulk copies into a raw ring.
-//  * warp 1: allocates tensor memory; one thread issues tcgen05.mma kind::f16 (M128 N256 K16,
-//    four per stage) from shared-memory descriptors and commits each stage's completion to the
-//    mbarrier that frees the stage.
-//  * warps 2-17: dequantise each raw chunk into the stage's fp16 B tile in the canonical K-major
+//  * warp 1: allocates tensor memory; one thread issues tcgen05.mma kind::f16 (M128 N128 K16,
+//    eight per stage: two token halves x four K steps) from shared-memory descriptors and commits
+//    each stage's completion to the mbarrier that frees the stage.
+//  * warps 2-9: dequantise each raw chunk into the stage's fp16 B tile in the canonical K-major
 //    128-byte-swizzled layout (a lane's 16 bytes of codes are two 8-K runs of two rows: one LOP3,
-//    one f16x2 subtract and one f16x2 multiply per pair of weights, 16-byte stores), then after
-//    the last stage read the accumulator with tcgen05.ld (each warp its 32 lanes) and store.
+//    one f16x2 subtract and one f16x2 multiply per pair of weights, 16-byte stores).
+//  * warps 10-13: read a finished tile's accumulators with tcgen05.ld (each warp its 32 lanes),
+//    apply the epilogue and store, then hand the buffer back to warp 1.
 // Every wait is bounded (2 s of global time) and reports through the error word.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -39,19 +41,21 @@ namespace onpu_b200 {
 
 namespace {
 
-constexpr int kTM = 128, kTN = 256, kTK = 64;           // CTA tile: tokens, weight rows, K per stage
-constexpr int kOpStages = 3, kRawStages = 4;
-constexpr int kXTile = kTM * kTK * 2;                   // 16 KB fp16 activations
-constexpr int kWTile = kTN * kTK * 2;                   // 32 KB fp16 weights
-constexpr int kRawMax = 4 * 2560;                       // four row groups' chunk (q4nx is largest)
-constexpr int kGThreads = 576;                          // 18 warps
-constexpr int kDqWarps = 16;                            // warps 2..17: dequantise, then the epilogue
-constexpr int kTmemCols = 256;
+constexpr int kTM = 256, kTN = 128, kTK = 64;           // CTA tile: tokens, weight rows, K per stage
+constexpr int kMmaM = 128;                              // one MMA: 128 tokens x kTN rows x 16 K
+constexpr int kOpStages = 4, kRawStages = 4;
+constexpr int kXTile = kTM * kTK * 2;                   // 32 KB fp16 activations (256 rows of 128 B)
+constexpr int kWTile = kTN * kTK * 2;                   // 16 KB fp16 weights
+constexpr int kRawMax = 2 * 2560;                       // two row groups' chunk (q4nx is largest)
+constexpr int kDqWarps = 8, kEpiWarps = 4;              // warps 2..9 dequantise, 10..13 store
+constexpr int kGThreads = (2 + kDqWarps + kEpiWarps) * 32;
+constexpr int kAccCols = 2 * kTN;                       // one tile's accumulators: 2 x 128 tokens
+constexpr int kTmemCols = 2 * kAccCols;                 // double-buffered: 512 columns (all of it)
 constexpr uint64_t kWaitNs = 2000000000ull;
 
 constexpr int smem_bytes() {
     return 1024 /* alignment slack */ + kOpStages * (kXTile + kWTile) + kRawStages * kRawMax +
-           (2 * kOpStages + 2 * kRawStages + 1) * 8 + 16;
+           (2 * kOpStages + 2 * kRawStages + 4) * 8 + 16;
 }
 
 // ---------------------------------------------------------------- tcgen05 / TMA
@@ -109,7 +113,7 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
 
 // Instruction descriptor for kind::f16: fp32 accumulator, fp16 A and B, both K-major, N and M.
 constexpr uint32_t kIdesc = (1u << 4) | (0u << 7) | (0u << 10) | (static_cast<uint32_t>(kTN >> 3) << 17) |
-                            (static_cast<uint32_t>(kTM >> 4) << 24);
+                            (static_cast<uint32_t>(kMmaM >> 4) << 24);
 
 // byte offset of 16-byte chunk c (0..7, 8 fp16 along K) of row n in a K-major 128-byte-swizzled tile
 __device__ __forceinline__ uint32_t swz(int n, int c) {
@@ -144,6 +148,78 @@ __device__ __forceinline__ uint32_t to_f16_bits(uint32_t v16) {
     return static_cast<uint32_t>(__half_as_ushort(__float2half_rn(__uint_as_float(v16 << 16))));
 }
 
+// The epilogue of one accumulator chunk: 32 outputs (columns nb..nb+31) of token `row`.
+template <int EPI>
+__device__ __forceinline__ void store_chunk(const DqGemmParams &p, int row, int nb, float tsc, bool vec_ok,
+                                            const uint32_t (&v)[32]) {
+    if constexpr (EPI == kEpiSwiGLU) {
+        // columns are GPU rows: strip rows 0-7 gate, 8-15 up of output 8 * strip + r; a full
+        // strip's 8 outputs go out as one 16-byte store when the row allows it
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int strip = (nb >> 4) + h;
+            if (strip * 16 >= p.N) continue;
+            __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(row) * p.ldy + strip * 8;
+            uint32_t pk[4];
+#pragma unroll
+            for (int r8 = 0; r8 < 8; r8 += 2) {
+                float o2[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    const float gte = __uint_as_float(v[h * 16 + r8 + e]) * tsc;
+                    const float up = __uint_as_float(v[h * 16 + 8 + r8 + e]) * tsc;
+                    o2[e] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
+                }
+                pk[r8 / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(o2[0]))) |
+                             (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(o2[1]))) << 16);
+            }
+            if (vec_ok && strip * 8 + 8 <= p.N / 2) {
+                *reinterpret_cast<uint4 *>(out) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            } else {
+#pragma unroll
+                for (int r8 = 0; r8 < 8; ++r8)
+                    if (strip * 8 + r8 < p.N / 2)
+                        reinterpret_cast<uint16_t *>(out)[r8] = static_cast<uint16_t>(pk[r8 / 2] >> (16 * (r8 & 1)));
+            }
+        }
+    } else if (vec_ok && !p.row_map && nb + 32 <= p.N) {
+        // 32 consecutive outputs of this token: 16-byte stores
+        if constexpr (EPI == kEpiF32) {
+            float4 *out = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.y) + static_cast<int64_t>(row) * p.ldy + nb);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                out[j] = make_float4(__uint_as_float(v[4 * j]) * tsc, __uint_as_float(v[4 * j + 1]) * tsc,
+                                     __uint_as_float(v[4 * j + 2]) * tsc, __uint_as_float(v[4 * j + 3]) * tsc);
+        } else {
+            uint4 *out = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(row) * p.ldy + nb);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t pk[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    pk[e] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[8 * j + 2 * e]) * tsc))) |
+                            (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[8 * j + 2 * e + 1]) * tsc))) << 16);
+                out[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const int n = nb + j;
+            if (n >= p.N) break;
+            const int col = p.row_map ? p.row_map[n] : n;
+            const float val = __uint_as_float(v[j]) * tsc;
+            const int64_t o = static_cast<int64_t>(row) * p.ldy + col;
+            if constexpr (EPI == kEpiF32) reinterpret_cast<float *>(p.y)[o] = val;
+            else reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(val);
+        }
+    }
+}
+
+// Persistent: CTA c takes tiles c, c + gridDim.x, ... (tokens fastest, so the CTAs running at one
+// time share weight tiles through L2); every role walks the same tile sequence and the stage rings
+// run on across tiles. Tensor memory holds two tiles' accumulators, so the epilogue warps drain
+// one tile while the next one accumulates.
 template <int FMT, int EPI>
 __global__ void __launch_bounds__(kGThreads, 1)
     dqgemm_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ DqGemmParams p) {
@@ -154,13 +230,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const uint32_t xs = sb, ws = xs + kOpStages * kXTile, raw = ws + kOpStages * kWTile;
     const uint32_t bars = raw + kRawStages * kRawMax;
     const uint32_t op_full = bars, op_empty = op_full + kOpStages * 8, raw_full = op_empty + kOpStages * 8,
-                   raw_empty = raw_full + kRawStages * 8, acc_full = raw_empty + kRawStages * 8;
-    const uint32_t tmem_slot = acc_full + 8;
+                   raw_empty = raw_full + kRawStages * 8, acc_full = raw_empty + kRawStages * 8,
+                   acc_empty = acc_full + 2 * 8;
+    const uint32_t tmem_slot = acc_empty + 2 * 8;
     volatile uint32_t *tmem_slot_p = reinterpret_cast<volatile uint32_t *>(base + (tmem_slot - sb));
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // raster: the token tile varies fastest, so the CTAs that share a weight tile run together
-    const int m0 = blockIdx.x * kTM, n0 = blockIdx.y * kTN, g0 = n0 / kRowGroup;
+    const int mtiles = (p.M + kTM - 1) / kTM, ntiles = (p.N + kTN - 1) / kTN, tiles = mtiles * ntiles;
     const int nk = p.chunks;
 
     if (threadIdx.x == 0) {
@@ -172,7 +248,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
             mbar_init(raw_full + r * 8, 1);
             mbar_init(raw_empty + r * 8, kDqWarps);
         }
-        mbar_init(acc_full, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + b * 8, 1);                // tcgen05.commit after a tile's last MMA
+            mbar_init(acc_empty + b * 8, kEpiWarps);       // the epilogue warps have read the buffer
+        }
         mbar_init_fence();
     }
     if (warp == 1) {
@@ -183,75 +262,90 @@ __global__ void __launch_bounds__(kGThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot_p;
-    bool failed = false;
 
     if (warp == 0) {
         // ============================================================ copies
         if (lane == 0) {
-            int nvalid = 0;
-            for (int gg = 0; gg < 4; ++gg) nvalid += g0 + gg < p.row_groups;
-            for (int kt = 0; kt < nk && !failed; ++kt) {
-                const int r = kt % kRawStages, rr = kt / kRawStages;
-                if (rr > 0 && !mbar_wait_bounded(raw_empty + r * 8, (rr - 1) & 1, kWaitNs)) {
-                    failed = true;
-                    break;
+            bool failed = false;
+            int stage = 0;
+            for (int t = blockIdx.x; t < tiles && !failed; t += gridDim.x) {
+                const int m0 = (t % mtiles) * kTM, g0 = (t / mtiles) * (kTN / kRowGroup);
+                const int nvalid = (g0 < p.row_groups) + (g0 + 1 < p.row_groups);
+                for (int kt = 0; kt < nk; ++kt, ++stage) {
+                    const int r = stage % kRawStages, rr = stage / kRawStages;
+                    if (rr > 0 && !mbar_wait_bounded(raw_empty + r * 8, (rr - 1) & 1, kWaitNs)) {
+                        failed = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(raw_full + r * 8, static_cast<uint32_t>(nvalid * CB));
+                    for (int gg = 0; gg < 2; ++gg)
+                        if (g0 + gg < p.row_groups)
+                            bulk_g2s(raw + r * kRawMax + gg * CB,
+                                     p.w + (static_cast<int64_t>(g0 + gg) * p.chunks + kt) * CB, CB, raw_full + r * 8);
+                    const int s = stage % kOpStages, sr = stage / kOpStages;
+                    if (sr > 0 && !mbar_wait_bounded(op_empty + s * 8, (sr - 1) & 1, kWaitNs)) {
+                        failed = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(op_full + s * 8, kXTile);
+                    tma_load_2d(xs + s * kXTile, &tmap_x, kt * kTK, m0, op_full + s * 8);
                 }
-                mbar_arrive_expect_tx(raw_full + r * 8, static_cast<uint32_t>(nvalid * CB));
-                for (int gg = 0; gg < 4; ++gg)
-                    if (g0 + gg < p.row_groups)
-                        bulk_g2s(raw + r * kRawMax + gg * CB,
-                                 p.w + (static_cast<int64_t>(g0 + gg) * p.chunks + kt) * CB, CB, raw_full + r * 8);
-                const int s = kt % kOpStages, sr = kt / kOpStages;
-                if (sr > 0 && !mbar_wait_bounded(op_empty + s * 8, (sr - 1) & 1, kWaitNs)) {
-                    failed = true;
-                    break;
-                }
-                mbar_arrive_expect_tx(op_full + s * 8, kXTile);
-                tma_load_2d(xs + s * kXTile, &tmap_x, kt * kTK, m0, op_full + s * 8);
             }
             if (failed) atomicOr(p.err, 64);
         }
     } else if (warp == 1) {
         // ============================================================ tensor-core issue
         if (lane == 0) {
-            for (int kt = 0; kt < nk; ++kt) {
-                const int s = kt % kOpStages, sr = kt / kOpStages;
-                if (!mbar_wait_bounded(op_full + s * 8, sr & 1, kWaitNs)) {
-                    atomicOr(p.err, 128);
-                    break;
-                }
+            bool failed = false;
+            int stage = 0, li = 0;
+            for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++li) {
+                const int b = li & 1, use = li >> 1;
+                if (!failed && use > 0 && !mbar_wait_bounded(acc_empty + b * 8, (use - 1) & 1, kWaitNs)) failed = true;
                 tc_fence_after();
+                const uint32_t d0 = tmem + b * kAccCols, d1 = d0 + kTN;
+                for (int kt = 0; kt < nk; ++kt, ++stage) {
+                    const int s = stage % kOpStages, sr = stage / kOpStages;
+                    if (!failed && !mbar_wait_bounded(op_full + s * 8, sr & 1, kWaitNs)) failed = true;
+                    tc_fence_after();
+                    if (!failed) {
+                        const uint32_t xa = xs + s * kXTile, wb = ws + s * kWTile;
 #pragma unroll
-                for (int kk = 0; kk < kTK / 16; ++kk)
-                    tc_mma_f16(tmem, sw128_desc(xs + s * kXTile + kk * 32), sw128_desc(ws + s * kWTile + kk * 32), kIdesc,
-                               (kt | kk) != 0 ? 1u : 0u);
-                tc_commit(op_empty + s * 8);
+                        for (int kk = 0; kk < kTK / 16; ++kk) {
+                            const uint64_t bdesc = sw128_desc(wb + kk * 32);
+                            const uint32_t acc = (kt | kk) != 0 ? 1u : 0u;
+                            tc_mma_f16(d0, sw128_desc(xa + kk * 32), bdesc, kIdesc, acc);
+                            tc_mma_f16(d1, sw128_desc(xa + kMmaM * 128 + kk * 32), bdesc, kIdesc, acc);
+                        }
+                    }
+                    tc_commit(op_empty + s * 8);           // also after a failure: keeps the rings moving
+                }
+                tc_commit(acc_full + b * 8);               // arrives once the tile's MMAs have completed
             }
-            tc_commit(acc_full);                           // arrives once every issued MMA has completed
+            if (failed) atomicOr(p.err, 128);
         }
-    } else {
-        // ============================================================ dequantise, then epilogue
-        const int dt = threadIdx.x - 64, dw = warp - 2;
+    } else if (warp < 2 + kDqWarps) {
+        // ============================================================ dequantise
+        const int dt = threadIdx.x - 64;                   // one 16-byte code block per thread and stage
+        const int gg = dt >> 7, st = (dt >> 5) & 3, L = dt & 31, rq = L >> 2, tq = L & 3;
         const uint32_t mlo = p.unpk[0], magic = p.unpk[2];
         const uint32_t c_off = FMT == kFmtQ4NX ? 0x64006400u : 0x64086408u;   // 1024 / 1032 in f16x2
-        for (int kt = 0; kt < nk; ++kt) {
-            const int r = kt % kRawStages, rr = kt / kRawStages, s = kt % kOpStages, sr = kt / kOpStages;
-            if (!failed && !mbar_wait_bounded(raw_full + r * 8, rr & 1, kWaitNs)) failed = true;
-            if (!failed && sr > 0 && !mbar_wait_bounded(op_empty + s * 8, (sr - 1) & 1, kWaitNs)) failed = true;
-            if (!failed) {
-                const uint32_t rbase = raw + r * kRawMax, wbase = ws + s * kWTile;
-                uint8_t *wtile = base + (wbase - sb);
-#pragma unroll
-                for (int b = 0; b < 512 / (kDqWarps * 32); ++b) {
-                    const int blk = dt + b * kDqWarps * 32, gg = blk >> 7, st = (blk >> 5) & 3, L = blk & 31;
-                    if (g0 + gg >= p.row_groups) continue;
-                    const int rq = L >> 2, t = L & 3;
-                    const uint32_t sbase = rbase + gg * CB + st * SB;
+        const int nlo = gg * kRowGroup + st * kStripRows + rq, nhi = nlo + 8;
+        bool failed = false;
+        int stage = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+            const int g0 = (t / mtiles) * (kTN / kRowGroup);
+            const bool valid = g0 + gg < p.row_groups;
+            for (int kt = 0; kt < nk; ++kt, ++stage) {
+                const int r = stage % kRawStages, rr = stage / kRawStages, s = stage % kOpStages, sr = stage / kOpStages;
+                if (!failed && !mbar_wait_bounded(raw_full + r * 8, rr & 1, kWaitNs)) failed = true;
+                if (!failed && sr > 0 && !mbar_wait_bounded(op_empty + s * 8, (sr - 1) & 1, kWaitNs)) failed = true;
+                if (!failed && valid) {
+                    const uint32_t sbase = raw + r * kRawMax + gg * CB + st * SB;
+                    uint8_t *wtile = base + (ws + s * kWTile - sb);
                     const uint4 code = lds_v4(sbase + L * 16);
                     const uint2 sc = lds_v2(sbase + kCodeBytes + rq * 8);
                     uint2 mn = make_uint2(0, 0);
                     if constexpr (FMT == kFmtQ4NX) mn = lds_v2(sbase + kCodeBytes + kScaleBytes + rq * 8);
-                    const int nlo = gg * kRowGroup + st * kStripRows + rq, nhi = nlo + 8;
 #pragma unroll
                     for (int gi = 0; gi < 2; ++gi) {
                         const uint32_t sp = gi ? sc.y : sc.x;
@@ -260,129 +354,77 @@ __global__ void __launch_bounds__(kGThreads, 1)
                         uint32_t mlo2 = 0, mhi2 = 0;
                         if constexpr (FMT == kFmtQ4NX) {
                             const uint32_t mp = gi ? mn.y : mn.x;
-                            const uint32_t a = to_f16_bits<FMT>(mp & 0xffffu), b2 = to_f16_bits<FMT>(mp >> 16);
-                            mlo2 = a | (a << 16);
-                            mhi2 = b2 | (b2 << 16);
+                            const uint32_t ma = to_f16_bits<FMT>(mp & 0xffffu), mb = to_f16_bits<FMT>(mp >> 16);
+                            mlo2 = ma | (ma << 16);
+                            mhi2 = mb | (mb << 16);
                         }
                         uint32_t rlo[4], rhi[4];
 #pragma unroll
                         for (int j = 0; j < 2; ++j) {
                             const uint32_t w = gi ? (j ? code.w : code.z) : (j ? code.y : code.x);
-                            uint32_t a[4];
-                            a[0] = lop3_and_or(w, mlo, magic);
-                            a[1] = lop3_and_or(w >> 4, mlo, magic);
-                            a[2] = lop3_and_or(w >> 8, mlo, magic);
-                            a[3] = lop3_and_or(w >> 12, mlo, magic);
+                            uint32_t a4[4];
+                            a4[0] = lop3_and_or(w, mlo, magic);
+                            a4[1] = lop3_and_or(w >> 4, mlo, magic);
+                            a4[2] = lop3_and_or(w >> 8, mlo, magic);
+                            a4[3] = lop3_and_or(w >> 12, mlo, magic);
 #pragma unroll
                             for (int i = 0; i < 4; ++i) {
-                                const uint32_t q = hsub2(a[i], c_off);          // exact: q - 8 (q4nx: q)
-                                if constexpr (FMT == kFmtQ4NX) a[i] = hfma2(q, (i & 1) ? shi2 : slo2, (i & 1) ? mhi2 : mlo2);
-                                else a[i] = hmul2(q, (i & 1) ? shi2 : slo2);
+                                const uint32_t q = hsub2(a4[i], c_off);         // exact: q - 8 (q4nx: q)
+                                if constexpr (FMT == kFmtQ4NX) a4[i] = hfma2(q, (i & 1) ? shi2 : slo2, (i & 1) ? mhi2 : mlo2);
+                                else a4[i] = hmul2(q, (i & 1) ? shi2 : slo2);
                             }
-                            rlo[2 * j] = a[0];
-                            rlo[2 * j + 1] = a[2];
-                            rhi[2 * j] = a[1];
-                            rhi[2 * j + 1] = a[3];
+                            rlo[2 * j] = a4[0];
+                            rlo[2 * j + 1] = a4[2];
+                            rhi[2 * j] = a4[1];
+                            rhi[2 * j + 1] = a4[3];
                         }
-                        *reinterpret_cast<uint4 *>(wtile + swz(nlo, gi * 4 + t)) = make_uint4(rlo[0], rlo[1], rlo[2], rlo[3]);
-                        *reinterpret_cast<uint4 *>(wtile + swz(nhi, gi * 4 + t)) = make_uint4(rhi[0], rhi[1], rhi[2], rhi[3]);
+                        *reinterpret_cast<uint4 *>(wtile + swz(nlo, gi * 4 + tq)) = make_uint4(rlo[0], rlo[1], rlo[2], rlo[3]);
+                        *reinterpret_cast<uint4 *>(wtile + swz(nhi, gi * 4 + tq)) = make_uint4(rhi[0], rhi[1], rhi[2], rhi[3]);
                     }
+                    fence_proxy_async_smem();              // generic stores -> tensor-core reads
                 }
-                fence_proxy_async_smem();                  // generic stores -> tensor-core reads
-            }
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(op_full + s * 8);
-                mbar_arrive(raw_empty + r * 8);
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(op_full + s * 8);
+                    mbar_arrive(raw_empty + r * 8);
+                }
             }
         }
         if (failed && lane == 0) atomicOr(p.err, 256);
-        (void)dw;
-
-        // ---- epilogue: warp w reads tensor-memory lanes 32 (w % 4) .. +31 (tokens of the tile) and
-        // the 64 columns (w - 2) / 4
-        const bool acc_ok = mbar_wait_bounded(acc_full, 0, kWaitNs);
-        tc_fence_after();
-        const int quarter = warp & 3, part = (warp - 2) >> 2, row = m0 + quarter * 32 + lane;
-        const float tsc = row < p.M ? p.tscale[row] : 0.f;
-        const bool do_store = acc_ok && row < p.M;
-        // 16-byte stores need a 16-byte aligned output and a row stride of 16 bytes
+    } else {
+        // ============================================================ epilogue
+        // warp w reads tensor-memory lanes 32 (w % 4) .. +31 of both accumulators of a tile
+        const int quarter = warp & 3;
         constexpr int kOutBytes = EPI == kEpiF32 ? 4 : 2;
         const bool vec_ok = (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && (p.ldy * kOutBytes) % 16 == 0;
-        for (int c = part * (kTN / 32 / (kDqWarps / 4)); c < (part + 1) * (kTN / 32 / (kDqWarps / 4)); ++c) {
-            uint32_t v[32];
-            __syncwarp();                                  // tcgen05.ld is warp-collective
-            tc_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, v);
-            if (!do_store) continue;
-            const int nb = n0 + c * 32;
-            if constexpr (EPI == kEpiSwiGLU) {
-                // columns are GPU rows: strip rows 0-7 gate, 8-15 up of output 8 * strip + r; a full
-                // strip's 8 outputs go out as one 16-byte store when the row allows it
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int strip = (nb >> 4) + h;
-                    if (strip * 16 >= p.N) continue;
-                    __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(row) * p.ldy + strip * 8;
-                    uint32_t pk[4];
-#pragma unroll
-                    for (int r8 = 0; r8 < 8; r8 += 2) {
-                        float o2[2];
-#pragma unroll
-                        for (int e = 0; e < 2; ++e) {
-                            const float gte = __uint_as_float(v[h * 16 + r8 + e]) * tsc;
-                            const float up = __uint_as_float(v[h * 16 + 8 + r8 + e]) * tsc;
-                            o2[e] = __fdividef(gte, 1.0f + __expf(-gte)) * up;
-                        }
-                        pk[r8 / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(o2[0]))) |
-                                     (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(o2[1]))) << 16);
-                    }
-                    if (vec_ok && strip * 8 + 8 <= p.N / 2) {
-                        *reinterpret_cast<uint4 *>(out) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    } else {
-#pragma unroll
-                        for (int r8 = 0; r8 < 8; ++r8)
-                            if (strip * 8 + r8 < p.N / 2)
-                                reinterpret_cast<uint16_t *>(out)[r8] = static_cast<uint16_t>(pk[r8 / 2] >> (16 * (r8 & 1)));
-                    }
-                }
-            } else if (vec_ok && !p.row_map && nb + 32 <= p.N) {
-                // 32 consecutive outputs of this token: 16-byte stores
-                if constexpr (EPI == kEpiF32) {
-                    float4 *out = reinterpret_cast<float4 *>(reinterpret_cast<float *>(p.y) + static_cast<int64_t>(row) * p.ldy + nb);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        out[j] = make_float4(__uint_as_float(v[4 * j]) * tsc, __uint_as_float(v[4 * j + 1]) * tsc,
-                                             __uint_as_float(v[4 * j + 2]) * tsc, __uint_as_float(v[4 * j + 3]) * tsc);
-                } else {
-                    uint4 *out = reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(row) * p.ldy + nb);
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        uint32_t pk[4];
-#pragma unroll
-                        for (int e = 0; e < 4; ++e)
-                            pk[e] = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[8 * j + 2 * e]) * tsc))) |
-                                    (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[8 * j + 2 * e + 1]) * tsc))) << 16);
-                        out[j] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                    }
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int n = nb + j;
-                    if (n >= p.N) break;
-                    const int col = p.row_map ? p.row_map[n] : n;
-                    const float val = __uint_as_float(v[j]) * tsc;
-                    const int64_t o = static_cast<int64_t>(row) * p.ldy + col;
-                    if constexpr (EPI == kEpiF32) reinterpret_cast<float *>(p.y)[o] = val;
-                    else reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(val);
+        bool failed = false;
+        int li = 0;
+        for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++li) {
+            const int b = li & 1, use = li >> 1;
+            const bool ok = !failed && mbar_wait_bounded(acc_full + b * 8, use & 1, kWaitNs);
+            if (!ok) failed = true;
+            tc_fence_after();
+            const int m0 = (t % mtiles) * kTM, n0 = (t / mtiles) * kTN;
+#pragma unroll 1
+            for (int a = 0; a < 2; ++a) {
+                const int row = m0 + a * kMmaM + quarter * 32 + lane;
+                const float tsc = row < p.M ? p.tscale[row] : 0.f;
+#pragma unroll 1
+                for (int c = 0; c < kTN / 32; ++c) {
+                    uint32_t v[32];
+                    __syncwarp();                          // tcgen05.ld is warp-collective
+                    tc_ld_32x32b_x32(tmem + (static_cast<uint32_t>(quarter * 32) << 16) + b * kAccCols + a * kTN + c * 32, v);
+                    if (ok && row < p.M) store_chunk<EPI>(p, row, n0 + c * 32, tsc, vec_ok, v);
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty + b * 8);
         }
-        if (!acc_ok && lane == 0) atomicOr(p.err, 512);
+        if (failed && lane == 0) atomicOr(p.err, 512);
     }
 
-    // ---- teardown: every MMA has completed (acc_full) before the tensor memory is freed
-    if (warp == 1) mbar_wait_bounded(acc_full, 0, kWaitNs);
+    // ---- teardown: the epilogue has waited for every tile's MMAs, so tensor memory is idle
     tc_fence_before();
     __syncthreads();
     if (warp == 1) tmem_dealloc(tmem, kTmemCols);
@@ -433,8 +475,15 @@ cudaError_t launch_t(const CUtensorMap &map, const DqGemmParams &p, cudaStream_t
         attr = true;
         cudaFuncSetAttribute(dqgemm_kernel<FMT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes());
     }
-    const dim3 grid((p.M + kTM - 1) / kTM, (p.N + kTN - 1) / kTN);
-    dqgemm_kernel<FMT, EPI><<<grid, kGThreads, smem_bytes(), s>>>(map, p);
+    static int nsm = 0;
+    if (!nsm) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        if (nsm <= 0) nsm = 1;
+    }
+    const int tiles = ((p.M + kTM - 1) / kTM) * ((p.N + kTN - 1) / kTN);
+    dqgemm_kernel<FMT, EPI><<<tiles < nsm ? tiles : nsm, kGThreads, smem_bytes(), s>>>(map, p);
     return cudaGetLastError();
 }
 
