@@ -334,6 +334,198 @@ def run_prefill(args):
         torch.distributed.destroy_process_group()
 
 
+M_E, M_K, M_HIDDEN, M_INTER, M_LAYERS = 128, 8, 2048, 768, 48
+
+
+def moe_expert_bytes():
+    """int4 codes + fp16 scales of one expert's gate_up (1536x2048) and down (2048x768)."""
+    return int4_param_bytes(2 * M_INTER, M_HIDDEN), int4_param_bytes(M_HIDDEN, M_INTER)
+
+
+class MoEStack:
+    """Qwen3-30B-A3B MoE layers (router 128 experts top-8 renormalised, experts
+    gate_up 1536x2048 + SwiGLU and down 2048x768 in int4), T tokens. One step = the router and the
+    routed-expert FFN of every layer; each layer has its own weights and its own bf16 N(0,1)
+    input rows, so the routing (and the experts read) differs per layer."""
+
+    def __init__(self, T, seed, layers=M_LAYERS):
+        from opennpu_b200 import moe
+        self.moe = moe
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+        self.T, self.layers = T, []
+        for _ in range(layers):
+            wr = (torch.randn(M_E, M_HIDDEN, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
+            gq = torch.randint(0, 256, (M_E, 2 * M_INTER, M_HIDDEN // 2), dtype=torch.uint8, device="cuda",
+                               generator=gen)
+            gs = ((torch.randn(M_E, 2 * M_INTER, M_HIDDEN // 32, device="cuda", generator=gen) * 0.02).abs()
+                  + 1e-4).half()
+            dq = torch.randint(0, 256, (M_E, M_HIDDEN, M_INTER // 2), dtype=torch.uint8, device="cuda", generator=gen)
+            ds = ((torch.randn(M_E, M_HIDDEN, M_INTER // 32, device="cuda", generator=gen) * 0.02).abs()
+                  + 1e-4).half()
+            ffn = moe.ExpertFFN(gq, gs, dq, ds)
+            del gq, gs, dq, ds
+            self.layers.append((wr, ffn))
+        torch.cuda.synchronize()
+        self.x = torch.randn(layers, T, M_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+        self.ids = torch.empty(layers, T, M_K, dtype=torch.int32, device="cuda")
+        self.w = torch.empty(layers, T, M_K, device="cuda")
+        self.y = torch.empty(layers, T, M_HIDDEN, device="cuda")
+        self.launches_per_step = 5 * layers            # router, job builder, gate_up, down, combine
+        self.lib = __import__("opennpu_b200.libonpu", fromlist=["load"]).load()
+
+    def step(self, stream):
+        sp = stream.cuda_stream
+        for l, (wr, ffn) in enumerate(self.layers):
+            x = self.x[l]
+            rc = self.lib.onpu_route_dev(x.data_ptr(), M_HIDDEN, self.T, wr.data_ptr(), M_E, M_HIDDEN, M_K, 1,
+                                         self.ids[l].data_ptr(), self.w[l].data_ptr(), None, sp)
+            assert rc == 0
+            ffn(x, self.ids[l], self.w[l], out=self.y[l], stream=stream)
+
+    def algorithmic_bytes(self):
+        """Per step: every layer's router weights and input rows, the int4 bytes of the experts its
+        tokens selected (each read once), the ids/weights and the fp32 outputs."""
+        gu, dn = moe_expert_bytes()
+        ids = self.ids.cpu().numpy()
+        b = 0
+        for l in range(len(self.layers)):
+            nexp = len(np.unique(ids[l]))
+            b += nexp * (gu + dn) + M_E * M_HIDDEN * 2 + self.T * M_HIDDEN * (2 + 4) + self.T * M_K * 8
+        return b
+
+
+def cpu_moe_sample(T, seconds=10.0, seed=0):
+    """The reference's CPU MoE layer (opennpu/native/reference.py:71-84): router softmax / top-8 /
+    renormalise, then per selected expert dequantise (v * s) and fp32 matmuls with SwiGLU, all host
+    threads; layer tokens/s."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    wr = (torch.randn(M_E, M_HIDDEN, generator=g) * 0.02).bfloat16().float()
+    gv = torch.randint(-8, 8, (M_E, 2 * M_INTER, M_HIDDEN), dtype=torch.int8, generator=g)
+    gsc = (torch.randn(M_E, 2 * M_INTER, M_HIDDEN // 32, generator=g).abs() * 0.02 + 1e-4).half()
+    dv = torch.randint(-8, 8, (M_E, M_HIDDEN, M_INTER), dtype=torch.int8, generator=g)
+    dsc = (torch.randn(M_E, M_HIDDEN, M_INTER // 32, generator=g).abs() * 0.02 + 1e-4).half()
+
+    def deq(v, s):
+        N, K = v.shape
+        return (v.view(N, K // 32, 32).float() * s.float()[..., None]).view(N, K)
+
+    def layer(x):
+        prob = (x @ wr.T).softmax(-1)
+        w, sel = prob.topk(M_K, -1)
+        w = w / w.sum(-1, keepdim=True)
+        out = torch.zeros_like(x)
+        for e in sel.unique().tolist():
+            rows = (sel == e).any(-1).nonzero().flatten()
+            we = (w * (sel == e)).sum(-1)[rows, None]
+            h = x[rows] @ deq(gv[e], gsc[e]).T
+            a = torch.nn.functional.silu(h[:, :M_INTER]) * h[:, M_INTER:]
+            out[rows] += we * (a @ deq(dv[e], dsc[e]).T)
+        return out
+
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 1:
+        layer(torch.randn(T, M_HIDDEN, generator=g).bfloat16().float())
+        n += 1
+    dt = time.perf_counter() - t0
+    return n * T / dt, torch.get_num_threads(), f"{n} x one Qwen3-30B-A3B MoE layer (router + dequant + fp32 experts) on {T} tokens"
+
+
+def run_moe(args):
+    rank, world, local = dist_setup(args.gpus)
+    hbm, _, peak_kind = peaks()
+    T = args.m if args.m > 0 else 1
+    layers = args.layers if args.layers != LAYERS else M_LAYERS
+    work = MoEStack(T, seed=3000 + rank, layers=layers)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(max(args.warmup, 1)):
+            work.step(s)
+    s.synchronize()
+    from opennpu_b200 import dense
+    dense.check_device()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        work.step(s)
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            graph.replay()
+    s.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(args.steps):
+            graph.replay()
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    dense.check_device()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    layer_us = ms_step * 1e3 / layers
+    tok_s = T * world / (layer_us * 1e-6)
+    nbytes = work.algorithmic_bytes()
+    gbs = nbytes / (ms_step * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(work.x.shape, dtype=torch.bfloat16, pin_memory=True)
+        hx.copy_(work.x)
+        hy = torch.empty(work.y.shape, dtype=torch.float32, pin_memory=True)
+        with torch.cuda.stream(s):
+            for i in range(3 + 10):
+                if i == 3:
+                    t0 = time.perf_counter()
+                work.x.copy_(hx, non_blocking=True)
+                work.step(s)
+                hy.copy_(work.y, non_blocking=True)
+                s.synchronize()
+        dt = (time.perf_counter() - t0) / 10
+        e2e = {"value": round(T / (dt / layers), 1), "unit": "tokens/s",
+               "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 4,
+               "ms_per_step": round(dt * 1e3, 3),
+               "path": "onpu_route_dev + onpu_moe_ffn_dev per layer (no graph), pinned host input/output copies, "
+                       "a host synchronisation per step"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, sample = cpu_moe_sample(T, seconds=args.cpu_seconds)
+        cpu = {"value": round(v, 2), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        line = {
+            "metric": "MoE layer tokens/s (Qwen3-30B-A3B: router + 128-expert top-8 int4 FFN)",
+            "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded random int4 experts, fp16 scales, bf16 N(0,1) tokens, N(0,0.02) router)",
+            "config": {"workload": "qwen3-30b-a3b-moe-layer", "T": T, "layers": layers, "experts": M_E,
+                       "top_k": M_K, "hidden": M_HIDDEN, "expert_inter": M_INTER,
+                       "parallelism": f"replicas{world}", "us_per_layer": round(layer_us, 3),
+                       "l2": "selected experts of all layers per step exceed L2 (no flush needed)",
+                       "cuda_graph": True},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs / hbm, 4), "peak_kind": peak_kind + " (copy bandwidth)",
+                         "traffic": None, "kernel": "whole MoE layer (router, job builder, gate_up + SwiGLU GEMV, "
+                                                    "down GEMV, combine)",
+                         "bytes_per_step": nbytes},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": work.launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 class GemvRotation:
     """one 4096x4096 int4 GEMV, M=1; the step rotates over 32 weight copies (302 MB
     > L2) so every launch reads HBM."""
@@ -666,7 +858,7 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill"])
+    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill", "moe"])
     ap.add_argument("--m", type=int, default=1)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
@@ -682,6 +874,8 @@ def main():
         run_reference(args)
     elif args.config == "prefill":
         run_prefill(args)
+    elif args.config == "moe":
+        run_moe(args)
     else:
         run_ours(args)
 

@@ -140,6 +140,34 @@ int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
 int onpu_dense_mm_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream);
 /* Prepare (allocate descriptors and scratch for) `rows`-row calls without running one. */
 int onpu_dense_prepare(void *h, int64_t rows);
+/* ---- device-resident MoE layer (config 4's routed experts, every buffer on the GPU)
+ * Router: logits = h . Wr^T (bf16 h [T][ldh], bf16 Wr [E][H], fp32 sums), probabilities softmax,
+ * the k largest (descending; equal probabilities: lower expert id first), weights renormalised over
+ * the k when norm != 0. Replaces the reference's CPU router (opennpu/native/reference.py:71-76,
+ * opennpu/native/moe_runtime.py:333-341). ids int32 [T][k], w fp32 [T][k], logits fp32
+ * [T][E] or NULL. 1 <= k <= 16, k <= E <= 256, H % 8 == 0, 16-byte aligned rows. Asynchronous. */
+int onpu_route_dev(const void *h, int64_t ldh, int64_t T, const void *wr, int64_t E, int64_t H, int k, int norm,
+                   int32_t *ids, float *w, float *logits, void *stream);
+/* An expert bank of E [N, K] matrices filled from int4 packed along K (the layout of
+ * onpu_dense_new_int4, experts back to back: qk[E][N][K/2], scales[E][N][K/32]). gateup != 0
+ * stores gate/up rows interleaved for the fused SwiGLU. The int4 counterpart of onpu_bank_new2
+ * (llama/ggml-opennpu/onpu_api.cpp:159-167) for checkpoints that are already group-32 int4. */
+void *onpu_bank_new_int4(int64_t N, int64_t K, int64_t E, int gateup);
+int onpu_bank_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream);
+/* A routed-expert FFN (gate_up [E][Ng][Kg] with Ng = 2 * Kd, down [E][Nd][Kd]) of int4 banks; fill
+ * them with onpu_bank_load_int4 on onpu_ffn_gu / onpu_ffn_dn. The int4 counterpart of onpu_ffn_new
+ * (llama/ggml-opennpu/onpu_api.cpp:292-309). */
+void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t E);
+/* y[t] = sum_j w[t][j] * down_e(silu(gate_e . x_t) * (up_e . x_t)), e = ids[t][j], on the GPU:
+ * x bf16 [T][ldx], ids/w from onpu_route_dev (device), y fp32 [T][ldy]. Four launches on `stream`,
+ * no host synchronisation (capturable in a CUDA graph once a first call has sized the scratch):
+ * the token-sorted expert jobs are built on the device from the ids, then gate_up (fused SwiGLU,
+ * bf16 activations), down and the weighted combine. An id outside [0, E) drops that (token, slot)
+ * pair and sets the device status (onpu_check_device reports it). At most 2048 experts. Replaces
+ * opennpu/native/reference.py:77-84 and the device part of onpu_moe_ffn
+ * (llama/ggml-opennpu/onpu_api.cpp:261-278). 0 ok, < 0 error. */
+int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
+                     float *y, int64_t ldy, void *stream);
 /* ---- GEMV chains: a decode step's dense GEMVs recorded once on fixed device buffers and run as
  * ONE persistent launch (the GPU analogue of the reference's instruction stream per call,
  * llama/ggml-opennpu/opennpu_core.hpp:418-505, and of onpu_ffn_run's gate_up -> act -> down

@@ -76,7 +76,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT), STAGE_W = stage_w_bytes(FMT);
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int W = p.workers, T = p.total_chunks, cta = blockIdx.x;
+    const int W = p.workers, cta = blockIdx.x;
+    int T = p.total_chunks;
+    if (p.njobs_dev) {                                // jobs built on the device by the previous kernel
+        pdl_wait_prerequisites();
+        T = __ldcg(p.njobs_dev) * p.row_groups * p.chunks;
+    }
     const int lo = static_cast<int>(static_cast<int64_t>(cta) * T / W);
     const int hi = static_cast<int>(static_cast<int64_t>(cta + 1) * T / W);
     const int nst = (hi - lo + kCPS - 1) / kCPS;
@@ -258,6 +263,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         // tail segment of the first contributor: collect cf+1 .. cl (bounded wait on their flags)
         if (warp == 0) {
             for (int w2 = cf + 1 + lane; w2 <= cl; w2 += 32) {
+                if (range_empty(w2, W, T)) continue;          // fewer chunks than CTAs: no partials
                 const uint64_t t0 = global_timer_ns();
                 while (ld_acquire_gpu(p.counters + w2) == 0u) {
                     __nanosleep(256);
@@ -279,7 +285,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
                     float v = acc[nt][f];
                     const int e = ((s * 8 + r) * 2 + (f >> 1)) * 16 + tok;
 #pragma unroll 4
-                    for (int w2 = cf + 1; w2 <= cl; ++w2) v += __ldcg(p.part + static_cast<int64_t>(w2) * kSlotFloats + e);
+                    for (int w2 = cf + 1; w2 <= cl; ++w2)
+                        if (!range_empty(w2, W, T)) v += __ldcg(p.part + static_cast<int64_t>(w2) * kSlotFloats + e);
                     acc[nt][f] = v;
                 }
             }

@@ -64,6 +64,11 @@ __device__ __forceinline__ int worker_of(int c, int W, int T) {
     return static_cast<int>((static_cast<int64_t>(c + 1) * W - 1) / T);
 }
 
+// CTA w of W owns chunks [w*T/W, (w+1)*T/W): empty when there are fewer chunks than CTAs
+__device__ __forceinline__ bool range_empty(int w, int W, int T) {
+    return static_cast<int64_t>(w) * T / W == static_cast<int64_t>(w + 1) * T / W;
+}
+
 // One strip (16 rows) x one chunk (2 groups of 32 along K) into acc. wsb: the strip's bytes in
 // shared memory; xa[nt]: shared address of this lane's 8 activations of the chunk's first group
 // for n-tile nt (the second group is 64 B further; absent tokens read zeros).

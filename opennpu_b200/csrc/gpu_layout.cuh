@@ -95,6 +95,8 @@ struct GemvParams {
     unsigned *counters;                // [workers] partial-ready flags, zero between launches
     int *err;                          // set non-zero on a timed-out wait
     int jobs_ready;                    // job list not written by the previous kernel in the stream
+    const int *njobs_dev;              // non-null: the job count lives on the device (written by the
+                                       // previous kernel); njobs / total_chunks are upper bounds
     uint32_t mul[4];                   // 2^28, 2^24, 2^20, 2^16: shift multipliers the compiler cannot fold
     uint32_t unpk[3];                  // 0x000F000F, 0x00F000F0, 0x64006400 (fp16 code unpacking)
     int xslots;                        // per-stage activations: slots per chunk (max tokens + 1 zero slot)

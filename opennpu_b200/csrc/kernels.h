@@ -53,6 +53,30 @@ cudaError_t x_to_f16_launch(const uint16_t *x, int64_t ldx, int M, int K, uint16
 cudaError_t dqgemm_launch(int fmt, int epi, const uint16_t *xh, const DqGemmParams &p, cudaStream_t stream);
 int dqgemm_tile_tokens();
 
+// ---- MoE router (router.cu): softmax(h . Wr^T) -> top-k -> renormalise, one CTA per token
+constexpr int kMaxRouteExperts = 256;
+constexpr int kMaxRouteK = 16;
+constexpr int kMaxJobExperts = 2048;    // expert_jobs_kernel keeps 4 ints per expert in shared memory
+
+// Device-side grouping of routed (token, slot) pairs into the GEMV jobs of two expert banks.
+struct ExpertJobsParams {
+    const int32_t *ids;        // [TK] expert per (token, slot)
+    int64_t TK;                // tokens * k
+    int k, E;
+    const uint8_t *w0;         // bank 0 (gate_up): expert e at w0 + e * bytes0; jobs read token rows
+    int64_t bytes0;
+    const uint8_t *w1;         // bank 1 (down): jobs read per-slot rows
+    int64_t bytes1;
+    GemvJob *jobs0, *jobs1;    // capacity min(E, TK) + TK / 16 each
+    int *njobs;                // out: jobs in each list
+    int *order;                // scratch [TK]
+    int *err;                  // bit 8: an id outside [0, E) (that pair is dropped)
+};
+cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream);
+
+cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16_t *wr, int E, int H, int k, int norm,
+                         int32_t *ids, float *w, float *logits, cudaStream_t stream);
+
 // ---- layout conversion (repack.cu)
 // Where the codes of the matrix come from.
 enum RepackSource : int {

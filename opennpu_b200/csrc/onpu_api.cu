@@ -111,6 +111,10 @@ struct Ctx {
     float *d_db = nullptr;
     int64_t db_cap = 0;
     std::vector<GemvJob> h_jobs;
+    int32_t *d_order = nullptr;         // device MoE layer: slots sorted by expert
+    int64_t order_cap = 0;
+    int *d_njobs = nullptr;             // and the job count of its job lists
+    int64_t njobs_cap = 0;
     uint16_t *d_xh = nullptr;           // prefill GEMM: fp16 copy of the activations
     int64_t xh_cap = 0;
     float *d_ts = nullptr;              // and their per-token scales
@@ -211,8 +215,10 @@ bool ensure_scratch(Ctx &c, int workers, int ntiles, int counters) {
 }
 
 // mmax: the largest token count of any job (the kernel sizes its activation slots by it)
+// d_njobs: the job count is written on the device by the previous kernel (njobs is its bound)
 int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntiles, int mmax, int epi,
-             const uint16_t *x, int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl) {
+             const uint16_t *x, int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl,
+             const int *d_njobs = nullptr) {
     const int T = njobs * m.gm.row_groups * m.gm.chunks;
     if (T == 0) return 0;
     const GemvLayout lay = gemv_layout(m.gm.fmt, njobs, mmax, m.gm.K);
@@ -235,7 +241,8 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     p.part = c.d_part;
     p.counters = c.d_cnt;
     p.err = c.d_err;
-    p.jobs_ready = 1;
+    p.jobs_ready = d_njobs ? 0 : 1;
+    p.njobs_dev = d_njobs;
     p.mul[0] = 1u << 28;
     p.mul[1] = 1u << 24;
     p.mul[2] = 1u << 20;
@@ -279,7 +286,11 @@ int check_device_err(Ctx &c) {
         cudaMemset(c.d_err, 0, sizeof(int));
         if (c.d_cnt) cudaMemset(c.d_cnt, 0, sizeof(unsigned) * c.cnt_cap);
         reset_chains_after_error();
-        set_err("a GEMV kernel timed out waiting for its weight copies (device status %d)", h);
+        if (h & 8)
+            set_err("an expert id was out of range [0, E) in a routed job list; those (token, slot) pairs were "
+                    "dropped (device status %d)", h);
+        else
+            set_err("a GEMV kernel timed out waiting for its weight copies (device status %d)", h);
         return -2;
     }
     return 0;
@@ -453,6 +464,7 @@ BankH *new_bank(int64_t N, int64_t K, int64_t E, int ncols, int sym) {
 }
 
 bool sync_bank(BankH *b) {
+    if (!b->h_buf) return true;   // int4 banks are loaded by onpu_bank_load_int4
     Ctx &c = ctx();
     const int64_t per = b->geo.nbytes;
     const int64_t batch = std::max<int64_t>(1, std::min<int64_t>(b->mat.E, (256LL << 20) / std::max<int64_t>(per, 1)));
@@ -968,6 +980,187 @@ int onpu_dense_mm_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
     p.unpk[2] = 0x64006400u;
     ONPU_CUDA(dqgemm_launch(d->mat.gm.fmt, epi, c.d_xh, p, s), -1);
     ++c.calls;
+    return 0;
+}
+
+int onpu_route_dev(const void *h, int64_t ldh, int64_t T, const void *wr, int64_t E, int64_t H, int k, int norm,
+                   int32_t *ids, float *w, float *logits, void *stream) {
+    clear_err();
+    if (T <= 0) return 0;
+    if (k < 1 || k > 16 || E < k || E > 256) {
+        set_err("onpu_route_dev: need 1 <= k <= 16 and k <= E <= 256 (k %d, E %lld)", k, static_cast<long long>(E));
+        return -1;
+    }
+    if (H <= 0 || H % 8 || ldh < H || ldh % 8 || (reinterpret_cast<uintptr_t>(h) & 15) ||
+        (reinterpret_cast<uintptr_t>(wr) & 15)) {
+        set_err("onpu_route_dev: h and Wr rows must be 16-byte aligned bf16 with H %% 8 == 0 and ldh >= H, ldh %% 8 == 0");
+        return -1;
+    }
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return -1;
+    }
+    ONPU_CUDA(route_launch(static_cast<const uint16_t *>(h), ldh, T, static_cast<const uint16_t *>(wr),
+                           static_cast<int>(E), static_cast<int>(H), k, norm, ids, w, logits,
+                           static_cast<cudaStream_t>(stream)),
+              -1);
+    return 0;
+}
+
+void *onpu_bank_new_int4(int64_t N, int64_t K, int64_t E, int gateup) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    if (N <= 0 || K <= 0 || K % 32 || E <= 0) {
+        set_err("onpu_bank_new_int4: need N > 0, K %% 32 == 0, E > 0");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *b = new BankH;
+    b->fmt = kFmtQ4F16;
+    b->owns_buf = false;
+    b->geo.N = N;                 // no stream-order geometry: the weights arrive as int4 + fp16 scales
+    b->geo.K = K;
+    if (!alloc_mat(b->mat, N, K, kFmtQ4F16, E) || (gateup && !set_gateup_interleave(b->mat))) {
+        if (gateup) set_err("onpu_bank_new_int4: gate/up rows need N %% 2 == 0 and N/2 %% 8 == 0");
+        delete b;
+        return nullptr;
+    }
+    return b;
+}
+
+int onpu_bank_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream) {
+    clear_err();
+    auto *b = static_cast<BankH *>(h);
+    if (b->fmt != kFmtQ4F16 || b->h_buf) {
+        set_err("onpu_bank_load_int4: bank was not created by onpu_bank_new_int4");
+        return -1;
+    }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int64_t N = b->mat.gm.N, K = b->mat.gm.K, E = b->mat.E;
+    const int64_t qb = N * K / 2, sb = N * (K / 32);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    uint8_t *tq = nullptr;
+    uint16_t *ts = nullptr;
+    if (!on_device) {
+        ONPU_CUDA(cudaMalloc(&tq, static_cast<size_t>(qb)), -1);
+        ONPU_CUDA(cudaMalloc(&ts, static_cast<size_t>(sb) * 2), -1);
+    }
+    cudaError_t e = cudaSuccess;
+    for (int64_t x = 0; x < E && e == cudaSuccess; ++x) {
+        const uint8_t *sq = qk + x * qb;
+        const uint16_t *ss = scales + x * sb;
+        if (!on_device) {
+            e = cudaMemcpyAsync(tq, sq, static_cast<size_t>(qb), cudaMemcpyHostToDevice, s);
+            if (e == cudaSuccess) e = cudaMemcpyAsync(ts, ss, static_cast<size_t>(sb) * 2, cudaMemcpyHostToDevice, s);
+            sq = tq;
+            ss = ts;
+        }
+        RepackParams p{};
+        p.src_kind = kSrcInt4K;
+        p.src = sq;
+        p.scales = ss;
+        p.src_row = b->mat.d_row_map;
+        p.N = N;
+        p.K = K;
+        p.fmt = kFmtQ4F16;
+        p.dst = b->mat.d_w + x * b->mat.gm.bytes;
+        if (e == cudaSuccess) e = repack_launch(p, s);
+        if (e == cudaSuccess && !on_device) e = cudaStreamSynchronize(s);   // the staging buffers are reused
+    }
+    if (e == cudaSuccess && (!on_device || !stream)) e = cudaStreamSynchronize(s);
+    if (tq) cudaFree(tq);
+    if (ts) cudaFree(ts);
+    if (e != cudaSuccess) {
+        set_err("onpu_bank_load_int4: %s", cudaGetErrorString(e));
+        return -1;
+    }
+    return 0;
+}
+
+void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t E) {
+    clear_err();
+    if (Kd * 2 != Ng) {
+        set_err("onpu_ffn_new_int4: down K (%lld) must be gate_up N / 2 (%lld)", static_cast<long long>(Kd),
+                static_cast<long long>(Ng / 2));
+        return nullptr;
+    }
+    auto *gu = static_cast<BankH *>(onpu_bank_new_int4(Ng, Kg, E, 1));
+    if (!gu) return nullptr;
+    auto *dn = static_cast<BankH *>(onpu_bank_new_int4(Nd, Kd, E, 0));
+    if (!dn) {
+        delete gu;
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *f = new FfnH;
+    f->gu = gu;
+    f->dn = dn;
+    f->fused = true;
+    return f;
+}
+
+int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
+                     float *y, int64_t ldy, void *stream) {
+    clear_err();
+    auto *f = static_cast<FfnH *>(ffn);
+    if (T <= 0) return 0;
+    if (!f || !f->fused || k < 1) {
+        set_err("onpu_moe_ffn_dev: needs an FFN handle with interleaved gate/up (onpu_ffn_new_int4) and k >= 1");
+        return -1;
+    }
+    BankH *gu = f->gu, *dn = f->dn;
+    const int64_t Kg = gu->mat.gm.K, Kd = dn->mat.gm.K, Nd = dn->mat.gm.N, TK = T * k, E = gu->mat.E;
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < Kg) {
+        set_err("onpu_moe_ffn_dev: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+        return -1;
+    }
+    if (ldy < Nd || (reinterpret_cast<uintptr_t>(y) & 3)) {
+        set_err("onpu_moe_ffn_dev: y row stride %lld is shorter than the output row", static_cast<long long>(ldy));
+        return -1;
+    }
+    if (E > kMaxJobExperts || dn->mat.E != E || TK > (int64_t{1} << 30)) {
+        set_err("onpu_moe_ffn_dev: at most %d experts (the same in both banks) and 2^30 routed slots", kMaxJobExperts);
+        return -1;
+    }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto s = static_cast<cudaStream_t>(stream);
+    // job lists are built on the device from the routed ids: no host round trip, capturable
+    const int64_t njmax = std::min(E, TK) + TK / kMaxTokensPerJob;
+    if (!grow(c.d_jobs, c.jobs_cap, 2 * njmax) || !grow(c.d_order, c.order_cap, TK) ||
+        !grow(c.d_njobs, c.njobs_cap, 1) || !grow(c.d_a, c.a_cap, TK * Kd) || !grow(c.d_o, c.o_cap, TK * Nd))
+        return -1;
+    ExpertJobsParams jp{};
+    jp.ids = ids;
+    jp.TK = TK;
+    jp.k = k;
+    jp.E = static_cast<int>(E);
+    jp.w0 = gu->mat.d_w;
+    jp.bytes0 = gu->mat.gm.bytes;
+    jp.w1 = dn->mat.d_w;
+    jp.bytes1 = dn->mat.gm.bytes;
+    jp.jobs0 = c.d_jobs;
+    jp.jobs1 = c.d_jobs + njmax;
+    jp.njobs = c.d_njobs;
+    jp.order = c.d_order;
+    jp.err = c.d_err;
+    ONPU_CUDA(expert_jobs_launch(jp, s), -1);
+    const int mmax = static_cast<int>(std::min<int64_t>(T, kMaxTokensPerJob)), ntiles = mmax > 8 ? 2 : 1;
+    // an expert sees each token at most once (the k experts of a token are distinct); the down
+    // projection's jobs hold the same slots, so both lists share the bound
+    if (run_gemv(c, gu->mat, jp.jobs0, static_cast<int>(njmax), ntiles, mmax, kEpiSwiGLU,
+                 static_cast<const uint16_t *>(x), ldx, c.d_a, Kd, s, true, c.d_njobs))
+        return -1;
+    if (run_gemv(c, dn->mat, jp.jobs1, static_cast<int>(njmax), ntiles, mmax, kEpiF32, c.d_a, Kd, c.d_o, Nd, s, true,
+                 c.d_njobs))
+        return -1;
+    ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, ids, w, nullptr, y, ldy, s), -1);
     return 0;
 }
 

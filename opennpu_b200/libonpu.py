@@ -61,6 +61,11 @@ SIGNATURES = {
     "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mm_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
+    "onpu_route_dev": (I32, [P, I64, I64, P, I64, I64, I32, I32, P, P, P, P]),
+    "onpu_bank_new_int4": (P, [I64, I64, I64, I32]),
+    "onpu_bank_load_int4": (I32, [P, P, P, I32, P]),
+    "onpu_ffn_new_int4": (P, [I64, I64, I64, I64, I64]),
+    "onpu_moe_ffn_dev": (I32, [P, P, I64, I64, P, P, I32, P, I64, P]),
     "onpu_chain_new": (P, []),
     "onpu_chain_add": (I32, [P, P, P, I64, I64, P, I64, I32, I32]),
     "onpu_chain_info": (I32, [P, I64P]),
