@@ -196,12 +196,22 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     int seg = lo;
     int m = p.jobs[j].m;
 
+    const int mslots = p.xslots - 1;                  // rows the activation region is laid out for
+    // resident activations: fp16 rows, a zero block, the offset table, token scales; staged
+    // again (after every consumer is done with them) when the range enters the next job
+    auto row_of = [](const GemvJob *jb) { return [jb](int n) { return jb->xrow[n]; }; };
     if (xres) {
-        // resident activations: fp16 rows, a zero block, the offset table, token scales
         const GemvJob *jb = p.jobs + j;
-        stage_activations<FMT, NT, false>(p.x, p.ldx, [jb](int n) { return jb->xrow[n]; }, m, p.K, p.xstride,
-                                smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
+        stage_activations<FMT, NT, false>(p.x, p.ldx, row_of(jb), jb->m, mslots, p.K, p.xstride,
+                                          smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
     }
+    // inside the chunk loop: fewer loads in flight per thread, so the loop keeps its registers
+    auto restage = [&](int jj) {
+        const GemvJob *jb = p.jobs + jj;
+        stage_activations<FMT, NT, false, decltype(row_of(jb)), 1>(p.x, p.ldx, row_of(jb), jb->m, mslots, p.K,
+                                                                   p.xstride, smem + kNS * STAGE_W, threadIdx.x,
+                                                                   kConsumers * 32);
+    };
     const float *tscale = reinterpret_cast<const float *>(smem + kNS * STAGE_W + p.ctab_off +
                                                           p.chunks * tab_chunk_bytes(NT));
 
@@ -213,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         for (int nt = 0; nt < NT; ++nt) {
             const int tok = nt * 8 + r;
             if (xres) {
-                xrb[nt] = xregion + (tok < m ? tok * p.xstride : m * p.xstride) + t * 16;
+                xrb[nt] = xregion + (tok < m ? tok * p.xstride : mslots * p.xstride) + t * 16;
                 xkm[nt] = tok < m ? 128u : 0u;        // absent tokens stay on the zero block
             } else {
                 xrb[nt] = xregion + (tok < m ? tok : p.xslots - 1) * kXSlot + t * 16;
@@ -310,7 +320,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
             if (++g == p.row_groups) {
                 g = 0;
                 ++j;
-                if (c + 1 < hi) load_rows();
+                if (c + 1 < hi) {
+                    if (xres) {
+                        named_bar_sync(1, kConsumers * 32);       // every warp is done with job j - 1
+                        restage(j);
+                    }
+                    load_rows();
+                }
             }
         }
     };
@@ -433,7 +449,8 @@ GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K) {
     GemvLayout L{};
     const int64_t xstride = xres_stride(K);
     const int64_t res_bytes = xres_bytes(mmax, K, mmax > 8 ? 2 : 1, xstride);   // rows, zero block, table, scales
-    L.xres = njobs == 1 && res_bytes <= kResidentXBudget;
+    L.xres = res_bytes <= kResidentXBudget;       // several jobs: staged again per job
+    (void)njobs;
     L.xstride = static_cast<int>(xstride);
     L.ctab_off = static_cast<int>(mmax * xstride + 128);
     L.xslots = mmax + 1;
@@ -441,6 +458,10 @@ GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K) {
     L.off_bar = static_cast<int>(kNS * stage_w_bytes(fmt) + (xbytes + 15) / 16 * 16);
     L.smem = L.off_bar + 2 * kNS * 8 + 16;
     return L;
+}
+
+bool gemv_resident(int mmax, int64_t K) {
+    return xres_bytes(mmax, K, mmax > 8 ? 2 : 1, xres_stride(K)) <= kResidentXBudget;
 }
 
 int gemv_ctas_per_sm(int fmt, int ntiles, int smem) {

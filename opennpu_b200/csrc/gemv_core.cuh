@@ -156,14 +156,16 @@ __device__ __forceinline__ void strip_chunk(uint32_t wsb, const uint32_t (&xa)[N
 }
 
 // ================================================================ fp16 path (resident activations)
-// The resident kernels feed the tensor cores fp16: A = 1024 + q for strip rows r (mask 0x000F000F)
+// The resident kernels feed the tensor cores fp16: 1024 + q for strip rows r (mask 0x000F000F)
 // and 1024 + 16 q for rows r+8 (mask 0x00F000F0), one three-register LOP3 each from the packed
-// word or the word >> 8 (fp16's 10-bit mantissa holds both nibbles of a byte), 5 instructions per
-// 8 codes. Rows r+8 carry a factor 16, removed exactly at the end of a segment (finish_rows). The
-// activations are staged as fp16 (scaled per token by a power of two when |x| would leave the
-// fp16 range); the MMA starts from c * sum(x) per 32-group and token (sums from a table):
-// symmetric c = -1032 (rows r) and -1152 (rows r+8, = -(1024 + 16 * 8)); q4nx c = -1024 both.
-// Products (1024 + 16 q) * x are exact in fp32; the weights are never rounded.
+// word or the word >> 8 (fp16's 10-bit mantissa holds both nibbles of a byte), then one HSUB2
+// removes the bias exactly (symmetric: 1032 and 1152 = 1024 + 16 * 8; q4nx: 1024), 9
+// instructions per 8 codes. Rows r+8 carry a factor 16, removed exactly at the end of a segment
+// (finish_rows). The activations are staged as fp16 (scaled per token by a power of two when |x|
+// would leave the fp16 range). Products (q - 8) * x are exact in fp32 and the MMA accumulates
+// sums of the size of the result (subtracting the bias after the MMA instead, from a table of
+// group sums, cancels ~1000x larger partial sums and costs ~10 bits of the fp32 accumulator);
+// q4nx adds m * sum(x) from the table of group sums. The weights are never rounded.
 struct Unpack {
     uint32_t mlo, mhi, magic;      // 0x000F000F, 0x00F000F0, 0x64006400 (kernel parameters: kept in registers)
 };
@@ -174,12 +176,24 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
     return d;
 }
 
+__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// 8 codes -> the A registers as exact centred fp16 values: rows r hold q - 8 (q for q4nx), rows
+// r+8 hold 16 (q - 8) (16 q): one LOP3 gives 1024 + q (1024 + 16 q), one HSUB2 removes the bias
+// exactly, so the MMA sums products of small integers and activations (no large offset to cancel)
+template <int FMT>
 __device__ __forceinline__ void codes_to_a_h(uint32_t w, const Unpack &u, uint32_t (&a)[4]) {
+    constexpr uint32_t off_lo = FMT == kFmtQ4NX ? 0x64006400u : 0x64086408u;   // 1024 | 1032
+    constexpr uint32_t off_hi = FMT == kFmtQ4NX ? 0x64006400u : 0x64806480u;   // 1024 | 1152
     const uint32_t s = w >> 8;
-    a[0] = lop3_and_or(w, u.mlo, u.magic);
-    a[1] = lop3_and_or(w, u.mhi, u.magic);
-    a[2] = lop3_and_or(s, u.mlo, u.magic);
-    a[3] = lop3_and_or(s, u.mhi, u.magic);
+    a[0] = hsub2_bits(lop3_and_or(w, u.mlo, u.magic), off_lo);
+    a[1] = hsub2_bits(lop3_and_or(w, u.mhi, u.magic), off_hi);
+    a[2] = hsub2_bits(lop3_and_or(s, u.mlo, u.magic), off_lo);
+    a[3] = hsub2_bits(lop3_and_or(s, u.mhi, u.magic), off_hi);
 }
 
 __device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -212,16 +226,19 @@ __device__ __forceinline__ void strip_chunk_h(uint32_t wsb, const uint32_t (&xa)
 #pragma unroll
     for (int gi = 0; gi < 2; ++gi) {
         uint32_t a0[4], a1[4];
-        codes_to_a_h(gi ? code.z : code.x, u, a0);
-        codes_to_a_h(gi ? code.w : code.y, u, a1);
+        codes_to_a_h<FMT>(gi ? code.z : code.x, u, a0);
+        codes_to_a_h<FMT>(gi ? code.w : code.y, u, a1);
         float s_lo, s_hi;
         decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
-        constexpr float c_lo = FMT == kFmtQ4NX ? -1024.0f : -1032.0f, c_hi = FMT == kFmtQ4NX ? -1024.0f : -1152.0f;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
-            const float x0 = __uint_as_float(c2.x), x1 = __uint_as_float(c2.y);
-            float d[4] = {c_lo * x0, c_lo * x1, c_hi * x0, c_hi * x1};
+            float x0 = 0.f, x1 = 0.f;
+            if constexpr (FMT == kFmtQ4NX) {
+                const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
+                x0 = __uint_as_float(c2.x);
+                x1 = __uint_as_float(c2.y);
+            }
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
             mma16816_f16(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
             mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
             acc[nt][0] = fmaf(s_lo, d[0], acc[nt][0]);
@@ -242,14 +259,13 @@ __device__ __forceinline__ void strip_chunk_h(uint32_t wsb, const uint32_t (&xa)
     }
 }
 
-// One whole chunk (all 4 strips) by one warp, fp16 path: the activations, the offset constants and
-// their table entries are read once per chunk and shared by the strips. wcb: the chunk in shared
+// One whole chunk (all 4 strips) by one warp, fp16 path: the activations (and for q4nx their
+// group sums) are read once per chunk and shared by the strips. wcb: the chunk in shared
 // memory; xa/ca as in strip_chunk_h; acc[strip][n-tile][4].
 template <int FMT, int NT>
 __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], uint32_t ca, int lane, int r,
                                         const uint32_t (&mul)[4], const Unpack &u, float (&acc)[4][NT][4]) {
     constexpr int SB = strip_bytes(FMT);
-    constexpr float c_lo = FMT == kFmtQ4NX ? -1024.0f : -1032.0f, c_hi = FMT == kFmtQ4NX ? -1024.0f : -1152.0f;
     uint32_t bx[2][NT][4];
     float xs[2][NT][2];
 #pragma unroll
@@ -258,9 +274,12 @@ __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], 
         for (int nt = 0; nt < NT; ++nt) {
             const uint4 v = lds_v4(xa[nt] + gi * 64);
             bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
-            const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
-            xs[gi][nt][0] = __uint_as_float(c2.x);
-            xs[gi][nt][1] = __uint_as_float(c2.y);
+            xs[gi][nt][0] = xs[gi][nt][1] = 0.f;
+            if constexpr (FMT == kFmtQ4NX) {          // the min term needs the group sums
+                const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
+                xs[gi][nt][0] = __uint_as_float(c2.x);
+                xs[gi][nt][1] = __uint_as_float(c2.y);
+            }
         }
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
@@ -271,8 +290,8 @@ __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], 
 #pragma unroll
         for (int gi = 0; gi < 2; ++gi) {
             uint32_t a0[4], a1[4];
-            codes_to_a_h(gi ? code.z : code.x, u, a0);
-            codes_to_a_h(gi ? code.w : code.y, u, a1);
+            codes_to_a_h<FMT>(gi ? code.z : code.x, u, a0);
+            codes_to_a_h<FMT>(gi ? code.w : code.y, u, a1);
             float s_lo, s_hi;
             decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
             float m_lo = 0.f, m_hi = 0.f;
@@ -283,7 +302,7 @@ __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], 
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const float x0 = xs[gi][nt][0], x1 = xs[gi][nt][1];
-                float d[4] = {c_lo * x0, c_lo * x1, c_hi * x0, c_hi * x1};
+                float d[4] = {0.f, 0.f, 0.f, 0.f};
                 mma16816_f16(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
                 mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
                 acc[s][nt][0] = fmaf(s_lo, d[0], acc[s][nt][0]);
@@ -334,18 +353,19 @@ __device__ __forceinline__ float group_to_f16(uint4 (&v)[4], float inv, uint32_t
 }
 
 // Stage m activation rows as fp16 + the offset table, by the nthr consumer threads (every one
-// must call this; named barrier 1 synchronises them). Row n is x + row_of(n) * ldx (bf16,
+// must call this; named barrier 1 synchronises them). The region is laid out for mslots >= m
+// rows: rows, a 128-B zero block at mslots * xstride, the table, the token scales. Row n is x + row_of(n) * ldx (bf16,
 // 16-byte aligned). CG: load through L2 only (rows written earlier in the same launch).
 // One pass: the (token, 32-group) items are spread evenly over the threads, each thread issues
-// all its loads (up to kSU groups) before converting, stores fp16 and writes the group's sum.
+// the loads of kSU groups before converting, stores fp16 and writes the group's sum.
 // A token whose |x| exceeds 2^15 is redone scaled by 2^-e (rare) and tscale[n] = 2^e.
-template <int FMT, int NT, bool CG, typename RowOf>
-__device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, int m, int K, int xstride, uint8_t *xs, int tid,
-                        int nthr) {
-    constexpr int MT = 8 * NT, kSU = 4;
+template <int FMT, int NT, bool CG, typename RowOf, int kSU = 4>
+__device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, int m, int mslots, int K, int xstride,
+                                  uint8_t *xs, int tid, int nthr) {
+    constexpr int MT = 8 * NT;
     const int chunks = (K + kChunkK - 1) / kChunkK, G = K / 32;
-    float *tab = reinterpret_cast<float *>(xs + m * xstride + 128);
-    float *tscale = reinterpret_cast<float *>(xs + m * xstride + 128 + chunks * tab_chunk_bytes(NT));
+    float *tab = reinterpret_cast<float *>(xs + mslots * xstride + 128);
+    float *tscale = reinterpret_cast<float *>(xs + mslots * xstride + 128 + chunks * tab_chunk_bytes(NT));
     unsigned *tmax = reinterpret_cast<unsigned *>(tscale + 16);
     auto tab_at = [&](int grp, int tok) -> float & {
         return tab[((grp * NT + tok / 8) * 4 + (tok % 8) / 2) * 2 + (tok & 1)];
@@ -356,7 +376,7 @@ __device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, 
         const int n = e / tail16, q = e - n * tail16;
         *reinterpret_cast<uint4 *>(xs + n * xstride + rowb + q * 16) = make_uint4(0, 0, 0, 0);
     }
-    if (tid < 8) *reinterpret_cast<uint4 *>(xs + m * xstride + tid * 16) = make_uint4(0, 0, 0, 0);
+    if (tid < 8) *reinterpret_cast<uint4 *>(xs + mslots * xstride + tid * 16) = make_uint4(0, 0, 0, 0);
     for (int e = tid; e < chunks * 2 * MT; e += nthr) {
         const int tok = e % MT, grp = e / MT;
         if (tok >= m || grp >= G) tab_at(grp, tok) = 0.f;

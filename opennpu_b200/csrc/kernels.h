@@ -22,6 +22,8 @@ struct GemvLayout {
     int smem;          // dynamic shared memory per CTA
 };
 GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K);
+// true when jobs of up to mmax tokens keep their activations resident (fp16 path) for this K
+bool gemv_resident(int mmax, int64_t K);
 int gemv_ctas_per_sm(int fmt, int ntiles, int smem);
 int gemv_chunks_per_stage();
 int64_t gemv_part_floats_per_worker(int ntiles);
@@ -63,19 +65,23 @@ struct ExpertJobsParams {
     const int32_t *ids;        // [TK] expert per (token, slot)
     int64_t TK;                // tokens * k
     int k, E;
+    int per_job;               // tokens per job at most (1..16)
     const uint8_t *w0;         // bank 0 (gate_up): expert e at w0 + e * bytes0; jobs read token rows
     int64_t bytes0;
     const uint8_t *w1;         // bank 1 (down): jobs read per-slot rows
     int64_t bytes1;
-    GemvJob *jobs0, *jobs1;    // capacity min(E, TK) + TK / 16 each
+    GemvJob *jobs0, *jobs1;    // capacity min(E, TK) + TK / per_job each
     int *njobs;                // out: jobs in each list
     int *order;                // scratch [TK]
     int *err;                  // bit 8: an id outside [0, E) (that pair is dropped)
 };
 cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream);
 
+// logits: fp32 [T][E] (output or scratch); counters: route_counter_slots(T) words, zero before the
+// first launch and left zero by every launch
 cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16_t *wr, int E, int H, int k, int norm,
-                         int32_t *ids, float *w, float *logits, cudaStream_t stream);
+                         int32_t *ids, float *w, float *logits, unsigned *counters, cudaStream_t stream);
+int64_t route_counter_slots(int64_t T);
 
 // ---- layout conversion (repack.cu)
 // Where the codes of the matrix come from.

@@ -111,6 +111,10 @@ struct Ctx {
     float *d_db = nullptr;
     int64_t db_cap = 0;
     std::vector<GemvJob> h_jobs;
+    unsigned *d_rcnt = nullptr;         // router: per-token-block arrival counters (kept zero)
+    int64_t rcnt_cap = 0;
+    float *d_rlg = nullptr;             // router: logits scratch when the caller wants none
+    int64_t rlg_cap = 0;
     int32_t *d_order = nullptr;         // device MoE layer: slots sorted by expert
     int64_t order_cap = 0;
     int *d_njobs = nullptr;             // and the job count of its job lists
@@ -1001,9 +1005,12 @@ int onpu_route_dev(const void *h, int64_t ldh, int64_t T, const void *wr, int64_
         set_err("no usable CUDA device");
         return -1;
     }
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!grow(c.d_rcnt, c.rcnt_cap, route_counter_slots(T), true) || (!logits && !grow(c.d_rlg, c.rlg_cap, T * E)))
+        return -1;
     ONPU_CUDA(route_launch(static_cast<const uint16_t *>(h), ldh, T, static_cast<const uint16_t *>(wr),
-                           static_cast<int>(E), static_cast<int>(H), k, norm, ids, w, logits,
-                           static_cast<cudaStream_t>(stream)),
+                           static_cast<int>(E), static_cast<int>(H), k, norm, ids, w, logits ? logits : c.d_rlg,
+                           c.d_rcnt, static_cast<cudaStream_t>(stream)),
               -1);
     return 0;
 }
@@ -1132,7 +1139,10 @@ int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     std::lock_guard<std::mutex> lk(g_mu);
     auto s = static_cast<cudaStream_t>(stream);
     // job lists are built on the device from the routed ids: no host round trip, capturable
-    const int64_t njmax = std::min(E, TK) + TK / kMaxTokensPerJob;
+    // jobs of 8 tokens when 16 would not keep their activations resident (fp16 path, one staging
+    // per job instead of a copy per token and chunk)
+    const int per_job = gemv_resident(16, std::max(Kg, Kd)) || !gemv_resident(8, std::max(Kg, Kd)) ? 16 : 8;
+    const int64_t njmax = std::min(E, TK) + TK / per_job;
     if (!grow(c.d_jobs, c.jobs_cap, 2 * njmax) || !grow(c.d_order, c.order_cap, TK) ||
         !grow(c.d_njobs, c.njobs_cap, 1) || !grow(c.d_a, c.a_cap, TK * Kd) || !grow(c.d_o, c.o_cap, TK * Nd))
         return -1;
@@ -1141,6 +1151,7 @@ int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     jp.TK = TK;
     jp.k = k;
     jp.E = static_cast<int>(E);
+    jp.per_job = per_job;
     jp.w0 = gu->mat.d_w;
     jp.bytes0 = gu->mat.gm.bytes;
     jp.w1 = dn->mat.d_w;
@@ -1151,7 +1162,7 @@ int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     jp.order = c.d_order;
     jp.err = c.d_err;
     ONPU_CUDA(expert_jobs_launch(jp, s), -1);
-    const int mmax = static_cast<int>(std::min<int64_t>(T, kMaxTokensPerJob)), ntiles = mmax > 8 ? 2 : 1;
+    const int mmax = static_cast<int>(std::min<int64_t>(T, per_job)), ntiles = mmax > 8 ? 2 : 1;
     // an expert sees each token at most once (the k experts of a token are distinct); the down
     // projection's jobs hold the same slots, so both lists share the bound
     if (run_gemv(c, gu->mat, jp.jobs0, static_cast<int>(njmax), ntiles, mmax, kEpiSwiGLU,

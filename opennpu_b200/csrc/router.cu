@@ -4,10 +4,10 @@
 // opennpu/native/moe_runtime.py:333-341): probabilities softmax(h Wr^T), the k largest in descending order (on
 // equal probabilities the lower expert id first, as a stable argsort of -p), weights renormalised
 // over the k when norm_topk_prob is set. bf16 h and Wr, fp32 logits (sums of exact products).
-// One CTA per token: eight warps compute the E logits (one dot product per warp and expert,
-// 16-byte loads, a warp reduction), warp 0 does the softmax and the top-k by k rounds of a warp
-// argmax. Renormalising divides by the selected sum, so the softmax denominator cancels; without
-// renormalisation it is kept.
+// The logits are spread over a grid of 8-expert x 8-token CTAs (a 1-token call reads the router
+// matrix with E/8 CTAs instead of one); the last CTA of each token block does the softmax and the
+// top-k by k rounds of a warp argmax. Renormalising divides by the selected sum, so the softmax
+// denominator cancels; without renormalisation it is kept.
 #include <cuda_runtime.h>
 
 #include <cfloat>
@@ -21,62 +21,102 @@ namespace onpu_b200 {
 namespace {
 
 constexpr int kRouterThreads = 256;
+constexpr int kRouteExperts = 8;     // experts per CTA: one per warp
+constexpr int kRouteTokens = 8;      // tokens per CTA
 
 __device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 
-__global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h, int64_t ldh, const uint16_t *wr, int E,
-                                                               int H, int k, int norm, int32_t *ids, float *w,
-                                                               float *logits) {
-    extern __shared__ float sm[];                    // [E] logits, then [E] exp(logit - max)
-    float *lg = sm, *ex = sm + E;
-    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint16_t *hr = h + static_cast<int64_t>(t) * ldh;
-    for (int e = warp; e < E; e += kRouterThreads / 32) {
+__device__ __forceinline__ float dot8(const uint4 a, const uint4 b, float acc) {
+    acc = fmaf(bf16_lo(a.x), bf16_lo(b.x), acc);
+    acc = fmaf(bf16_hi(a.x), bf16_hi(b.x), acc);
+    acc = fmaf(bf16_lo(a.y), bf16_lo(b.y), acc);
+    acc = fmaf(bf16_hi(a.y), bf16_hi(b.y), acc);
+    acc = fmaf(bf16_lo(a.z), bf16_lo(b.z), acc);
+    acc = fmaf(bf16_hi(a.z), bf16_hi(b.z), acc);
+    acc = fmaf(bf16_lo(a.w), bf16_lo(b.w), acc);
+    return fmaf(bf16_hi(a.w), bf16_hi(b.w), acc);
+}
+
+// Grid (experts / 8, tokens / 8). Warp w computes the logits of expert 8*bx + w for the CTA's 8
+// tokens (the expert row is loaded once per 8 tokens; every load of a lane's K slices is
+// independent, so the whole row is in flight at once). The last CTA of a token block to finish
+// (counter per token block, reset by that CTA) runs the softmax and top-k of its 8 tokens, one
+// warp per token, with the E probabilities in registers (E <= 256: 8 per lane).
+__global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h, int64_t ldh, int64_t T,
+                                                               const uint16_t *wr, int E, int H, int k, int norm,
+                                                               int32_t *ids, float *w, float *lg, unsigned *counters) {
+    __shared__ int last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRouteTokens;
+    const int nt = T - t0 < kRouteTokens ? static_cast<int>(T - t0) : kRouteTokens;
+    const int e = blockIdx.x * kRouteExperts + warp;
+    if (e < E) {
         const uint16_t *wrow = wr + static_cast<int64_t>(e) * H;
-        float acc = 0.f;
+        float acc[kRouteTokens];
+#pragma unroll
+        for (int n = 0; n < kRouteTokens; ++n) acc[n] = 0.f;
+#pragma unroll 4
         for (int d = lane * 8; d < H; d += 32 * 8) {
-            const uint4 a = ld_nc_v4(hr + d), b = ld_nc_v4(wrow + d);
-            acc = fmaf(bf16_lo(a.x), bf16_lo(b.x), acc);
-            acc = fmaf(bf16_hi(a.x), bf16_hi(b.x), acc);
-            acc = fmaf(bf16_lo(a.y), bf16_lo(b.y), acc);
-            acc = fmaf(bf16_hi(a.y), bf16_hi(b.y), acc);
-            acc = fmaf(bf16_lo(a.z), bf16_lo(b.z), acc);
-            acc = fmaf(bf16_hi(a.z), bf16_hi(b.z), acc);
-            acc = fmaf(bf16_lo(a.w), bf16_lo(b.w), acc);
-            acc = fmaf(bf16_hi(a.w), bf16_hi(b.w), acc);
+            const uint4 b = ld_nc_v4(wrow + d);
+            uint4 a[kRouteTokens];
+#pragma unroll
+            for (int n = 0; n < kRouteTokens; ++n)
+                a[n] = n < nt ? ld_nc_v4(h + (t0 + n) * ldh + d) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int n = 0; n < kRouteTokens; ++n) acc[n] = dot8(a[n], b, acc[n]);
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) lg[e] = acc;
+        for (int n = 0; n < kRouteTokens; ++n) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], o);
+        }
+        if (lane < nt) {
+            float v = acc[0];
+#pragma unroll
+            for (int n = 1; n < kRouteTokens; ++n)
+                if (lane == n) v = acc[n];
+            lg[(t0 + lane) * E + e] = v;
+        }
     }
+    __threadfence();
     __syncthreads();
-    if (warp != 0) return;
+    if (threadIdx.x == 0) last = atomicAdd(counters + blockIdx.y, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x == 0) counters[blockIdx.y] = 0u;          // ready for the next launch
+    if (warp >= nt) return;
+    const int64_t t = t0 + warp;
+    const float *row = lg + t * E;
+    float v[kMaxRouteExperts / 32];
     float mx = -FLT_MAX;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, lg[e]);
+#pragma unroll
+    for (int i = 0; i < kMaxRouteExperts / 32; ++i) {
+        const int x = lane + 32 * i;
+        v[i] = x < E ? __ldcg(row + x) : -FLT_MAX;
+        mx = fmaxf(mx, v[i]);
+    }
 #pragma unroll
     for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
     float total = 0.f;
-    for (int e = lane; e < E; e += 32) {
-        const float v = __expf(lg[e] - mx);
-        ex[e] = v;
-        total += v;
-        if (logits) logits[static_cast<int64_t>(t) * E + e] = lg[e];
+#pragma unroll
+    for (int i = 0; i < kMaxRouteExperts / 32; ++i) {
+        v[i] = lane + 32 * i < E ? __expf(v[i] - mx) : -3.f;   // probabilities up to the common factor
+        total += fmaxf(v[i], 0.f);
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) total += __shfl_xor_sync(0xffffffffu, total, o);
-    __syncwarp();
-    float sel_sum = 0.f, mine = 0.f;                 // lane j keeps the j-th selected value
-    for (int j = 0; j < k; ++j) {
-        float bv = -1.f;
+    float sel_sum = 0.f, mine = 0.f;                          // lane j keeps the j-th selected value
+    for (int j = 0; j < k; ++j) {                             // absent -3 < taken -2 < start < any p >= 0
+        float bv = -1.5f;
         int bi = 0x7fffffff;
-        for (int e = lane; e < E; e += 32) {
-            const float v = ex[e];
-            if (v > bv || (v == bv && e < bi)) {
-                bv = v;
-                bi = e;
+#pragma unroll
+        for (int i = 0; i < kMaxRouteExperts / 32; ++i)
+            if (v[i] > bv) {                                  // ascending ids: ties keep the lower one
+                bv = v[i];
+                bi = lane + 32 * i;
             }
-        }
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
             const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -86,16 +126,17 @@ __global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h
                 bi = oi;
             }
         }
-        if (lane == 0) {
-            ids[static_cast<int64_t>(t) * k + j] = bi;
-            ex[bi] = -2.f;                           // taken
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int i = 0; i < kMaxRouteExperts / 32; ++i)
+                if (lane + 32 * i == bi) v[i] = -2.f;         // taken
         }
+        if (lane == 0) ids[t * k + j] = bi;
         if (lane == j) mine = bv;
         sel_sum += bv;
-        __syncwarp();
     }
     const float denom = norm ? sel_sum : total;
-    if (lane < k) w[static_cast<int64_t>(t) * k + lane] = mine / denom;
+    if (lane < k) w[t * k + lane] = mine / denom;
 }
 
 constexpr int kJobThreads = 1024;
@@ -128,8 +169,8 @@ __device__ int block_exclusive_scan(int v, int &total, int *warp_sums) {
     return r;
 }
 
-// Routed (token, slot) pairs grouped by expert into GEMV jobs of <= 16 tokens, on the device: the
-// grouping of the host builder (ascending expert id, slots in arrival order), so the whole MoE
+// Routed (token, slot) pairs grouped by expert into GEMV jobs of <= per_job tokens, on the device:
+// the grouping of the host builder (ascending expert id, slots in arrival order), so the whole MoE
 // layer runs without a host round trip. One CTA. jobs0 read token rows (slot / k) against bank 0
 // (gate_up), jobs1 read the per-slot activation rows against bank 1 (down); both write per slot.
 __global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJobsParams p) {
@@ -152,7 +193,7 @@ __global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJo
     int base_s = 0, base_j = 0;
     for (int e0 = 0; e0 < p.E; e0 += kJobThreads) {
         const int e = e0 + tid;
-        const int c = e < p.E ? cnt[e] : 0, nj = (c + kMaxTokensPerJob - 1) / kMaxTokensPerJob;
+        const int c = e < p.E ? cnt[e] : 0, nj = (c + p.per_job - 1) / p.per_job;
         int ts, tj;
         const int xs = block_exclusive_scan(c, ts, warp_sums);
         const int xj = block_exclusive_scan(nj, tj, warp_sums);
@@ -193,19 +234,17 @@ __global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJo
             if (jstart[mid] <= jb) lo = mid;
             else hi = mid;
         }
-        const int e = lo, part = jb - jstart[e], a = start[e] + part * kMaxTokensPerJob;
-        const int m = min(kMaxTokensPerJob, cnt[e] - part * kMaxTokensPerJob);
-        GemvJob j0{}, j1{};
-        j0.w = p.w0 + static_cast<int64_t>(e) * p.bytes0;
-        j1.w = p.w1 + static_cast<int64_t>(e) * p.bytes1;
-        j0.m = j1.m = m;
-        for (int n = 0; n < m; ++n) {
-            const int slot = p.order[a + n];
-            j0.xrow[n] = slot / p.k;
-            j0.yrow[n] = j1.xrow[n] = j1.yrow[n] = slot;
+        const int e = lo, part = jb - jstart[e], a = start[e] + part * p.per_job;
+        const int m = min(p.per_job, cnt[e] - part * p.per_job);
+        GemvJob *j0 = p.jobs0 + jb, *j1 = p.jobs1 + jb;
+        j0->w = p.w0 + static_cast<int64_t>(e) * p.bytes0;
+        j1->w = p.w1 + static_cast<int64_t>(e) * p.bytes1;
+        j0->m = j1->m = m;
+        for (int n = 0; n < kMaxTokensPerJob; ++n) {
+            const int slot = n < m ? p.order[a + n] : 0;
+            j0->xrow[n] = slot / p.k;
+            j0->yrow[n] = j1->xrow[n] = j1->yrow[n] = slot;
         }
-        p.jobs0[jb] = j0;
-        p.jobs1[jb] = j1;
     }
     if (tid == 0) *p.njobs = NJ;
 }
@@ -220,11 +259,13 @@ cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream) {
 }
 
 cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16_t *wr, int E, int H, int k, int norm,
-                         int32_t *ids, float *w, float *logits, cudaStream_t stream) {
+                         int32_t *ids, float *w, float *logits, unsigned *counters, cudaStream_t stream) {
     if (T <= 0) return cudaSuccess;
-    route_kernel<<<static_cast<unsigned>(T), kRouterThreads, 2 * E * sizeof(float), stream>>>(h, ldh, wr, E, H, k, norm,
-                                                                                              ids, w, logits);
+    const dim3 grid((E + kRouteExperts - 1) / kRouteExperts, static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens));
+    route_kernel<<<grid, kRouterThreads, 0, stream>>>(h, ldh, T, wr, E, H, k, norm, ids, w, logits, counters);
     return cudaGetLastError();
 }
+
+int64_t route_counter_slots(int64_t T) { return (T + kRouteTokens - 1) / kRouteTokens; }
 
 }  // namespace onpu_b200
