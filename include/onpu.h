@@ -195,6 +195,12 @@ int onpu_chain_run(void *chain, void *stream);
  * during the link. NULL turns it off. CTAs from onpu_chain_info. */
 int onpu_chain_trace(void *chain, uint64_t *stamps);
 void onpu_chain_free(void *chain);
+/* Tracing of the GEMV kernels (dense and expert launches through this library): later launches
+ * with at most `ctas` CTAs write 8 %globaltimer values per CTA to the device buffer `stamps`
+ * [ctas][8]: entry, producer's first copy issued, consumers past griddepcontrol.wait, activations
+ * staged, first weights arrived, last stage consumed, range flushed, then the nanoseconds the
+ * consumers waited for weights. Each launch overwrites the same slots. NULL turns it off. */
+int onpu_gemv_trace(uint64_t *stamps, int64_t ctas);
 
 /* onpu_dense_mv_dev with no allocation in the call: no reference counterpart (the NPU library
  * has no device scratch). Same arguments and result as onpu_dense_mv_dev, but the split-row

@@ -77,6 +77,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int W = p.workers, cta = blockIdx.x;
+    unsigned long long *trace = p.trace ? p.trace + static_cast<int64_t>(cta) * kGemvTrace : nullptr;
+    if (trace && threadIdx.x == 0) trace[0] = global_timer_ns();
     int T = p.total_chunks;
     if (p.njobs_dev) {                                // jobs built on the device by the previous kernel
         pdl_wait_prerequisites();
@@ -126,6 +128,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         const int npro = min(kNS, nst);
         if (lane == 0 && p.jobs_ready)
             for (int st = 0; st < npro; ++st) issue_weights(st);
+        if (trace && lane == 0) trace[1] = global_timer_ns();
         pdl_launch_dependents();
         pdl_wait_prerequisites();                     // activations may come from the previous kernel
         if (lane == 0 && !p.jobs_ready) {
@@ -189,6 +192,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     volatile int *flag = reinterpret_cast<volatile int *>(smem + p.off_bar + 2 * kNS * 8);
     pdl_launch_dependents();
     pdl_wait_prerequisites();                         // x / outputs / scratch may belong to the previous kernel
+    const bool tr = trace && threadIdx.x == 0;
+    if (tr) trace[2] = global_timer_ns();
 
     int j = lo / per_job;
     int g = (lo - j * per_job) / p.chunks;
@@ -205,6 +210,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         stage_activations<FMT, NT, false>(p.x, p.ldx, row_of(jb), jb->m, mslots, p.K, p.xstride,
                                           smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
     }
+    if (tr) trace[3] = global_timer_ns();
+    uint64_t waited = 0;
     // inside the chunk loop: fewer loads in flight per thread, so the loop keeps its registers
     auto restage = [&](int jj) {
         const GemvJob *jb = p.jobs + jj;
@@ -348,9 +355,15 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     bool failed = false;
     for (int st = 0; st < nst; ++st) {
         const int slot = st % kNS;
+        const uint64_t tw = tr ? global_timer_ns() : 0;
         if (!failed && !mbar_wait_bounded(full + slot * 8, (st / kNS) & 1, kWaitLimitNs)) {
             failed = true;
             if (lane == 0) atomicOr(p.err, 1);
+        }
+        if (tr) {
+            const uint64_t now = global_timer_ns();
+            waited += now - tw;
+            if (st == 0) trace[4] = now;
         }
         const int c0 = lo + st * kCPS, n = min(hi - c0, kCPS);
         const uint32_t wsb = wring + slot * STAGE_W + s * SB, xstage = slot * xstage_bytes;
@@ -380,7 +393,12 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         __syncwarp();
         if (lane == 0) mbar_arrive(empty + slot * 8);
     }
+    if (tr) trace[5] = global_timer_ns();
     if (seg < hi) flush(seg, hi);
+    if (tr) {
+        trace[6] = global_timer_ns();
+        trace[7] = waited;
+    }
 }
 
 template <int FMT, int NT, int EPI, bool CI>

@@ -203,6 +203,14 @@ __device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// the same with C = 0 (a fresh per-group sum: no register copies of zeros)
+__device__ __forceinline__ void mma16816_f16_z(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.f));
+}
+
 // offset table bytes per 64-K chunk: [group][n-tile][t][2 floats] = sum(x) of tokens 2t, 2t+1
 __host__ __device__ constexpr int tab_chunk_bytes(int nt) { return 2 * nt * 4 * 8; }
 
@@ -238,8 +246,8 @@ __device__ __forceinline__ void strip_chunk_h(uint32_t wsb, const uint32_t (&xa)
                 x0 = __uint_as_float(c2.x);
                 x1 = __uint_as_float(c2.y);
             }
-            float d[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816_f16(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+            float d[4];
+            mma16816_f16_z(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
             mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
             acc[nt][0] = fmaf(s_lo, d[0], acc[nt][0]);
             acc[nt][1] = fmaf(s_lo, d[1], acc[nt][1]);
@@ -302,8 +310,8 @@ __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], 
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 const float x0 = xs[gi][nt][0], x1 = xs[gi][nt][1];
-                float d[4] = {0.f, 0.f, 0.f, 0.f};
-                mma16816_f16(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+                float d[4];
+                mma16816_f16_z(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
                 mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
                 acc[s][nt][0] = fmaf(s_lo, d[0], acc[s][nt][0]);
                 acc[s][nt][1] = fmaf(s_lo, d[1], acc[s][nt][1]);

@@ -79,6 +79,11 @@ enum GemvEpilogue : int {
     kEpiSwiGLU = 2,   // strip rows 0-7 gate, 8-15 up: y[yrow][i] = bf16(silu(gate_i) * up_i)
 };
 
+// GEMV tracing: per CTA, ns stamps of kernel entry, producer's first copy issued, consumers past
+// griddepcontrol.wait, activations staged, first weight stage arrived, last stage consumed, range
+// flushed (split row groups closed), and the ns the consumers waited for weights in total
+constexpr int kGemvTrace = 8;
+
 struct GemvParams {
     const GemvJob *jobs;
     int njobs;
@@ -97,6 +102,7 @@ struct GemvParams {
     int jobs_ready;                    // job list not written by the previous kernel in the stream
     const int *njobs_dev;              // non-null: the job count lives on the device (written by the
                                        // previous kernel); njobs / total_chunks are upper bounds
+    unsigned long long *trace;         // non-null: %globaltimer stamps, kGemvTrace per CTA
     uint32_t mul[4];                   // 2^28, 2^24, 2^20, 2^16: shift multipliers the compiler cannot fold
     uint32_t unpk[3];                  // 0x000F000F, 0x00F000F0, 0x64006400 (fp16 code unpacking)
     int xslots;                        // per-stage activations: slots per chunk (max tokens + 1 zero slot)

@@ -125,6 +125,8 @@ struct Ctx {
     int64_t ts_cap = 0;
     int64_t calls = 0;
     double wait_s = 0;
+    unsigned long long *gemv_trace = nullptr;   // onpu_gemv_trace: stamps of later GEMV launches
+    int64_t gemv_trace_ctas = 0;
 };
 
 Ctx &ctx() {
@@ -247,6 +249,7 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     p.err = c.d_err;
     p.jobs_ready = d_njobs ? 0 : 1;
     p.njobs_dev = d_njobs;
+    p.trace = c.gemv_trace && W <= c.gemv_trace_ctas ? c.gemv_trace : nullptr;
     p.mul[0] = 1u << 28;
     p.mul[1] = 1u << 24;
     p.mul[2] = 1u << 20;
@@ -1586,6 +1589,14 @@ int onpu_chain_run(void *chain, void *stream) {
     p.trace = ch->trace;
     ONPU_CUDA(chain_launch(ch->fmt, ch->ntiles, p, ch->smem, static_cast<cudaStream_t>(stream)), -1);
     ++c.calls;
+    return 0;
+}
+
+int onpu_gemv_trace(uint64_t *stamps, int64_t ctas) {
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    c.gemv_trace = reinterpret_cast<unsigned long long *>(stamps);
+    c.gemv_trace_ctas = stamps ? ctas : 0;
     return 0;
 }
 

@@ -74,6 +74,7 @@ SIGNATURES = {
     "onpu_chain_run": (I32, [P, P]),
     "onpu_chain_trace": (I32, [P, P]),
     "onpu_chain_free": (None, [P]),
+    "onpu_gemv_trace": (I32, [P, I64]),
 }
 
 _LIB = None
