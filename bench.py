@@ -348,50 +348,68 @@ class MoEStack:
     routed-expert FFN of every layer; each layer has its own weights and its own bf16 N(0,1)
     input rows, so the routing (and the experts read) differs per layer."""
 
-    def __init__(self, T, seed, layers=M_LAYERS):
+    def __init__(self, T, seed, layers=M_LAYERS, rank=0, world=1, group=None):
+        """world > 1: expert parallelism, this rank holds experts [rank * E / world, ...) of every
+        layer and its own T tokens (moe.EPMoELayer: all-gather of tokens and routing, reduce-scatter
+        of the outputs). Router weights are the same on every rank."""
         from opennpu_b200 import moe
         self.moe = moe
         gen = torch.Generator(device="cuda")
-        gen.manual_seed(seed)
-        self.T, self.layers = T, []
+        gen.manual_seed(seed + 7919 * rank)
+        rgen = torch.Generator(device="cuda")
+        rgen.manual_seed(seed)
+        el = M_E // world
+        self.T, self.layers, self.world, self.rank = T, [], world, rank
         for _ in range(layers):
-            wr = (torch.randn(M_E, M_HIDDEN, device="cuda", generator=gen) * 0.02).to(torch.bfloat16)
-            gq = torch.randint(0, 256, (M_E, 2 * M_INTER, M_HIDDEN // 2), dtype=torch.uint8, device="cuda",
+            wr = (torch.randn(M_E, M_HIDDEN, device="cuda", generator=rgen) * 0.02).to(torch.bfloat16)
+            gq = torch.randint(0, 256, (el, 2 * M_INTER, M_HIDDEN // 2), dtype=torch.uint8, device="cuda",
                                generator=gen)
-            gs = ((torch.randn(M_E, 2 * M_INTER, M_HIDDEN // 32, device="cuda", generator=gen) * 0.02).abs()
+            gs = ((torch.randn(el, 2 * M_INTER, M_HIDDEN // 32, device="cuda", generator=gen) * 0.02).abs()
                   + 1e-4).half()
-            dq = torch.randint(0, 256, (M_E, M_HIDDEN, M_INTER // 2), dtype=torch.uint8, device="cuda", generator=gen)
-            ds = ((torch.randn(M_E, M_HIDDEN, M_INTER // 32, device="cuda", generator=gen) * 0.02).abs()
+            dq = torch.randint(0, 256, (el, M_HIDDEN, M_INTER // 2), dtype=torch.uint8, device="cuda", generator=gen)
+            ds = ((torch.randn(el, M_HIDDEN, M_INTER // 32, device="cuda", generator=gen) * 0.02).abs()
                   + 1e-4).half()
             ffn = moe.ExpertFFN(gq, gs, dq, ds)
             del gq, gs, dq, ds
-            self.layers.append((wr, ffn))
+            ep = moe.EPMoELayer(wr, ffn, rank, world, M_E, group=group, k=M_K) if world > 1 else None
+            self.layers.append((wr, ffn, ep))
         torch.cuda.synchronize()
         self.x = torch.randn(layers, T, M_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
         self.ids = torch.empty(layers, T, M_K, dtype=torch.int32, device="cuda")
         self.w = torch.empty(layers, T, M_K, device="cuda")
         self.y = torch.empty(layers, T, M_HIDDEN, device="cuda")
+        self.bufs = [ep.buffers(T, M_HIDDEN) for _, _, ep in self.layers] if world > 1 else None
         self.launches_per_step = 5 * layers            # router, job builder, gate_up, down, combine
         self.lib = __import__("opennpu_b200.libonpu", fromlist=["load"]).load()
 
     def step(self, stream):
         sp = stream.cuda_stream
-        for l, (wr, ffn) in enumerate(self.layers):
+        for l, (wr, ffn, ep) in enumerate(self.layers):
             x = self.x[l]
+            if ep is not None:
+                self.y[l].copy_(ep(x, self.bufs[l], stream=stream))
+                continue
             rc = self.lib.onpu_route_dev(x.data_ptr(), M_HIDDEN, self.T, wr.data_ptr(), M_E, M_HIDDEN, M_K, 1,
                                          self.ids[l].data_ptr(), self.w[l].data_ptr(), None, sp)
             assert rc == 0
             ffn(x, self.ids[l], self.w[l], out=self.y[l], stream=stream)
 
     def algorithmic_bytes(self):
-        """Per step: every layer's router weights and input rows, the int4 bytes of the experts its
-        tokens selected (each read once), the ids/weights and the fp32 outputs."""
+        """Per step and GPU: every layer's router weights and input rows, the int4 bytes of this
+        GPU's experts that the (all ranks') tokens selected, each read once, the ids/weights and the
+        fp32 outputs."""
         gu, dn = moe_expert_bytes()
-        ids = self.ids.cpu().numpy()
         b = 0
+        el = M_E // self.world
         for l in range(len(self.layers)):
-            nexp = len(np.unique(ids[l]))
-            b += nexp * (gu + dn) + M_E * M_HIDDEN * 2 + self.T * M_HIDDEN * (2 + 4) + self.T * M_K * 8
+            if self.world > 1:
+                ids = self.bufs[l]["ids_all"].cpu().numpy()
+                nexp = len({int(e) for e in np.unique(ids) if self.rank * el <= e < (self.rank + 1) * el})
+                toks = self.T * self.world
+            else:
+                nexp = len(np.unique(self.ids[l].cpu().numpy()))
+                toks = self.T
+            b += nexp * (gu + dn) + M_E * M_HIDDEN * 2 + toks * M_HIDDEN * (2 + 4) + toks * M_K * 8
         return b
 
 
@@ -437,7 +455,8 @@ def run_moe(args):
     hbm, _, peak_kind = peaks()
     T = args.m if args.m > 0 else 1
     layers = args.layers if args.layers != LAYERS else M_LAYERS
-    work = MoEStack(T, seed=3000 + rank, layers=layers)
+    group = torch.distributed.group.WORLD if world > 1 else None
+    work = MoEStack(T, seed=3000, layers=layers, rank=rank, world=world, group=group)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(max(args.warmup, 1)):
@@ -486,13 +505,19 @@ def run_moe(args):
         with torch.cuda.stream(s):
             for i in range(3 + 10):
                 if i == 3:
+                    if world > 1:
+                        torch.distributed.barrier()
                     t0 = time.perf_counter()
                 work.x.copy_(hx, non_blocking=True)
                 work.step(s)
                 hy.copy_(work.y, non_blocking=True)
                 s.synchronize()
         dt = (time.perf_counter() - t0) / 10
-        e2e = {"value": round(T / (dt / layers), 1), "unit": "tokens/s",
+        if world > 1:
+            t = torch.tensor([dt], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            dt = float(t.item())
+        e2e = {"value": round(T * world / (dt / layers), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 4,
                "ms_per_step": round(dt * 1e3, 3),
                "path": "onpu_route_dev + onpu_moe_ffn_dev per layer (no graph), pinned host input/output copies, "
@@ -508,9 +533,11 @@ def run_moe(args):
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
             "data": "synthetic (seeded random int4 experts, fp16 scales, bf16 N(0,1) tokens, N(0,0.02) router)",
-            "config": {"workload": "qwen3-30b-a3b-moe-layer", "T": T, "layers": layers, "experts": M_E,
-                       "top_k": M_K, "hidden": M_HIDDEN, "expert_inter": M_INTER,
-                       "parallelism": f"replicas{world}", "us_per_layer": round(layer_us, 3),
+            "config": {"workload": "qwen3-30b-a3b-moe-layer", "T": T, "T_per_gpu": T, "layers": layers,
+                       "experts": M_E, "top_k": M_K, "hidden": M_HIDDEN, "expert_inter": M_INTER,
+                       "parallelism": f"ep{world}" if world > 1 else "single", "us_per_layer": round(layer_us, 3),
+                       "collective": "NCCL all-gather (tokens, ids, weights) + reduce-scatter (outputs)"
+                       if world > 1 else None,
                        "l2": "selected experts of all layers per step exceed L2 (no flush needed)",
                        "cuda_graph": True},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
@@ -523,6 +550,180 @@ def run_moe(args):
         print(json.dumps(line), flush=True)
     del graph
     if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+T_HIDDEN, T_INTER, T_QH, T_KVH, T_LAYERS = 5120, 27648, 40, 8, 64
+
+
+class TPStack:
+    """Qwen2.5-32B decode projections, 64 layers of random int4 weights, tensor-parallel
+    over the ranks: q/k/v and gate/up column-parallel (row blocks), o and down row-parallel (K
+    blocks on 32-group boundaries) with an all-reduce of the fp32 partial outputs after each. Each
+    rank generates only its own shards. The layer input of layer l+1 is layer l's output (bf16)."""
+
+    def __init__(self, M, rank, world, group, seed, layers=T_LAYERS, allreduce=None):
+        from opennpu_b200 import tp
+        self.tp = tp
+        gen = torch.Generator(device="cuda")
+        gen.manual_seed(seed)
+        q, kv = T_QH * 128 // world, T_KVH * 128 // world
+        i_r, h_r = T_INTER // world, T_HIDDEN // world
+        self.layers = []
+        for _ in range(layers):
+            qkv = gen_int4_cuda(q + 2 * kv, T_HIDDEN, gen)
+            o = gen_int4_cuda(T_HIDDEN, h_r, gen)
+            gu = gen_int4_cuda(2 * i_r, T_HIDDEN, gen)
+            dn = gen_int4_cuda(T_HIDDEN, i_r, gen)
+            self.layers.append(tp.TPDecoderLayer(qkv, o, gu, dn, q, group=group, allreduce=allreduce))
+            del qkv, o, gu, dn
+        torch.cuda.synchronize()
+        self.M, self.world = M, world
+        self.x = torch.randn(M, T_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+        self.xs = [torch.empty(M, T_HIDDEN, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+        self.bufs = self.layers[0].buffers(M)
+        shards = [(q + 2 * kv, T_HIDDEN), (T_HIDDEN, h_r), (2 * i_r, T_HIDDEN), (T_HIDDEN, i_r)]
+        self.bytes_per_layer = sum(int4_param_bytes(N, K) + M * K * 2 + M * N * 4 for N, K in shards)
+        self.launches_per_step = 4 * layers                   # our GEMVs (plus NCCL all-reduces, casts)
+
+    def step(self):
+        x = self.x
+        for i, lay in enumerate(self.layers):
+            nx = self.xs[i & 1]
+            lay(x, self.bufs, y_bf16=nx)
+            x = nx
+        return self.bufs["y"]
+
+
+def cpu_tp_sample(M, seconds=10.0, seed=0):
+    """The reference's CPU path on one Qwen2.5-32B layer's projections (dequantise per 32 and fp32
+    matmul, all host threads, M tokens); GB/s of int4 weights."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    from opennpu_b200 import tp
+    mats = []
+    for name, N, K in tp.dense_layer_shapes(T_HIDDEN, T_INTER, T_QH, T_KVH):
+        v = torch.randint(-8, 8, (N, K), dtype=torch.int8, generator=g)
+        sc = ((torch.randn(N, K // 32, generator=g) * 0.02).abs() + 1e-4).to(torch.float16)
+        mats.append((N, K, v, sc))
+    x = torch.randn(M, T_HIDDEN, generator=g).bfloat16().float()
+    a = torch.randn(M, T_INTER, generator=g).bfloat16().float()
+    layer_bytes = sum(int4_param_bytes(N, K) for N, K, _, _ in mats)
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds or n < 1:
+        for N, K, v, sc in mats:
+            W = (v.view(N, K // 32, 32).float() * sc.float()[..., None]).view(N, K)
+            (x if K == T_HIDDEN else (a if K == T_INTER else x)) @ W.T
+        n += 1
+    dt = time.perf_counter() - t0
+    return n * layer_bytes / dt / 1e9, torch.get_num_threads(), f"{n} x one Qwen2.5-32B layer's 7 projections (dequant + fp32 matmul, M={M})"
+
+
+def run_tp(args):
+    rank, world, local = dist_setup(args.gpus)
+    hbm, _, peak_kind = peaks()
+    M = args.m
+    layers = args.layers if args.layers != LAYERS else T_LAYERS
+    group = torch.distributed.group.WORLD if world > 1 else None
+    allreduce = None
+    if world > 1 and args.allreduce == "peer":
+        from opennpu_b200.comm import PeerAllReduce
+        allreduce = PeerAllReduce(group, cap_floats=M * T_HIDDEN)
+    work = TPStack(M, rank, world, group, seed=4000 + rank, layers=layers, allreduce=allreduce)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(max(args.warmup, 1)):
+            work.step()
+    s.synchronize()
+    from opennpu_b200 import dense
+    dense.check_device()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        work.step()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            graph.replay()
+    s.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(args.steps):
+            graph.replay()
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    dense.check_device()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    tok_s = M / (ms_step * 1e-3)
+    rank_bytes = work.bytes_per_layer * layers
+    gbs_rank = rank_bytes / (ms_step * 1e-3) / 1e9
+
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(work.x.shape, dtype=torch.bfloat16, pin_memory=True)
+        hx.copy_(work.x)
+        hy = torch.empty(work.bufs["y"].shape, dtype=torch.float32, pin_memory=True)
+        with torch.cuda.stream(s):
+            for i in range(3 + 10):
+                if i == 3:
+                    if world > 1:
+                        torch.distributed.barrier()
+                    t0 = time.perf_counter()
+                work.x.copy_(hx, non_blocking=True)
+                graph.replay()
+                hy.copy_(work.bufs["y"], non_blocking=True)
+                s.synchronize()
+        dt = (time.perf_counter() - t0) / 10
+        if world > 1:
+            t = torch.tensor([dt], device="cuda")
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            dt = float(t.item())
+        e2e = {"value": round(M / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": hx.numel() * 2,
+               "d2h_bytes_per_step": hy.numel() * 4, "ms_per_step": round(dt * 1e3, 3),
+               "path": "TPDecoderLayer stack (onpu_dense_mv_dev + NCCL all-reduce) from a CUDA graph, pinned host "
+                       "input/output copies and a host synchronisation per step"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, sample = cpu_tp_sample(M, seconds=args.cpu_seconds)
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        line = {
+            "metric": "int4 dense decode stack tokens/s (Qwen2.5-32B, tensor-parallel)", "value": round(tok_s, 2),
+            "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1))",
+            "config": {"workload": "qwen2.5-32b-decode-projections-tp", "M": M, "layers": layers,
+                       "parallelism": f"tp{world}", "gb_per_s_all_ranks": round(gbs_rank * world, 1),
+                       "bytes_per_step_per_gpu": rank_bytes,
+                       "l2": "inputs larger than L2 (no flush needed)", "cuda_graph": True,
+                       "collective": (("one-shot all-reduce over NVLink peer memory (libonpu comm kernel)"
+                                       if allreduce is not None else "NCCL all-reduce") + " (fp32) after o and down")
+                       if world > 1 else None},
+            "roofline": {"bound": "hbm", "achieved": round(gbs_rank, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(gbs_rank / hbm, 4), "peak_kind": peak_kind + " (copy bandwidth)",
+                         "traffic": None, "kernel": "whole decode step per GPU (GEMVs, all-reduces, casts)"},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": work.launches_per_step * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        torch.distributed.barrier()
+        if allreduce is not None:
+            allreduce.close()
+            torch.distributed.barrier()
         torch.distributed.destroy_process_group()
 
 
@@ -858,8 +1059,11 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill", "moe"])
-    ap.add_argument("--m", type=int, default=1)
+    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill", "moe", "qwen2.5-32b"])
+    ap.add_argument("--m", "--rows", dest="m", type=int, default=1,
+                    help="tokens (M / T); spell it --rows under torchrun, which claims --m")
+    ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
+                    help="qwen2.5-32b at N>1: the row-parallel all-reduce (peer-memory kernel or NCCL)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -876,6 +1080,8 @@ def main():
         run_prefill(args)
     elif args.config == "moe":
         run_moe(args)
+    elif args.config == "qwen2.5-32b":
+        run_tp(args)
     else:
         run_ours(args)
 

@@ -168,6 +168,28 @@ void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t 
  * (llama/ggml-opennpu/onpu_api.cpp:261-278). 0 ok, < 0 error. */
 int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
                      float *y, int64_t ldy, void *stream);
+/* Expert parallelism: the same layer when this FFN holds only experts e0 .. e0 + E - 1 of a larger
+ * pool. ids are global; slots routed to other experts are skipped, so y[t] is this rank's share of
+ * the sum (the ranks' shares add up to onpu_moe_ffn_dev's y). No reference counterpart (the
+ * reference has no multi-device path). 0 ok, < 0 error. */
+int onpu_moe_ffn_dev_ep(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
+                        int64_t e0, float *y, int64_t ldy, void *stream);
+/* ---- one-shot all-reduce over NVLink peer memory (tensor-parallel decode; no reference
+ * counterpart). One handle per rank (one process per GPU): onpu_comm_new allocates this rank's
+ * buffer for vectors of up to cap floats, onpu_comm_ipc_handle writes its 64-byte CUDA IPC handle,
+ * the caller exchanges the handles (e.g. an all-gather on the host) and passes all world of them,
+ * in rank order, to onpu_comm_open. onpu_comm_allreduce: the sum over ranks of src (n floats) into
+ * dst (fp32, may be src) and / or dst_bf16 (bf16; either may be NULL), one launch on `stream`:
+ * every rank stores each value, paired with the call number in one 8-byte word, into every peer's
+ * buffer, then reads the world words of each element until they carry this call's number and
+ * adds them in rank order (identical sums on every rank). Every rank must make the same sequence
+ * of calls; capturable in a CUDA graph. A peer that does not arrive within 2 s sets the device
+ * status (onpu_check_device). */
+void *onpu_comm_new(int rank, int world, int64_t cap_floats);
+int onpu_comm_ipc_handle(void *comm, void *out64);
+int onpu_comm_open(void *comm, const void *handles);
+int onpu_comm_allreduce(void *comm, const float *src, float *dst, void *dst_bf16, int64_t n, void *stream);
+void onpu_comm_free(void *comm);
 /* ---- GEMV chains: a decode step's dense GEMVs recorded once on fixed device buffers and run as
  * ONE persistent launch (the GPU analogue of the reference's instruction stream per call,
  * llama/ggml-opennpu/opennpu_core.hpp:418-505, and of onpu_ffn_run's gate_up -> act -> down

@@ -1,0 +1,116 @@
+// One-shot all-reduce of small fp32 vectors between the GPUs of one node over NVLink peer memory
+// (tensor-parallel decode: the [M, hidden] partial outputs of the row-parallel o and down
+// projections, 20-160 KB), with the sum also written as bf16 (the next projection's input).
+//
+// Every rank owns one buffer (cudaMalloc, shared with the peers through CUDA IPC handles):
+//   slots[2][world][cap] of 8-byte words {fp32 value, call number} | calls[kCommCtas] u32
+// A call is one launch of kCommCtas CTAs; CTA b owns elements [b * per, (b + 1) * per):
+//  1. every thread stores its elements of the local partial, each paired with the call number in
+//     one 8-byte store, into slot [parity][rank] of every rank's buffer (peer stores over NVLink);
+//  2. it then reads slot [parity][s][i] of its own buffer for every rank s, until the word carries
+//     this call's number (an 8-byte store lands whole, so value and number arrive together: no
+//     fence, no separate flag), and adds the values in rank order (the same float sum on every
+//     rank). Waits are bounded (2 s, then the error word is set and the word's value is used).
+// The call number is kept per CTA in the owner's buffer, so CUDA-graph replays need no host
+// state. Two slot sets by call parity: a rank can be at most one call ahead of a peer that is
+// still reading (it cannot finish call c+1 without that peer's words of call c+1).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "ptx.cuh"
+
+namespace onpu_b200 {
+
+namespace {
+
+constexpr int kCommThreads = 256;
+constexpr uint64_t kCommWaitNs = 2000000000ull;
+
+struct CommParams {
+    uint2 *bufs[kCommMaxRanks];      // every rank's buffer (this rank's own at [rank])
+    int rank, world;
+    int64_t cap;                     // words per slot
+    const float *src;                // this rank's partial [n]
+    float *dst;                      // the sum [n] (may alias src; may be null)
+    __nv_bfloat16 *dst_bf16;         // the sum as bf16 [n] (may be null)
+    int64_t n;
+    int *err;
+};
+
+__device__ __forceinline__ void st_word(uint2 *p, uint32_t v, uint32_t tag) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint2 ld_word(const uint2 *p) {
+    uint2 r;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+    return r;
+}
+
+__global__ void __launch_bounds__(kCommThreads) comm_allreduce_kernel(const CommParams p) {
+    const int b = blockIdx.x;
+    const int64_t per = (p.n + kCommCtas - 1) / kCommCtas;
+    const int64_t lo = b * per, hi = lo + per < p.n ? lo + per : p.n;
+    uint2 *own = p.bufs[p.rank];
+    uint32_t *calls = reinterpret_cast<uint32_t *>(own + 2 * static_cast<int64_t>(p.world) * p.cap);
+    __shared__ uint32_t call;
+    if (threadIdx.x == 0) call = calls[b] + 1u;
+    __syncthreads();
+    const uint32_t c = call;
+    const int64_t set = static_cast<int64_t>(c & 1u) * p.world;
+    for (int64_t i = lo + threadIdx.x; i < hi; i += kCommThreads) {
+        const uint32_t v = __float_as_uint(p.src[i]);
+        for (int d = 0; d < p.world; ++d) st_word(p.bufs[d] + (set + p.rank) * p.cap + i, v, c);
+    }
+    for (int64_t i = lo + threadIdx.x; i < hi; i += kCommThreads) {
+        float acc = 0.f;
+        for (int s = 0; s < p.world; ++s) {
+            const uint2 *w = own + (set + s) * p.cap + i;
+            uint2 r = ld_word(w);
+            if (r.y != c) {
+                const uint64_t t0 = global_timer_ns();
+                for (int it = 0; r.y != c; ++it) {
+                    if ((it & 255) == 255 && global_timer_ns() - t0 > kCommWaitNs) {
+                        atomicOr(p.err, 16);
+                        break;
+                    }
+                    r = ld_word(w);
+                }
+            }
+            const float x = __uint_as_float(r.x);
+            acc = s == 0 ? x : acc + x;
+        }
+        if (p.dst) p.dst[i] = acc;
+        if (p.dst_bf16) p.dst_bf16[i] = __float2bfloat16_rn(acc);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) calls[b] = c;
+}
+
+}  // namespace
+
+int64_t comm_buffer_bytes(int world, int64_t cap) {
+    return 2 * static_cast<int64_t>(world) * cap * 8 + kCommCtas * 4;
+}
+
+cudaError_t comm_allreduce_launch(void *const *bufs, int rank, int world, int64_t cap, const float *src, float *dst,
+                                  void *dst_bf16, int64_t n, int *err, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    if (world < 1 || world > kCommMaxRanks || n > cap) return cudaErrorInvalidValue;
+    CommParams p{};
+    for (int r = 0; r < world; ++r) p.bufs[r] = static_cast<uint2 *>(bufs[r]);
+    p.rank = rank;
+    p.world = world;
+    p.cap = cap;
+    p.src = src;
+    p.dst = dst;
+    p.dst_bf16 = static_cast<__nv_bfloat16 *>(dst_bf16);
+    p.n = n;
+    p.err = err;
+    comm_allreduce_kernel<<<kCommCtas, kCommThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+}  // namespace onpu_b200

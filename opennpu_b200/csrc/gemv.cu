@@ -86,6 +86,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     }
     const int lo = static_cast<int>(static_cast<int64_t>(cta) * T / W);
     const int hi = static_cast<int>(static_cast<int64_t>(cta + 1) * T / W);
+    if (lo >= hi) return;      // no chunks (a device-side job count below the grid, or zero jobs)
     const int nst = (hi - lo + kCPS - 1) / kCPS;
     const int per_job = p.row_groups * p.chunks;
     constexpr bool xres = CI;                         // resident activations carry the offset table

@@ -2,6 +2,7 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstdint>
 
 #include "gpu_layout.cuh"
@@ -55,6 +56,16 @@ cudaError_t x_to_f16_launch(const uint16_t *x, int64_t ldx, int M, int K, uint16
 cudaError_t dqgemm_launch(int fmt, int epi, const uint16_t *xh, const DqGemmParams &p, cudaStream_t stream);
 int dqgemm_tile_tokens();
 
+// ---- one-shot all-reduce over NVLink peer memory (comm.cu)
+constexpr int kCommCtas = 16;
+constexpr int kCommMaxRanks = 8;
+// bytes of one rank's buffer: two slot sets of world x cap 8-byte words, per-CTA call counters
+int64_t comm_buffer_bytes(int world, int64_t cap);
+// bufs[r]: rank r's buffer as mapped in this process (own at [rank]); dst (fp32) and / or dst_bf16
+// = the sum over ranks of src, added in rank order
+cudaError_t comm_allreduce_launch(void *const *bufs, int rank, int world, int64_t cap, const float *src, float *dst,
+                                  void *dst_bf16, int64_t n, int *err, cudaStream_t stream);
+
 // ---- MoE router (router.cu): softmax(h . Wr^T) -> top-k -> renormalise, one CTA per token
 constexpr int kMaxRouteExperts = 256;
 constexpr int kMaxRouteK = 16;
@@ -74,6 +85,8 @@ struct ExpertJobsParams {
     int *njobs;                // out: jobs in each list
     int *order;                // scratch [TK]
     int *err;                  // bit 8: an id outside [0, E) (that pair is dropped)
+    int id_base;               // the bank holds experts id_base .. id_base + E - 1
+    int skip_foreign;          // 1: ids outside that range belong to other ranks (skipped, no error)
 };
 cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream);
 
@@ -120,7 +133,10 @@ cudaError_t moe_act_launch(const float *h, int64_t ldh, int64_t rows, int64_t Ng
                            const float *gu_bias, int act, float alpha, float limit, uint16_t *a, int64_t lda,
                            cudaStream_t stream);
 // y[t][n] = sum_j w[t][j] * (o[(t*k + j)][n] + bias[ids[t*k+j]][n]) in slot order.
+// Only slots whose expert id lies in [id_lo, id_hi) contribute (expert parallelism: this rank's
+// experts); the default range takes every slot.
 cudaError_t moe_combine_launch(const float *o, int64_t ldo, int64_t T, int k, int64_t N, const int32_t *ids,
-                               const float *w, const float *bias, float *y, int64_t ldy, cudaStream_t stream);
+                               const float *w, const float *bias, float *y, int64_t ldy, cudaStream_t stream,
+                               int id_lo = INT32_MIN, int id_hi = INT32_MAX);
 
 }  // namespace onpu_b200

@@ -28,7 +28,7 @@ __global__ void f32_to_bf16_kernel(const float *x, int64_t rows, int64_t cols, i
 // Weighted sum of a token's expert outputs in slot order (onpu_cpu.cpp:259-274 semantics):
 // deterministic, one thread per output element.
 __global__ void moe_combine_kernel(const float *o, int64_t ldo, int64_t T, int k, int64_t N, const int32_t *ids,
-                                   const float *w, const float *bias, float *y, int64_t ldy) {
+                                   const float *w, const float *bias, float *y, int64_t ldy, int id_lo, int id_hi) {
     const int64_t n = T * N;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -36,6 +36,7 @@ __global__ void moe_combine_kernel(const float *o, int64_t ldo, int64_t T, int k
         float acc = 0.f;
         for (int j = 0; j < k; ++j) {
             const int64_t slot = t * k + j;
+            if (ids[slot] < id_lo || ids[slot] >= id_hi) continue;
             float v = o[slot * ldo + c];
             if (bias) v += bias[static_cast<int64_t>(ids[slot]) * N + c];
             acc += w[slot] * v;
@@ -93,9 +94,10 @@ cudaError_t f32_to_bf16_launch(const float *x, int64_t rows, int64_t cols, int64
 }
 
 cudaError_t moe_combine_launch(const float *o, int64_t ldo, int64_t T, int k, int64_t N, const int32_t *ids,
-                               const float *w, const float *bias, float *y, int64_t ldy, cudaStream_t stream) {
+                               const float *w, const float *bias, float *y, int64_t ldy, cudaStream_t stream,
+                               int id_lo, int id_hi) {
     if (T * N == 0) return cudaSuccess;
-    moe_combine_kernel<<<grid_for(T * N, 256), 256, 0, stream>>>(o, ldo, T, k, N, ids, w, bias, y, ldy);
+    moe_combine_kernel<<<grid_for(T * N, 256), 256, 0, stream>>>(o, ldo, T, k, N, ids, w, bias, y, ldy, id_lo, id_hi);
     return cudaGetLastError();
 }
 

@@ -293,7 +293,9 @@ int check_device_err(Ctx &c) {
         cudaMemset(c.d_err, 0, sizeof(int));
         if (c.d_cnt) cudaMemset(c.d_cnt, 0, sizeof(unsigned) * c.cnt_cap);
         reset_chains_after_error();
-        if (h & 8)
+        if (h & 16)
+            set_err("an all-reduce timed out waiting for a peer rank (device status %d)", h);
+        else if (h & 8)
             set_err("an expert id was out of range [0, E) in a routed job list; those (token, slot) pairs were "
                     "dropped (device status %d)", h);
         else
@@ -1115,9 +1117,11 @@ void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t 
     return f;
 }
 
-int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
-                     float *y, int64_t ldy, void *stream) {
-    clear_err();
+namespace {
+// e0 >= 0: expert parallelism, the FFN holds experts e0 .. e0 + E - 1 and the other ids are
+// skipped (their slots contribute nothing to y)
+int moe_ffn_dev_impl(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
+                     int64_t e0, float *y, int64_t ldy, void *stream) {
     auto *f = static_cast<FfnH *>(ffn);
     if (T <= 0) return 0;
     if (!f || !f->fused || k < 1) {
@@ -1164,6 +1168,8 @@ int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     jp.njobs = c.d_njobs;
     jp.order = c.d_order;
     jp.err = c.d_err;
+    jp.id_base = e0 >= 0 ? static_cast<int>(e0) : 0;
+    jp.skip_foreign = e0 >= 0 ? 1 : 0;
     ONPU_CUDA(expert_jobs_launch(jp, s), -1);
     const int mmax = static_cast<int>(std::min<int64_t>(T, per_job)), ntiles = mmax > 8 ? 2 : 1;
     // an expert sees each token at most once (the k experts of a token are distinct); the down
@@ -1174,8 +1180,30 @@ int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     if (run_gemv(c, dn->mat, jp.jobs1, static_cast<int>(njmax), ntiles, mmax, kEpiF32, c.d_a, Kd, c.d_o, Nd, s, true,
                  c.d_njobs))
         return -1;
-    ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, ids, w, nullptr, y, ldy, s), -1);
+    if (e0 >= 0)
+        ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, ids, w, nullptr, y, ldy, s, static_cast<int>(e0),
+                                     static_cast<int>(e0 + E)),
+                  -1);
+    else
+        ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, ids, w, nullptr, y, ldy, s), -1);
     return 0;
+}
+}  // namespace
+
+int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
+                     float *y, int64_t ldy, void *stream) {
+    clear_err();
+    return moe_ffn_dev_impl(ffn, x, ldx, T, ids, w, k, -1, y, ldy, stream);
+}
+
+int onpu_moe_ffn_dev_ep(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
+                        int64_t e0, float *y, int64_t ldy, void *stream) {
+    clear_err();
+    if (e0 < 0 || e0 > INT32_MAX / 2) {
+        set_err("onpu_moe_ffn_dev_ep: first expert id %lld out of range", static_cast<long long>(e0));
+        return -1;
+    }
+    return moe_ffn_dev_impl(ffn, x, ldx, T, ids, w, k, e0, y, ldy, stream);
 }
 
 int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream) {
@@ -1590,6 +1618,104 @@ int onpu_chain_run(void *chain, void *stream) {
     ONPU_CUDA(chain_launch(ch->fmt, ch->ntiles, p, ch->smem, static_cast<cudaStream_t>(stream)), -1);
     ++c.calls;
     return 0;
+}
+
+// ---- one-shot all-reduce between the ranks of one node (tensor-parallel decode)
+struct CommH {
+    int rank = 0, world = 1, device = -1;
+    int64_t cap = 0;
+    void *buf = nullptr;                        // this rank's buffer
+    void *bufs[kCommMaxRanks] = {};             // every rank's buffer, mapped here
+    bool mapped[kCommMaxRanks] = {};
+    ~CommH() {
+        for (int r = 0; r < kCommMaxRanks; ++r)
+            if (mapped[r]) cudaIpcCloseMemHandle(bufs[r]);
+        if (buf) cudaFree(buf);
+    }
+};
+
+void *onpu_comm_new(int rank, int world, int64_t cap_floats) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    if (world < 1 || world > kCommMaxRanks || rank < 0 || rank >= world || cap_floats <= 0) {
+        set_err("onpu_comm_new: need 1 <= world <= %d, 0 <= rank < world, cap > 0", kCommMaxRanks);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *h = new CommH;
+    h->rank = rank;
+    h->world = world;
+    h->cap = (cap_floats + 3) / 4 * 4;
+    cudaGetDevice(&h->device);
+    const int64_t bytes = comm_buffer_bytes(world, h->cap);
+    if (cudaMalloc(&h->buf, static_cast<size_t>(bytes)) != cudaSuccess ||
+        cudaMemset(h->buf, 0, static_cast<size_t>(bytes)) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        set_err("onpu_comm_new: %s", cudaGetErrorString(cudaGetLastError()));
+        delete h;
+        return nullptr;
+    }
+    h->bufs[rank] = h->buf;
+    return h;
+}
+
+int onpu_comm_ipc_handle(void *comm, void *out) {
+    clear_err();
+    auto *h = static_cast<CommH *>(comm);
+    cudaIpcMemHandle_t ih;
+    ONPU_CUDA(cudaIpcGetMemHandle(&ih, h->buf), -1);
+    std::memcpy(out, &ih, sizeof(ih));
+    return static_cast<int>(sizeof(ih));
+}
+
+int onpu_comm_open(void *comm, const void *handles) {
+    clear_err();
+    auto *h = static_cast<CommH *>(comm);
+    std::lock_guard<std::mutex> lk(g_mu);
+    const auto *hb = static_cast<const unsigned char *>(handles);
+    for (int r = 0; r < h->world; ++r) {
+        if (r == h->rank || h->mapped[r]) continue;
+        cudaIpcMemHandle_t ih;
+        std::memcpy(&ih, hb + r * sizeof(ih), sizeof(ih));
+        void *ptr = nullptr;
+        ONPU_CUDA(cudaIpcOpenMemHandle(&ptr, ih, cudaIpcMemLazyEnablePeerAccess), -1);
+        h->bufs[r] = ptr;
+        h->mapped[r] = true;
+    }
+    return 0;
+}
+
+int onpu_comm_allreduce(void *comm, const float *src, float *dst, void *dst_bf16, int64_t n, void *stream) {
+    clear_err();
+    auto *h = static_cast<CommH *>(comm);
+    if ((!dst && !dst_bf16) || (dst_bf16 && (reinterpret_cast<uintptr_t>(dst_bf16) & 1))) {
+        set_err("onpu_comm_allreduce: needs an fp32 and / or an aligned bf16 output");
+        return -1;
+    }
+    if (n > h->cap || n < 0) {
+        set_err("onpu_comm_allreduce: %lld floats exceed the buffer's %lld", static_cast<long long>(n),
+                static_cast<long long>(h->cap));
+        return -1;
+    }
+    for (int r = 0; r < h->world; ++r)
+        if (!h->bufs[r]) {
+            set_err("onpu_comm_allreduce: rank %d's buffer is not mapped (onpu_comm_open)", r);
+            return -1;
+        }
+    Ctx &c = ctx();
+    ONPU_CUDA(comm_allreduce_launch(h->bufs, h->rank, h->world, h->cap, src, dst, dst_bf16, n, c.d_err,
+                                    static_cast<cudaStream_t>(stream)),
+              -1);
+    return 0;
+}
+
+void onpu_comm_free(void *comm) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaDeviceSynchronize();
+    delete static_cast<CommH *>(comm);
 }
 
 int onpu_gemv_trace(uint64_t *stamps, int64_t ctas) {

@@ -184,9 +184,9 @@ __global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJo
     }
     __syncthreads();
     for (int64_t i = tid; i < p.TK; i += kJobThreads) {
-        const int e = p.ids[i];
+        const int e = p.ids[i] - p.id_base;
         if (e >= 0 && e < p.E) atomicAdd(&cnt[e], 1);
-        else atomicOr(p.err, 8);
+        else if (!p.skip_foreign) atomicOr(p.err, 8);
     }
     __syncthreads();
     // slot offsets and job offsets per expert (E may exceed the block: scan in pieces)
@@ -209,7 +209,7 @@ __global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJo
     // stable placement: warps in turn claim consecutive places per expert
     for (int64_t b = 0; b < p.TK; b += kJobThreads) {
         const int64_t i = b + tid;
-        const int e = i < p.TK ? p.ids[i] : -1;
+        const int e = i < p.TK ? p.ids[i] - p.id_base : -1;
         const bool ok = e >= 0 && e < p.E;
         const unsigned grp = __match_any_sync(0xffffffffu, ok ? e : -1);
         const int rank = __popc(grp & ((1u << lane) - 1u)), leader = __ffs(grp) - 1;

@@ -66,6 +66,12 @@ SIGNATURES = {
     "onpu_bank_load_int4": (I32, [P, P, P, I32, P]),
     "onpu_ffn_new_int4": (P, [I64, I64, I64, I64, I64]),
     "onpu_moe_ffn_dev": (I32, [P, P, I64, I64, P, P, I32, P, I64, P]),
+    "onpu_moe_ffn_dev_ep": (I32, [P, P, I64, I64, P, P, I32, I64, P, I64, P]),
+    "onpu_comm_new": (P, [I32, I32, I64]),
+    "onpu_comm_ipc_handle": (I32, [P, P]),
+    "onpu_comm_open": (I32, [P, P]),
+    "onpu_comm_allreduce": (I32, [P, P, P, P, I64, P]),
+    "onpu_comm_free": (None, [P]),
     "onpu_chain_new": (P, []),
     "onpu_chain_add": (I32, [P, P, P, I64, I64, P, I64, I32, I32]),
     "onpu_chain_info": (I32, [P, I64P]),

@@ -54,15 +54,22 @@ class ExpertFFN:
             rc = lib.onpu_bank_load_int4(bank, qk.numpy().ctypes.data, s.numpy().ctypes.data, 0, None)
         L.check(rc, "onpu_bank_load_int4")
 
-    def __call__(self, x, ids, w, out=None, stream=None):
-        """x: bf16 CUDA [T, H]; ids int32 / w fp32 CUDA [T, k] (from ``route``) -> fp32 [T, H]."""
+    def __call__(self, x, ids, w, out=None, stream=None, e0=None):
+        """x: bf16 CUDA [T, H]; ids int32 / w fp32 CUDA [T, k] (from ``route``) -> fp32 [T, H].
+        e0: this FFN holds experts e0 .. e0 + E - 1 of a larger pool (expert parallelism); slots
+        routed elsewhere are skipped and the result is this shard's share of the sum."""
         assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
         assert ids.dtype == torch.int32 and ids.is_contiguous() and w.dtype == torch.float32 and w.is_contiguous()
         T, k = ids.shape
         if out is None:
             out = torch.empty(T, self.Nd, dtype=torch.float32, device=x.device)
-        rc = L.load().onpu_moe_ffn_dev(self.h, x.data_ptr(), x.stride(0), T, ids.data_ptr(), w.data_ptr(), k,
-                                       out.data_ptr(), out.stride(0), _stream_ptr(stream))
+        lib = L.load()
+        if e0 is None:
+            rc = lib.onpu_moe_ffn_dev(self.h, x.data_ptr(), x.stride(0), T, ids.data_ptr(), w.data_ptr(), k,
+                                      out.data_ptr(), out.stride(0), _stream_ptr(stream))
+        else:
+            rc = lib.onpu_moe_ffn_dev_ep(self.h, x.data_ptr(), x.stride(0), T, ids.data_ptr(), w.data_ptr(), k, e0,
+                                         out.data_ptr(), out.stride(0), _stream_ptr(stream))
         L.check(rc, "onpu_moe_ffn_dev")
         return out
 
@@ -73,3 +80,42 @@ class ExpertFFN:
                 self.h = None
         except Exception:   # interpreter shutdown: the library may already be unloaded
             pass
+
+
+class EPMoELayer:
+    """Expert-parallel MoE layer on one rank of a process group (NCCL): this rank holds experts
+    [rank * E / world, (rank + 1) * E / world) and its own T tokens. The ranks all-gather their
+    tokens and routing (ids, weights), each runs its experts over every rank's tokens routed to
+    them, and a reduce-scatter sums the shares back to the tokens' owners. The router runs where
+    the tokens live."""
+
+    def __init__(self, wr, ffn, rank, world, E, group=None, k=8, norm_topk_prob=True):
+        self.wr, self.ffn, self.rank, self.world, self.group = wr, ffn, rank, world, group
+        self.E, self.k, self.norm = E, k, norm_topk_prob
+        assert E % world == 0 and ffn.E == E // world
+        self.e0 = rank * (E // world)
+
+    def buffers(self, T, H, device="cuda"):
+        W = self.world
+        return {"ids": torch.empty(T, self.k, dtype=torch.int32, device=device),
+                "w": torch.empty(T, self.k, device=device),
+                "x_all": torch.empty(W * T, H, dtype=torch.bfloat16, device=device),
+                "ids_all": torch.empty(W * T, self.k, dtype=torch.int32, device=device),
+                "w_all": torch.empty(W * T, self.k, device=device),
+                "y_all": torch.empty(W * T, self.ffn.Nd, device=device),
+                "y": torch.empty(T, self.ffn.Nd, device=device)}
+
+    def __call__(self, x, b, stream=None):
+        """x: bf16 [T, H] (this rank's tokens) -> b["y"] fp32 [T, H]."""
+        T = x.shape[0]
+        lib = L.load()
+        rc = lib.onpu_route_dev(x.data_ptr(), x.stride(0), T, self.wr.data_ptr(), self.E, self.wr.shape[1], self.k,
+                                int(self.norm), b["ids"].data_ptr(), b["w"].data_ptr(), None, _stream_ptr(stream))
+        L.check(rc, "onpu_route_dev")
+        dist = torch.distributed
+        dist.all_gather_into_tensor(b["x_all"], x, group=self.group)
+        dist.all_gather_into_tensor(b["ids_all"], b["ids"], group=self.group)
+        dist.all_gather_into_tensor(b["w_all"], b["w"], group=self.group)
+        self.ffn(b["x_all"], b["ids_all"], b["w_all"], out=b["y_all"], stream=stream, e0=self.e0)
+        dist.reduce_scatter_tensor(b["y"], b["y_all"], group=self.group)
+        return b["y"]

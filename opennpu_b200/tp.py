@@ -1,0 +1,121 @@
+"""Tensor-parallel int4 projections (one process per GPU, torch.distributed over NCCL).
+
+Column-parallel matrices (q/k/v, gate/up) keep a contiguous block of output rows per rank; row-
+parallel matrices (o, down) keep a contiguous block of the K axis per rank, cut on 32-group
+boundaries so every rank's scales stay whole, and their partial outputs are summed across ranks
+(all-reduce, fp32). The reference has no multi-device path; the split follows the usual Megatron
+layout for a decoder layer: q/k/v and gate/up by output rows (heads), o and down by input columns.
+
+Weights are int4 packed along K (uint8 [N, K/2], element 2j in the low nibble of byte j) with fp16
+scales [N, K/32], the layout `DenseMatrix.from_int4` takes.
+"""
+import torch
+
+from .dense import DenseMatrix, EPI_BF16, EPI_F32, EPI_SWIGLU
+
+GROUP = 32
+
+
+def split_range(n, rank, world, align=1):
+    """[lo, hi) of rank's block when n items are split evenly in units of `align`."""
+    if n % (world * align):
+        raise ValueError(f"{n} does not split into {world} blocks of a multiple of {align}")
+    b = n // world
+    return rank * b, (rank + 1) * b
+
+
+def column_shard(qk, s, rank, world):
+    """Output rows [lo, hi) of an [N, K] int4 matrix."""
+    lo, hi = split_range(qk.shape[0], rank, world)
+    return qk[lo:hi], s[lo:hi]
+
+
+def row_shard(qk, s, rank, world):
+    """Input columns [k0, k1) of an [N, K] int4 matrix, K cut on 32-group boundaries."""
+    K = qk.shape[1] * 2
+    k0, k1 = split_range(K, rank, world, GROUP)
+    return qk[:, k0 // 2:k1 // 2], s[:, k0 // GROUP:k1 // GROUP]
+
+
+def fused_rows_shard(parts, rank, world):
+    """Column shard of several matrices stacked by rows (q | k | v, or gate | up): each part
+    contributes its own rank block, in order. parts: [(qk, s), ...]."""
+    sh = [column_shard(qk, s, rank, world) for qk, s in parts]
+    return torch.cat([q for q, _ in sh]), torch.cat([s for _, s in sh])
+
+
+class TPLinear:
+    """One rank's shard of an int4 projection. kind "column": y = x . W_shard^T (a block of the
+    output); kind "row": y = sum over ranks of x_shard . W_shard^T, all-reduced by `allreduce`
+    (a comm.PeerAllReduce: one launch over NVLink peer memory) or, when only a process group is
+    given, by NCCL."""
+
+    def __init__(self, qk, s, kind, gateup=False, group=None, allreduce=None):
+        assert kind in ("column", "row")
+        self.kind, self.group, self.allreduce = kind, group, allreduce
+        self.m = DenseMatrix.from_int4(qk, s, gateup=gateup)
+        self.N, self.K = self.m.N, self.m.K
+
+    def __call__(self, x, out, epi=EPI_F32, stream=None, reduce=True, out_bf16=None):
+        """out_bf16 (row-parallel): also receive the reduced sum as bf16 (the next projection's
+        input); the peer all-reduce writes it in the same launch."""
+        self.m.mv(x, out=out, epi=epi, stream=stream)
+        if self.kind == "row" and reduce:
+            if self.allreduce is not None:
+                self.allreduce(out, out=out, out_bf16=out_bf16, stream=stream)
+                return out
+            if self.group is not None:
+                torch.distributed.all_reduce(out, group=self.group)
+        if out_bf16 is not None:
+            out_bf16.copy_(out)
+        return out
+
+
+class TPDecoderLayer:
+    """One decoder layer's projections on one rank: q/k/v (column), o (row), gate/up with the
+    SwiGLU epilogue (column), down (row). Attention is not part of the path: o takes this rank's
+    q-projection output (its heads, bf16) as the stand-in for the attention output of those heads.
+    The layer's input x (bf16 [M, hidden]) is the same on every rank; its output (fp32 [M, hidden],
+    all-reduced) too."""
+
+    def __init__(self, qkv, o, gu, dn, nq, group=None, allreduce=None):
+        """qkv / gu: this rank's stacked row blocks (q|k|v, gate|up); o / dn: its K blocks; each an
+        (int4 codes, fp16 scales) pair. nq: this rank's q rows (= o's K block). allreduce: see
+        TPLinear."""
+        self.qkv = TPLinear(*qkv, "column", group=group)
+        self.o = TPLinear(*o, "row", group=group, allreduce=allreduce)
+        self.gu = TPLinear(*gu, "column", gateup=True, group=group)
+        self.dn = TPLinear(*dn, "row", group=group, allreduce=allreduce)
+        self.nq = nq
+        assert self.o.K == nq
+
+    @classmethod
+    def from_full(cls, w, rank, world, group=None, allreduce=None):
+        """w: dict of full matrices (codes, scales) for q, k, v, o, gate, up, down."""
+        nq = split_range(w["q"][0].shape[0], rank, world)
+        return cls(fused_rows_shard([w["q"], w["k"], w["v"]], rank, world), row_shard(*w["o"], rank, world),
+                   fused_rows_shard([w["gate"], w["up"]], rank, world), row_shard(*w["down"], rank, world),
+                   nq[1] - nq[0], group, allreduce)
+
+    def buffers(self, M, device="cuda"):
+        return {"qkv": torch.empty(M, self.qkv.N, device=device, dtype=torch.bfloat16),
+                "h": torch.empty(M, self.o.N, device=device),
+                "x2": torch.empty(M, self.o.N, device=device, dtype=torch.bfloat16),
+                "a": torch.empty(M, self.gu.N // 2, device=device, dtype=torch.bfloat16),
+                "y": torch.empty(M, self.dn.N, device=device)}
+
+    def __call__(self, x, b, stream=None, y_bf16=None):
+        """x: bf16 [M, hidden]; b: buffers(); returns b["y"] (fp32, summed over ranks). y_bf16: also
+        receive the output as bf16 (the next layer's input)."""
+        self.qkv(x, b["qkv"], epi=EPI_BF16, stream=stream)
+        self.o(b["qkv"][:, :self.nq], b["h"], stream=stream, out_bf16=b["x2"])
+        self.gu(b["x2"], b["a"], epi=EPI_SWIGLU, stream=stream)
+        self.dn(b["a"], b["y"], stream=stream, out_bf16=y_bf16)
+        return b["y"]
+
+
+def dense_layer_shapes(hidden, inter, q_heads, kv_heads, head_dim=128):
+    """(name, N, K) of a decoder layer's projections."""
+    q, kv = q_heads * head_dim, kv_heads * head_dim
+    return [("q", q, hidden), ("k", kv, hidden), ("v", kv, hidden), ("o", hidden, q),
+            ("gate", inter, hidden), ("up", inter, hidden), ("down", hidden, inter)]

@@ -231,3 +231,49 @@ def test_moe_ffn_dev_is_deterministic(config4):
     b = ffn(x, ids, w)
     torch.cuda.synchronize()
     assert torch.equal(a, b)
+
+
+# ------------------------------------------------------------------ expert parallelism
+@pytest.mark.parametrize("world", [2, 4])
+def test_moe_ffn_expert_shards_sum_to_the_full_layer(world):
+    """Each rank's FFN holds E / world experts; run over every token with the global ids, the
+    shards' outputs (each skipping the slots routed elsewhere) add up to the full layer."""
+    E, H, I, T, k = 32, 1024, 256, 24, 8
+    gq, gs = _bank(E, 2 * I, H, seed=31)
+    dq, ds = _bank(E, H, I, seed=32)
+    full = ExpertFFN(gq, gs, dq, ds)
+    g = torch.Generator(device="cuda").manual_seed(33)
+    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+    wr = (torch.randn(E, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    ids, w = route(x, wr, k)
+    y_full = full(x, ids, w)
+    el = E // world
+    y = torch.zeros(T, H, device="cuda")
+    for r in range(world):
+        sh = ExpertFFN(gq[r * el:(r + 1) * el], gs[r * el:(r + 1) * el], dq[r * el:(r + 1) * el],
+                       ds[r * el:(r + 1) * el])
+        y += sh(x, ids, w, e0=r * el)
+    torch.cuda.synchronize()
+    assert L.load().onpu_check_device() == 0, L.last_error()
+    # the shards' GEMVs split their rows differently from the full run's: fp32 sums differ in the
+    # last bits and may flip a bf16 rounding of an activation, ~1e-5 relative
+    err = ((y - y_full).norm() / y_full.norm()).item()
+    assert err <= 1e-4, err
+    ref = _ffn_oracle(x.float().cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy(), gq.cpu().numpy(),
+                      gs.cpu().numpy(), dq.cpu().numpy(), ds.cpu().numpy())
+    _assert_close(y.cpu().numpy(), ref)
+
+
+def test_moe_ffn_expert_shard_with_no_routed_tokens():
+    """A shard none of whose experts was chosen contributes exact zeros."""
+    E, H, I, T = 16, 512, 128, 4
+    gq, gs = _bank(E, 2 * I, H, seed=41)
+    dq, ds = _bank(E, H, I, seed=42)
+    sh = ExpertFFN(gq[8:], gs[8:], dq[8:], ds[8:])
+    x = torch.randn(T, H, device="cuda").to(torch.bfloat16)
+    ids = torch.arange(T * 2, dtype=torch.int32, device="cuda").view(T, 2) % 8
+    w = torch.full((T, 2), 0.5, device="cuda")
+    y = sh(x, ids, w, e0=8)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(y).item() == 0
+    assert L.load().onpu_check_device() == 0
