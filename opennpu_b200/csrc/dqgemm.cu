@@ -346,8 +346,12 @@ __global__ void __launch_bounds__(kGThreads, 1)
                     const uint2 sc = lds_v2(sbase + kCodeBytes + rq * 8);
                     uint2 mn = make_uint2(0, 0);
                     if constexpr (FMT == kFmtQ4NX) mn = lds_v2(sbase + kCodeBytes + kScaleBytes + rq * 8);
+                    // lanes of odd rows take the groups in the other order: within each 8-lane
+                    // phase of a 16-byte store, rows rq and rq^1 then hit eight different 16-byte
+                    // units of the swizzled row (no shared-memory bank conflicts)
 #pragma unroll
-                    for (int gi = 0; gi < 2; ++gi) {
+                    for (int k = 0; k < 2; ++k) {
+                        const int gi = k ^ (rq & 1);
                         const uint32_t sp = gi ? sc.y : sc.x;
                         const uint32_t slo = to_f16_bits<FMT>(sp & 0xffffu), shi = to_f16_bits<FMT>(sp >> 16);
                         const uint32_t slo2 = slo | (slo << 16), shi2 = shi | (shi << 16);
