@@ -2,6 +2,7 @@
 #include <cuda_runtime.h>
 
 #include "kernels.h"
+#include "ptx.cuh"
 
 namespace onpu_b200 {
 
@@ -29,6 +30,8 @@ __global__ void f32_to_bf16_kernel(const float *x, int64_t rows, int64_t cols, i
 // deterministic, one thread per output element.
 __global__ void moe_combine_kernel(const float *o, int64_t ldo, int64_t T, int k, int64_t N, const int32_t *ids,
                                    const float *w, const float *bias, float *y, int64_t ldy, int id_lo, int id_hi) {
+    pdl_wait_prerequisites();                              // the expert outputs
+    pdl_launch_dependents();
     const int64_t n = T * N;
     for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -97,8 +100,8 @@ cudaError_t moe_combine_launch(const float *o, int64_t ldo, int64_t T, int k, in
                                const float *w, const float *bias, float *y, int64_t ldy, cudaStream_t stream,
                                int id_lo, int id_hi) {
     if (T * N == 0) return cudaSuccess;
-    moe_combine_kernel<<<grid_for(T * N, 256), 256, 0, stream>>>(o, ldo, T, k, N, ids, w, bias, y, ldy, id_lo, id_hi);
-    return cudaGetLastError();
+    return launch_pdl(moe_combine_kernel, dim3(grid_for(T * N, 256)), dim3(256), 0, stream, o, ldo, T, k, N, ids, w,
+                      bias, y, ldy, id_lo, id_hi);
 }
 
 }  // namespace onpu_b200

@@ -101,6 +101,25 @@ __device__ __forceinline__ void pdl_wait_prerequisites() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Launch with programmatic dependent launch allowed: the kernel may start while the previous one
+// in the stream finishes, so it must call pdl_wait_prerequisites() before touching that kernel's
+// outputs (the small MoE kernels do it first thing).
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // ---------------------------------------------------------------- flags between CTAs
 __device__ __forceinline__ void st_release_gpu(unsigned *p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");

@@ -47,6 +47,8 @@ __global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h
                                                                const uint16_t *wr, int E, int H, int k, int norm,
                                                                int32_t *ids, float *w, float *lg, unsigned *counters) {
     __shared__ int last;
+    pdl_wait_prerequisites();                              // h (and the counters) of earlier kernels
+    pdl_launch_dependents();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRouteTokens;
     const int nt = T - t0 < kRouteTokens ? static_cast<int>(T - t0) : kRouteTokens;
@@ -177,6 +179,8 @@ __global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJo
     extern __shared__ int js[];
     int *cnt = js, *start = cnt + p.E, *jstart = start + p.E, *cursor = jstart + p.E + 1;
     __shared__ int warp_sums[33];
+    pdl_wait_prerequisites();                              // the routed ids
+    pdl_launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     for (int e = tid; e < p.E; e += kJobThreads) {
         cnt[e] = 0;
@@ -254,16 +258,15 @@ __global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJo
 cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream) {
     if (p.TK <= 0) return cudaSuccess;
     const size_t smem = sizeof(int) * (3 * static_cast<size_t>(p.E) + 1 + p.E);
-    expert_jobs_kernel<<<1, kJobThreads, smem, stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(expert_jobs_kernel, dim3(1), dim3(kJobThreads), smem, stream, p);
 }
 
 cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16_t *wr, int E, int H, int k, int norm,
                          int32_t *ids, float *w, float *logits, unsigned *counters, cudaStream_t stream) {
     if (T <= 0) return cudaSuccess;
     const dim3 grid((E + kRouteExperts - 1) / kRouteExperts, static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens));
-    route_kernel<<<grid, kRouterThreads, 0, stream>>>(h, ldh, T, wr, E, H, k, norm, ids, w, logits, counters);
-    return cudaGetLastError();
+    return launch_pdl(route_kernel, grid, dim3(kRouterThreads), 0, stream, h, ldh, T, wr, E, H, k, norm, ids, w, logits,
+                      counters);
 }
 
 int64_t route_counter_slots(int64_t T) { return (T + kRouteTokens - 1) / kRouteTokens; }
