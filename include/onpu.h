@@ -124,6 +124,16 @@ int onpu_check_device(void);
 void *onpu_dense_new_int4(int64_t N, int64_t K, int gateup);
 /* Fill from host (on_device = 0) or device (on_device = 1) arrays; 0 ok, < 0 error. */
 int onpu_dense_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream);
+/* The load-time search quantisers on the GPU: W fp32 [N][ldw] (device, 16-byte
+ * aligned, ldw % 4 == 0, K % 32 == 0) -> codes q [N][K] (0..15), 16-bit (bf16) scales [N][K/32] and,
+ * for q4nx (sym = 0), mins [N][K/32]; bit-exact with onpu_pack's quantisers
+ * (opennpu_core.hpp:103-169, which the reference runs on the host at load time). Asynchronous. */
+int onpu_quantize_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, uint8_t *q, uint16_t *scales,
+                      uint16_t *mins, void *stream);
+/* A dense handle quantised on the GPU from fp32 weights (q4s when sym != 0, else q4nx): the same
+ * codes and scales onpu_pack + onpu_dense_sync produce, without the host pass. gateup as in
+ * onpu_dense_new_int4. Synchronous; NULL on error. */
+void *onpu_dense_new_f32_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, int gateup, void *stream);
 /* Format, N, K, bytes of the GPU-layout matrix. */
 int onpu_dense_info(void *h, int64_t *out4);
 /* y = x . W^T on the GPU, asynchronous on `stream` (NULL: the legacy default stream).

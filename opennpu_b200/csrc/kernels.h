@@ -56,6 +56,12 @@ cudaError_t x_to_f16_launch(const uint16_t *x, int64_t ldx, int M, int K, uint16
 cudaError_t dqgemm_launch(int fmt, int epi, const uint16_t *xh, const DqGemmParams &p, cudaStream_t stream);
 int dqgemm_tile_tokens();
 
+// ---- load-time search quantisers (quant.cu): W fp32 [N][ldw] -> codes [N][K], 16-bit scales and
+// mins [N][K/32] (mins may be null; q4s writes none), bit-exact with host_codec's quant_q4s32 /
+// quant_q4nx32. ldw % 4 == 0, W 16-byte aligned, K % 32 == 0.
+cudaError_t quant_launch(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, uint8_t *q, uint16_t *scales,
+                         uint16_t *mins, cudaStream_t stream);
+
 // ---- one-shot all-reduce over NVLink peer memory (comm.cu)
 constexpr int kCommCtas = 16;
 constexpr int kCommMaxRanks = 8;

@@ -847,6 +847,85 @@ void *onpu_dense_new_int4(int64_t N, int64_t K, int gateup) {
     return d;
 }
 
+int onpu_quantize_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, uint8_t *q, uint16_t *scales,
+                      uint16_t *mins, void *stream) {
+    clear_err();
+    if (N <= 0 || K <= 0 || K % 32 || ldw < K || ldw % 4 || (reinterpret_cast<uintptr_t>(W) & 15) ||
+        (reinterpret_cast<uintptr_t>(q) & 3)) {
+        set_err("onpu_quantize_dev: need K %% 32 == 0, ldw >= K with ldw %% 4 == 0, 16-byte aligned W, 4-byte aligned q");
+        return -1;
+    }
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return -1;
+    }
+    ONPU_CUDA(quant_launch(W, ldw, N, K, sym, q, scales, mins, static_cast<cudaStream_t>(stream)), -1);
+    return 0;
+}
+
+void *onpu_dense_new_f32_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, int gateup, void *stream) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    if (N <= 0 || K <= 0 || K % 32) {
+        set_err("onpu_dense_new_f32_dev: need N > 0 and K %% 32 == 0");
+        return nullptr;
+    }
+    auto s = static_cast<cudaStream_t>(stream);
+    uint8_t *q = nullptr;
+    uint16_t *sc = nullptr, *mn = nullptr;
+    const size_t nq = static_cast<size_t>(N * K), ns = static_cast<size_t>(N * (K / 32));
+    if (cudaMalloc(&q, nq) != cudaSuccess || cudaMalloc(&sc, ns * 2) != cudaSuccess ||
+        cudaMalloc(&mn, ns * 2) != cudaSuccess) {
+        set_err("onpu_dense_new_f32_dev: %s", cudaGetErrorString(cudaGetLastError()));
+        cudaFree(q);
+        cudaFree(sc);
+        return nullptr;
+    }
+    DenseH *d = nullptr;
+    if (onpu_quantize_dev(W, ldw, N, K, sym, q, sc, mn, stream) == 0) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        d = new DenseH;
+        d->fmt = sym ? kFmtQ4S : kFmtQ4NX;
+        d->gateup = gateup != 0;
+        bool ok = alloc_mat(d->mat, N, K, d->fmt, 1);
+        if (ok && d->gateup && !set_gateup_interleave(d->mat)) {
+            set_err("onpu_dense_new_f32_dev: gate/up matrix needs N/2 %% 8 == 0");
+            ok = false;
+        }
+        if (ok) {
+            RepackParams p{};
+            p.src_kind = kSrcCodes;
+            p.src = q;
+            p.scales = sc;
+            p.mins = mn;
+            p.src_row = d->mat.d_row_map;
+            p.N = N;
+            p.K = K;
+            p.fmt = d->fmt;
+            p.dst = d->mat.d_w;
+            cudaError_t e = repack_launch(p, s);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+            if (e != cudaSuccess) {
+                set_err("onpu_dense_new_f32_dev: %s", cudaGetErrorString(e));
+                ok = false;
+            }
+        }
+        if (!ok) {
+            delete d;
+            d = nullptr;
+        }
+    }
+    cudaFree(q);
+    cudaFree(sc);
+    cudaFree(mn);
+    return d;
+}
+
 int onpu_dense_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream) {
     clear_err();
     auto *d = static_cast<DenseH *>(h);

@@ -51,6 +51,18 @@ class DenseMatrix:
         L.check(rc, "onpu_dense_load_int4")
 
     @classmethod
+    def from_float(cls, W, sym=True, gateup=False, stream=None):
+        """fp32 CUDA weights [N, K] quantised on the GPU with the reference's search quantisers
+        (q4s when sym, else q4nx): the codes and scales the host packer would produce."""
+        lib = L.require_device()
+        assert W.is_cuda and W.dtype == torch.float32 and W.dim() == 2 and W.stride(1) == 1
+        N, K = W.shape
+        h = lib.onpu_dense_new_f32_dev(W.data_ptr(), W.stride(0), N, K, int(sym), int(gateup), _stream_ptr(stream))
+        if not h:
+            raise L.OnpuError(f"onpu_dense_new_f32_dev: {L.last_error()}")
+        return cls(h, N, K, FMT_Q4S if sym else FMT_Q4NX, gateup)
+
+    @classmethod
     def from_stream(cls, N, K, sym, packed):
         """The reference upload protocol: onpu_dense_new2 + fill onpu_dense_buf + onpu_dense_sync."""
         lib = L.require_device()
