@@ -111,6 +111,8 @@ void onpu_quant_dequant(const float *W, int64_t N, int64_t K, int sym, float *ou
 #define ONPU_EPI_BF16 1   /* y bf16                                                    */
 #define ONPU_EPI_SWIGLU 2 /* y[i] = bf16(silu(acc[gate i]) * acc[up i]); needs a gate/up */
                           /* matrix created with onpu_dense_new_int4(..., gateup = 1)     */
+#define ONPU_EPI_PAIRSUM 3 /* y[i] = acc[row i] + acc[residual of row i], fp32; needs a    */
+                           /* matrix from onpu_dense_new_residual_f32_dev                 */
 
 /* Last error message of this thread (NULL if the last failing-capable call succeeded). */
 const char *onpu_last_error(void);
@@ -134,6 +136,13 @@ int onpu_quantize_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym
  * codes and scales onpu_pack + onpu_dense_sync produce, without the host pass. gateup as in
  * onpu_dense_new_int4. Synchronous; NULL on error. */
 void *onpu_dense_new_f32_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, int gateup, void *stream);
+/* The two-pass (~8-bit) mode of the reference's NPULinearGroup(residual=True)
+ * (opennpu/native/npu4/model.py:793-833): rows [W; W - quant_dequant(W)], each pass quantised with
+ * the search quantiser, the two halves added after the product. Here both halves are quantised on
+ * the GPU from fp32 W [N][ldw] (N % 8 == 0) and stored interleaved per 16-row strip, so one GEMV
+ * launch with ONPU_EPI_PAIRSUM (onpu_dense_mv_dev, output [rows][N] fp32) streams both and adds
+ * them in its epilogue. Synchronous; NULL on error. */
+void *onpu_dense_new_residual_f32_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, void *stream);
 /* Format, N, K, bytes of the GPU-layout matrix. */
 int onpu_dense_info(void *h, int64_t *out4);
 /* y = x . W^T on the GPU, asynchronous on `stream` (NULL: the legacy default stream).

@@ -50,11 +50,13 @@ using namespace gemv_core;
 template <int EPI>
 __device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, int r, int yr, float v_lo, float v_hi) {
     if (yr < 0) return;
-    if constexpr (EPI == kEpiSwiGLU) {
-        const int i = g * (kRowGroup / 2) + s * 8 + r;       // gate row r, up row r+8 of the strip
-        if (i < p.N / 2)
-            reinterpret_cast<__nv_bfloat16 *>(p.y)[static_cast<int64_t>(yr) * p.ldy + i] =
-                __float2bfloat16_rn(silu_f(v_lo) * v_hi);
+    if constexpr (EPI == kEpiSwiGLU || EPI == kEpiPairSum) {
+        const int i = g * (kRowGroup / 2) + s * 8 + r;       // row r and row r+8 of the strip pair up
+        if (i < p.N / 2) {
+            const int64_t o = static_cast<int64_t>(yr) * p.ldy + i;
+            if constexpr (EPI == kEpiSwiGLU) reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(silu_f(v_lo) * v_hi);
+            else reinterpret_cast<float *>(p.y)[o] = v_lo + v_hi;
+        }
     } else {
         const int row = g * kRowGroup + s * kStripRows + r;
 #pragma unroll
@@ -442,6 +444,7 @@ cudaError_t dispatch_epi_ci(int epi, const GemvParams &p, int smem, cudaStream_t
         case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, CI>::launch(p, smem, s, pdl);
         case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16, CI>::launch(p, smem, s, pdl);
         case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, CI>::launch(p, smem, s, pdl);
+        case kEpiPairSum: return GemvKernel<FMT, NT, kEpiPairSum, CI>::launch(p, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

@@ -77,6 +77,7 @@ enum GemvEpilogue : int {
     kEpiF32 = 0,      // y[yrow][n] = acc (fp32)
     kEpiBF16 = 1,     // y[yrow][n] = bf16(acc)
     kEpiSwiGLU = 2,   // strip rows 0-7 gate, 8-15 up: y[yrow][i] = bf16(silu(gate_i) * up_i)
+    kEpiPairSum = 3,  // strip rows 0-7 a row, 8-15 its residual: y[yrow][i] = row_i + residual_i (fp32)
 };
 
 // GEMV tracing: per CTA, ns stamps of kernel entry, producer's first copy issued, consumers past

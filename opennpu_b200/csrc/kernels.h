@@ -61,6 +61,9 @@ int dqgemm_tile_tokens();
 // quant_q4nx32. ldw % 4 == 0, W 16-byte aligned, K % 32 == 0.
 cudaError_t quant_launch(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, uint8_t *q, uint16_t *scales,
                          uint16_t *mins, cudaStream_t stream);
+// R [N][K] = W - the dequantised codes (the host's rounding), for the two-pass residual rows
+cudaError_t residual_launch(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, const uint8_t *q,
+                            const uint16_t *scales, const uint16_t *mins, float *R, cudaStream_t stream);
 
 // ---- one-shot all-reduce over NVLink peer memory (comm.cu)
 constexpr int kCommCtas = 16;

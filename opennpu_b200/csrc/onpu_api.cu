@@ -243,7 +243,7 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     p.ldx = ldx;
     p.y = y;
     p.ldy = ldy;
-    p.row_map = epi == kEpiSwiGLU ? nullptr : m.d_row_map;
+    p.row_map = epi == kEpiSwiGLU || epi == kEpiPairSum ? nullptr : m.d_row_map;
     p.part = c.d_part;
     p.counters = c.d_cnt;
     p.err = c.d_err;
@@ -371,6 +371,7 @@ struct DenseH {
     GpuMat mat;
     uint8_t *h_buf = nullptr;     // pinned stream-order upload buffer
     bool gateup = false;
+    bool residual = false;        // rows [W; W - dequant(W)] interleaved per strip (two-pass mode)
     std::map<int64_t, JobSet> jobs;
     ~DenseH() {
         if (h_buf) cudaFreeHost(h_buf);
@@ -926,6 +927,69 @@ void *onpu_dense_new_f32_dev(const float *W, int64_t ldw, int64_t N, int64_t K, 
     return d;
 }
 
+void *onpu_dense_new_residual_f32_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, void *stream) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    if (N <= 0 || N % 8 || K <= 0 || K % 32 || ldw < K || ldw % 4 || (reinterpret_cast<uintptr_t>(W) & 15)) {
+        set_err("onpu_dense_new_residual_f32_dev: need N %% 8 == 0, K %% 32 == 0, ldw >= K with ldw %% 4 == 0, "
+                "16-byte aligned W");
+        return nullptr;
+    }
+    auto s = static_cast<cudaStream_t>(stream);
+    const int64_t G = K / 32;
+    uint8_t *q = nullptr;
+    uint16_t *sc = nullptr, *mn = nullptr;
+    float *R = nullptr;
+    DenseH *d = nullptr;
+    cudaError_t e = cudaMalloc(&q, static_cast<size_t>(2 * N * K));
+    if (e == cudaSuccess) e = cudaMalloc(&sc, static_cast<size_t>(2 * N * G) * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&mn, static_cast<size_t>(2 * N * G) * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&R, static_cast<size_t>(N * K) * 4);
+    // pass 1: W; residual R = W - what pass 1 makes of W; pass 2: R (rows N .. 2N - 1 of the codes)
+    if (e == cudaSuccess) e = quant_launch(W, ldw, N, K, sym, q, sc, mn, s);
+    if (e == cudaSuccess) e = residual_launch(W, ldw, N, K, sym, q, sc, mn, R, s);
+    if (e == cudaSuccess) e = quant_launch(R, K, N, K, sym, q + N * K, sc + N * G, mn + N * G, s);
+    if (e == cudaSuccess) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        d = new DenseH;
+        d->fmt = sym ? kFmtQ4S : kFmtQ4NX;
+        d->residual = true;
+        // GPU strip rows 0-7: rows 8s..8s+7 of W, rows 8-15: the same rows of R (as gate/up pairs)
+        if (!alloc_mat(d->mat, 2 * N, K, d->fmt, 1) || !set_gateup_interleave(d->mat)) {
+            if (!onpu_last_error()) set_err("onpu_dense_new_residual_f32_dev: allocation failed");
+            delete d;
+            d = nullptr;
+        } else {
+            RepackParams p{};
+            p.src_kind = kSrcCodes;
+            p.src = q;
+            p.scales = sc;
+            p.mins = mn;
+            p.src_row = d->mat.d_row_map;
+            p.N = 2 * N;
+            p.K = K;
+            p.fmt = d->fmt;
+            p.dst = d->mat.d_w;
+            e = repack_launch(p, s);
+        }
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    cudaFree(q);
+    cudaFree(sc);
+    cudaFree(mn);
+    cudaFree(R);
+    if (e != cudaSuccess) {
+        set_err("onpu_dense_new_residual_f32_dev: %s", cudaGetErrorString(e));
+        delete d;
+        return nullptr;
+    }
+    return d;
+}
+
 int onpu_dense_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream) {
     clear_err();
     auto *d = static_cast<DenseH *>(h);
@@ -995,7 +1059,8 @@ int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
     clear_err();
     auto *d = static_cast<DenseH *>(h);
     if (rows <= 0) return 0;
-    if (epi < kEpiF32 || epi > kEpiSwiGLU || (epi == kEpiSwiGLU && !d->gateup)) {
+    if (epi < kEpiF32 || epi > kEpiPairSum || (epi == kEpiSwiGLU && !d->gateup) ||
+        (epi == kEpiPairSum && !d->residual)) {
         set_err("onpu_dense_mv_dev: bad epilogue %d for this matrix", epi);
         return -1;
     }
@@ -1007,7 +1072,7 @@ int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y
         set_err("onpu_dense_mv_dev: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
         return -1;
     }
-    if (ldy < (epi == kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
+    if (ldy < (epi >= kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
         set_err("onpu_dense_mv_dev: y row stride %lld is shorter than the output row", static_cast<long long>(ldy));
         return -1;
     }

@@ -159,7 +159,28 @@ __global__ void __launch_bounds__(128) quant_kernel(const float *W, int64_t ldw,
     if (mins) mins[row * G + g] = sym ? uint16_t{0} : m;
 }
 
+// R = W - dequant(codes) with the host's rounding: (q - 8) * d, or q * s + m (a product then a sum,
+// not contracted), then one subtraction - the residual rows of the two-pass (~8-bit) mode
+__global__ void residual_kernel(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, const uint8_t *q,
+                                const uint16_t *scales, const uint16_t *mins, float *R) {
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= N * K) return;
+    const int64_t row = i / K, col = i - row * K, gidx = row * (K / 32) + col / 32;
+    const float qf = static_cast<float>(q[i]);
+    const float dq = sym ? mul(sub(qf, 8.0f), from_bf16(scales[gidx]))
+                         : add(mul(qf, from_bf16(scales[gidx])), from_bf16(mins[gidx]));
+    R[i] = sub(W[row * ldw + col], dq);
+}
+
 }  // namespace
+
+cudaError_t residual_launch(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, const uint8_t *q,
+                            const uint16_t *scales, const uint16_t *mins, float *R, cudaStream_t stream) {
+    const int64_t n = N * K;
+    if (n <= 0) return cudaSuccess;
+    residual_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, stream>>>(W, ldw, N, K, sym, q, scales, mins, R);
+    return cudaGetLastError();
+}
 
 cudaError_t quant_launch(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, uint8_t *q, uint16_t *scales,
                          uint16_t *mins, cudaStream_t stream) {

@@ -10,7 +10,7 @@ import torch
 
 from . import libonpu as L
 
-EPI_F32, EPI_BF16, EPI_SWIGLU = 0, 1, 2
+EPI_F32, EPI_BF16, EPI_SWIGLU, EPI_PAIRSUM = 0, 1, 2, 3
 FMT_Q4NX, FMT_Q4S, FMT_Q4F16 = 0, 1, 2
 
 
@@ -20,8 +20,8 @@ def _stream_ptr(stream=None):
 
 
 class DenseMatrix:
-    def __init__(self, handle, N, K, fmt, gateup=False):
-        self.h, self.N, self.K, self.fmt, self.gateup = handle, N, K, fmt, gateup
+    def __init__(self, handle, N, K, fmt, gateup=False, residual=False):
+        self.h, self.N, self.K, self.fmt, self.gateup, self.residual = handle, N, K, fmt, gateup, residual
         self.Kg = self.info()[2]          # K of the GPU layout (K rounded up to 32)
 
     # ---------------------------------------------------------------- construction
@@ -63,6 +63,19 @@ class DenseMatrix:
         return cls(h, N, K, FMT_Q4S if sym else FMT_Q4NX, gateup)
 
     @classmethod
+    def from_float_residual(cls, W, sym=True, stream=None):
+        """The two-pass (~8-bit) form of fp32 CUDA weights [N, K] (N % 8 == 0): W and its
+        quantisation residual, each quantised on the GPU, in one matrix of 2N GPU rows; ``mv`` with
+        EPI_PAIRSUM (its default for these) returns the [M, N] sum of the two passes."""
+        lib = L.require_device()
+        assert W.is_cuda and W.dtype == torch.float32 and W.dim() == 2 and W.stride(1) == 1
+        N, K = W.shape
+        h = lib.onpu_dense_new_residual_f32_dev(W.data_ptr(), W.stride(0), N, K, int(sym), _stream_ptr(stream))
+        if not h:
+            raise L.OnpuError(f"onpu_dense_new_residual_f32_dev: {L.last_error()}")
+        return cls(h, 2 * N, K, FMT_Q4S if sym else FMT_Q4NX, residual=True)
+
+    @classmethod
     def from_stream(cls, N, K, sym, packed):
         """The reference upload protocol: onpu_dense_new2 + fill onpu_dense_buf + onpu_dense_sync."""
         lib = L.require_device()
@@ -98,14 +111,18 @@ class DenseMatrix:
     def prepare(self, rows):
         L.check(L.load().onpu_dense_prepare(self.h, rows), "onpu_dense_prepare")
 
-    def mv(self, x, out=None, epi=EPI_F32, stream=None):
-        """x: bf16 CUDA [M, K] (row stride % 8 == 0) -> [M, N] fp32 (EPI_F32), bf16 (EPI_BF16) or
-        [M, N/2] bf16 silu(gate) * up (EPI_SWIGLU)."""
+    def mv(self, x, out=None, epi=None, stream=None):
+        """x: bf16 CUDA [M, K] (row stride % 8 == 0) -> [M, N] fp32 (EPI_F32), bf16 (EPI_BF16),
+        [M, N/2] bf16 silu(gate) * up (EPI_SWIGLU) or [M, N/2] fp32 row + residual (EPI_PAIRSUM,
+        the default of a two-pass matrix; EPI_F32 otherwise)."""
         assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+        if epi is None:
+            epi = EPI_PAIRSUM if self.residual else EPI_F32
         M = x.shape[0]
         if out is None:
-            ncol = self.N // 2 if epi == EPI_SWIGLU else self.N
-            out = torch.empty(M, ncol, device=x.device, dtype=torch.float32 if epi == EPI_F32 else torch.bfloat16)
+            ncol = self.N // 2 if epi in (EPI_SWIGLU, EPI_PAIRSUM) else self.N
+            fp32 = epi in (EPI_F32, EPI_PAIRSUM)
+            out = torch.empty(M, ncol, device=x.device, dtype=torch.float32 if fp32 else torch.bfloat16)
         rc = L.load().onpu_dense_mv_dev(self.h, x.data_ptr(), x.stride(0), M, out.data_ptr(), out.stride(0), epi,
                                         _stream_ptr(stream))
         L.check(rc, "onpu_dense_mv_dev")

@@ -58,6 +58,7 @@ SIGNATURES = {
     "onpu_dense_info": (I32, [P, I64P]),
     "onpu_quantize_dev": (I32, [P, I64, I64, I64, I32, P, P, P, P]),
     "onpu_dense_new_f32_dev": (P, [P, I64, I64, I64, I32, I32, P]),
+    "onpu_dense_new_residual_f32_dev": (P, [P, I64, I64, I64, I32, P]),
     "onpu_dense_prepare": (I32, [P, I64]),
     "onpu_dense_mv_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),

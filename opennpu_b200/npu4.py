@@ -140,15 +140,17 @@ class NPULinearGroup:
     """Sibling Linear layers reading the same input, packed as one matrix: the first call computes
     all of them for that input, the others take their slice (model.py:789-862)."""
 
-    def __init__(self, names, weights, sizes=None, K=None, sym=False, packed=None):
+    def __init__(self, names, weights, sizes=None, K=None, sym=False, packed=None, residual=False):
         """weights: the matrices (or a callable returning them). packed: already-packed stream-order
-        bytes (skips quantisation)."""
+        bytes (skips quantisation). residual: rows [W; W - quant_dequant(W)] (two 4-bit passes,
+        ~8-bit precision), the two halves added after each product (model.py:793-833)."""
         self.names = names
         self.sizes = sizes or [w.shape[0] for w in weights]
         self.N1 = sum(self.sizes)
+        self.residual = residual
         if K is None:
             K = (weights() if callable(weights) else weights)[0].shape[1]
-        self.m = Mat(self.N1, K, NC, sym)
+        self.m = Mat(self.N1 * (2 if residual else 1), K, NC, sym)
         lib = clib()
         check_geometry(self.m)
         self.ch = lib.onpu_dense_new2(self.m.N, self.m.K, int(sym))
@@ -158,6 +160,8 @@ class NPULinearGroup:
         if packed is None:
             ws = weights() if callable(weights) else weights
             W = np.ascontiguousarray(np.concatenate(ws) if len(ws) > 1 else ws[0], np.float32)
+            if residual:
+                W = np.concatenate([W, W - quant_dequant(W, sym)])
             packed = self.m.pack(W, threads=8)
         buf[:] = packed
         lib.onpu_dense_sync(self.ch)
@@ -181,6 +185,8 @@ class NPULinearGroup:
             err = L.last_error()
             if err:
                 raise L.OnpuError(err)
+            if self.residual:
+                self._y = self._y[:, :self.N1] + self._y[:, self.N1:]
             self._key = (x, x._version)
         o = sum(self.sizes[:i])
         return self._y[:, o:o + self.sizes[i]]
