@@ -209,6 +209,15 @@ int onpu_comm_ipc_handle(void *comm, void *out64);
 int onpu_comm_open(void *comm, const void *handles);
 int onpu_comm_allreduce(void *comm, const float *src, float *dst, void *dst_bf16, int64_t n, void *stream);
 void onpu_comm_free(void *comm);
+/* The row-parallel projection and its all-reduce fused (no reference counterpart): y / y_bf16
+ * (either may be NULL) = the sum over ranks of x . W_rank^T, rows x N fp32 / bf16, where W_rank is
+ * this rank's K block (dense handle h, no gate/up or residual rows) and comm an opened
+ * onpu_comm handle with cap >= rows x N. The GEMV's epilogue stores every finished output, paired
+ * with the call number in one 8-byte word, straight into every rank's buffer over NVLink while the
+ * rest of the matrix is still streaming; a second small launch waits for all ranks' words and adds
+ * them in rank order. Same call-sequence rule as onpu_comm_allreduce. 0 ok, < 0 error. */
+int onpu_dense_mv_allreduce_dev(void *h, void *comm, const void *x, int64_t ldx, int64_t rows, float *y,
+                                void *y_bf16, void *stream);
 /* ---- GEMV chains: a decode step's dense GEMVs recorded once on fixed device buffers and run as
  * ONE persistent launch (the GPU analogue of the reference's instruction stream per call,
  * llama/ggml-opennpu/opennpu_core.hpp:418-505, and of onpu_ffn_run's gate_up -> act -> down

@@ -1,6 +1,9 @@
 // One-shot all-reduce of small fp32 vectors between the GPUs of one node over NVLink peer memory
 // (tensor-parallel decode: the [M, hidden] partial outputs of the row-parallel o and down
 // projections, 20-160 KB), with the sum also written as bf16 (the next projection's input).
+// The send half can instead be the row-parallel GEMV's own epilogue (gemv.cu, kEpiPeer): its
+// finished rows go to the peers while the rest of the matrix is still streaming, and this kernel
+// only receives and adds (comm_reduce_launch).
 //
 // Every rank owns one buffer (cudaMalloc, shared with the peers through CUDA IPC handles):
 //   slots[2][world][cap] of 8-byte words {fp32 value, call number} | calls[kCommCtas] u32
@@ -38,6 +41,7 @@ struct CommParams {
     __nv_bfloat16 *dst_bf16;         // the sum as bf16 [n] (may be null)
     int64_t n;
     int *err;
+    int send;                        // 0: the values were sent by a GEMV epilogue; only receive
 };
 
 __device__ __forceinline__ void st_word(uint2 *p, uint32_t v, uint32_t tag) {
@@ -60,10 +64,11 @@ __global__ void __launch_bounds__(kCommThreads) comm_allreduce_kernel(const Comm
     __syncthreads();
     const uint32_t c = call;
     const int64_t set = static_cast<int64_t>(c & 1u) * p.world;
-    for (int64_t i = lo + threadIdx.x; i < hi; i += kCommThreads) {
-        const uint32_t v = __float_as_uint(p.src[i]);
-        for (int d = 0; d < p.world; ++d) st_word(p.bufs[d] + (set + p.rank) * p.cap + i, v, c);
-    }
+    if (p.send)
+        for (int64_t i = lo + threadIdx.x; i < hi; i += kCommThreads) {
+            const uint32_t v = __float_as_uint(p.src[i]);
+            for (int d = 0; d < p.world; ++d) st_word(p.bufs[d] + (set + p.rank) * p.cap + i, v, c);
+        }
     for (int64_t i = lo + threadIdx.x; i < hi; i += kCommThreads) {
         float acc = 0.f;
         for (int s = 0; s < p.world; ++s) {
@@ -109,6 +114,25 @@ cudaError_t comm_allreduce_launch(void *const *bufs, int rank, int world, int64_
     p.dst_bf16 = static_cast<__nv_bfloat16 *>(dst_bf16);
     p.n = n;
     p.err = err;
+    p.send = 1;
+    comm_allreduce_kernel<<<kCommCtas, kCommThreads, 0, stream>>>(p);
+    return cudaGetLastError();
+}
+
+cudaError_t comm_reduce_launch(void *const *bufs, int rank, int world, int64_t cap, float *dst, void *dst_bf16,
+                               int64_t n, int *err, cudaStream_t stream) {
+    if (n <= 0) return cudaSuccess;
+    if (world < 1 || world > kCommMaxRanks || n > cap) return cudaErrorInvalidValue;
+    CommParams p{};
+    for (int r = 0; r < world; ++r) p.bufs[r] = static_cast<uint2 *>(bufs[r]);
+    p.rank = rank;
+    p.world = world;
+    p.cap = cap;
+    p.dst = dst;
+    p.dst_bf16 = static_cast<__nv_bfloat16 *>(dst_bf16);
+    p.n = n;
+    p.err = err;
+    p.send = 0;
     comm_allreduce_kernel<<<kCommCtas, kCommThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }

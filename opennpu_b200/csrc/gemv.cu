@@ -57,6 +57,24 @@ __device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, in
             if constexpr (EPI == kEpiSwiGLU) reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(silu_f(v_lo) * v_hi);
             else reinterpret_cast<float *>(p.y)[o] = v_lo + v_hi;
         }
+    } else if constexpr (EPI == kEpiPeer) {
+        // row-parallel projection: each finished value goes straight to every rank's all-reduce
+        // buffer as one 8-byte {value, call number} word (the receive side waits on the number)
+        const uint32_t call = __ldcg(p.peer_calls) + 1u;
+        const int64_t set = static_cast<int64_t>(call & 1u) * p.peer_world;
+        const int row = g * kRowGroup + s * kStripRows + r;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int rr = row + 8 * h;
+            if (rr < p.N) {
+                const int64_t e = static_cast<int64_t>(yr) * p.ldy + rr;
+                const uint32_t v = __float_as_uint(h ? v_hi : v_lo);
+                for (int d = 0; d < p.peer_world; ++d) {
+                    uint2 *w = static_cast<uint2 *>(p.peer[d]) + (set + p.peer_rank) * p.peer_cap + e;
+                    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(w), "r"(v), "r"(call) : "memory");
+                }
+            }
+        }
     } else {
         const int row = g * kRowGroup + s * kStripRows + r;
 #pragma unroll
@@ -445,6 +463,7 @@ cudaError_t dispatch_epi_ci(int epi, const GemvParams &p, int smem, cudaStream_t
         case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16, CI>::launch(p, smem, s, pdl);
         case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, CI>::launch(p, smem, s, pdl);
         case kEpiPairSum: return GemvKernel<FMT, NT, kEpiPairSum, CI>::launch(p, smem, s, pdl);
+        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, CI>::launch(p, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }

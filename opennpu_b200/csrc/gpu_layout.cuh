@@ -78,12 +78,15 @@ enum GemvEpilogue : int {
     kEpiBF16 = 1,     // y[yrow][n] = bf16(acc)
     kEpiSwiGLU = 2,   // strip rows 0-7 gate, 8-15 up: y[yrow][i] = bf16(silu(gate_i) * up_i)
     kEpiPairSum = 3,  // strip rows 0-7 a row, 8-15 its residual: y[yrow][i] = row_i + residual_i (fp32)
+    kEpiPeer = 4,     // fp32 y[yrow][n] sent to every rank's all-reduce buffer (8-byte {value, call} words)
 };
 
 // GEMV tracing: per CTA, ns stamps of kernel entry, producer's first copy issued, consumers past
 // griddepcontrol.wait, activations staged, first weight stage arrived, last stage consumed, range
 // flushed (split row groups closed), and the ns the consumers waited for weights in total
 constexpr int kGemvTrace = 8;
+
+constexpr int kPeerMaxRanks = 8;       // ranks of the peer-memory all-reduce (comm.cu)
 
 struct GemvParams {
     const GemvJob *jobs;
@@ -111,6 +114,12 @@ struct GemvParams {
     int xstride;                       // resident: bytes per token row
     int ctab_off;                      // resident: offset table position in the activation region
     int off_bar;                       // shared-memory offset of the mbarriers
+    // kEpiPeer: every output value goes, with the all-reduce call number, into slot [parity][rank]
+    // of each rank's buffer (comm.cu layout); the call number is the buffer's counter + 1
+    void *peer[kPeerMaxRanks];
+    int peer_rank, peer_world;
+    int64_t peer_cap;
+    const uint32_t *peer_calls;
 };
 
 // One link of a GEMV chain: y = x . W^T for m consecutive activation rows, run inside one

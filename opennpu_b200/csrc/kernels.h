@@ -67,7 +67,17 @@ cudaError_t residual_launch(const float *W, int64_t ldw, int64_t N, int64_t K, i
 
 // ---- one-shot all-reduce over NVLink peer memory (comm.cu)
 constexpr int kCommCtas = 16;
-constexpr int kCommMaxRanks = 8;
+constexpr int kCommMaxRanks = kPeerMaxRanks;
+// where a fused row-parallel GEMV sends its outputs: every rank's all-reduce buffer
+struct PeerOut {
+    void *bufs[kCommMaxRanks];
+    int rank, world;
+    int64_t cap;
+};
+// the receive half of comm_allreduce_launch: wait for every rank's words of this call (the senders
+// were the GEMV's kEpiPeer epilogues) and add them in rank order into dst / dst_bf16
+cudaError_t comm_reduce_launch(void *const *bufs, int rank, int world, int64_t cap, float *dst, void *dst_bf16,
+                               int64_t n, int *err, cudaStream_t stream);
 // bytes of one rank's buffer: two slot sets of world x cap 8-byte words, per-CTA call counters
 int64_t comm_buffer_bytes(int world, int64_t cap);
 // bufs[r]: rank r's buffer as mapped in this process (own at [rank]); dst (fp32) and / or dst_bf16

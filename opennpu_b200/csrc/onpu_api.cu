@@ -224,7 +224,7 @@ bool ensure_scratch(Ctx &c, int workers, int ntiles, int counters) {
 // d_njobs: the job count is written on the device by the previous kernel (njobs is its bound)
 int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntiles, int mmax, int epi,
              const uint16_t *x, int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl,
-             const int *d_njobs = nullptr) {
+             const int *d_njobs = nullptr, const PeerOut *peer = nullptr) {
     const int T = njobs * m.gm.row_groups * m.gm.chunks;
     if (T == 0) return 0;
     const GemvLayout lay = gemv_layout(m.gm.fmt, njobs, mmax, m.gm.K);
@@ -250,6 +250,14 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     p.jobs_ready = d_njobs ? 0 : 1;
     p.njobs_dev = d_njobs;
     p.trace = c.gemv_trace && W <= c.gemv_trace_ctas ? c.gemv_trace : nullptr;
+    if (peer) {
+        for (int r = 0; r < peer->world; ++r) p.peer[r] = peer->bufs[r];
+        p.peer_rank = peer->rank;
+        p.peer_world = peer->world;
+        p.peer_cap = peer->cap;
+        p.peer_calls = reinterpret_cast<const uint32_t *>(static_cast<const uint2 *>(peer->bufs[peer->rank]) +
+                                                          2 * static_cast<int64_t>(peer->world) * peer->cap);
+    }
     p.mul[0] = 1u << 28;
     p.mul[1] = 1u << 24;
     p.mul[2] = 1u << 20;
@@ -1829,6 +1837,48 @@ int onpu_comm_open(void *comm, const void *handles) {
         h->bufs[r] = ptr;
         h->mapped[r] = true;
     }
+    return 0;
+}
+
+int onpu_dense_mv_allreduce_dev(void *h, void *comm, const void *x, int64_t ldx, int64_t rows, float *y,
+                                void *y_bf16, void *stream) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    auto *cm = static_cast<CommH *>(comm);
+    if (rows <= 0) return 0;
+    if (d->gateup || d->residual || (d->geo.ok && d->geo.K != d->mat.gm.K)) {
+        set_err("onpu_dense_mv_allreduce_dev: needs a plain matrix (no gate/up or residual rows, K %% 32 == 0)");
+        return -1;
+    }
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < d->mat.gm.K) {
+        set_err("onpu_dense_mv_allreduce_dev: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+        return -1;
+    }
+    const int64_t n = rows * d->mat.gm.N;
+    if (n > cm->cap || (!y && !y_bf16) || (y_bf16 && (reinterpret_cast<uintptr_t>(y_bf16) & 1))) {
+        set_err("onpu_dense_mv_allreduce_dev: rows x N = %lld exceeds the all-reduce buffer (%lld) or no output",
+                static_cast<long long>(n), static_cast<long long>(cm->cap));
+        return -1;
+    }
+    for (int r = 0; r < cm->world; ++r)
+        if (!cm->bufs[r]) {
+            set_err("onpu_dense_mv_allreduce_dev: rank %d's buffer is not mapped (onpu_comm_open)", r);
+            return -1;
+        }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    JobSet *js = dense_jobs(d, rows);
+    if (!js) return -1;
+    PeerOut po{};
+    for (int r = 0; r < cm->world; ++r) po.bufs[r] = cm->bufs[r];
+    po.rank = cm->rank;
+    po.world = cm->world;
+    po.cap = cm->cap;
+    auto s = static_cast<cudaStream_t>(stream);
+    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiPeer, static_cast<const uint16_t *>(x), ldx,
+                 nullptr, d->mat.gm.N, s, pdl_enabled(), nullptr, &po))
+        return -1;
+    ONPU_CUDA(comm_reduce_launch(cm->bufs, cm->rank, cm->world, cm->cap, y, y_bf16, n, c.d_err, s), -1);
     return 0;
 }
 

@@ -75,6 +75,7 @@ SIGNATURES = {
     "onpu_comm_open": (I32, [P, P]),
     "onpu_comm_allreduce": (I32, [P, P, P, P, I64, P]),
     "onpu_comm_free": (None, [P]),
+    "onpu_dense_mv_allreduce_dev": (I32, [P, P, P, I64, I64, P, P, P]),
     "onpu_chain_new": (P, []),
     "onpu_chain_add": (I32, [P, P, P, I64, I64, P, I64, I32, I32]),
     "onpu_chain_info": (I32, [P, I64P]),

@@ -58,7 +58,10 @@ class TPLinear:
 
     def __call__(self, x, out, epi=EPI_F32, stream=None, reduce=True, out_bf16=None):
         """out_bf16 (row-parallel): also receive the reduced sum as bf16 (the next projection's
-        input); the peer all-reduce writes it in the same launch."""
+        input). With the peer all-reduce, the GEMV's epilogue sends its outputs to the peers itself
+        (onpu_dense_mv_allreduce_dev) and the receiving launch writes both outputs."""
+        if self.kind == "row" and reduce and self.allreduce is not None and epi == EPI_F32:
+            return self.allreduce.linear(self.m, x, out=out, out_bf16=out_bf16, stream=stream)
         self.m.mv(x, out=out, epi=epi, stream=stream)
         if self.kind == "row" and reduce:
             if self.allreduce is not None:
