@@ -393,7 +393,9 @@ class MoEStack:
         self.w = torch.empty(layers, T, M_K, device="cuda")
         self.y = torch.empty(layers, T, M_HIDDEN, device="cuda")
         self.bufs = [ep.buffers(T, M_HIDDEN) for _, _, ep in self.layers] if world > 1 else None
-        self.launches_per_step = 5 * layers            # router, job builder, gate_up, down, combine
+        # router (+ job lists), gate_up, down, combine; with expert parallelism the job builder runs
+        # separately (the ids are all-gathered first)
+        self.launches_per_step = (4 if world == 1 else 5) * layers
         self.lib = __import__("opennpu_b200.libonpu", fromlist=["load"]).load()
 
     def step(self, stream):
@@ -403,10 +405,7 @@ class MoEStack:
             if ep is not None:
                 self.y[l].copy_(ep(x, self.bufs[l], stream=stream))
                 continue
-            rc = self.lib.onpu_route_dev(x.data_ptr(), M_HIDDEN, self.T, wr.data_ptr(), M_E, M_HIDDEN, M_K, 1,
-                                         self.ids[l].data_ptr(), self.w[l].data_ptr(), None, sp)
-            assert rc == 0
-            ffn(x, self.ids[l], self.w[l], out=self.y[l], stream=stream)
+            ffn.layer(x, wr, M_K, out=self.y[l], ids=self.ids[l], w=self.w[l], stream=stream)
 
     def algorithmic_bytes(self):
         """Per step and GPU: every layer's router weights and input rows, the int4 bytes of this
@@ -538,8 +537,8 @@ def run_moe(args):
         e2e = {"value": round(T * world / (dt / layers), 1), "unit": "tokens/s",
                "h2d_bytes_per_step": hx.numel() * 2, "d2h_bytes_per_step": hy.numel() * 4,
                "ms_per_step": round(dt * 1e3, 3),
-               "path": "onpu_route_dev + onpu_moe_ffn_dev per layer (no graph), pinned host input/output copies, "
-                       "a host synchronisation per step"}
+               "path": "onpu_moe_layer_dev per layer (EPMoELayer at N > 1; no graph), pinned host input/output "
+                       "copies, a host synchronisation per step"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, sample = cpu_moe_sample(T, seconds=args.cpu_seconds)
@@ -560,7 +559,7 @@ def run_moe(args):
                        "cuda_graph": True},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gbs / hbm, 4), "peak_kind": peak_kind + " (copy bandwidth)",
-                         "traffic": None, "kernel": "whole MoE layer (router, job builder, gate_up + SwiGLU GEMV, "
+                         "traffic": None, "kernel": "whole MoE layer (router + job lists, gate_up + SwiGLU GEMV, "
                                                     "down GEMV, combine)",
                          "bytes_per_step": nbytes},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": work.launches_per_step * args.steps,
@@ -714,7 +713,7 @@ def run_tp(args):
             dt = float(t.item())
         e2e = {"value": round(M / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": hx.numel() * 2,
                "d2h_bytes_per_step": hy.numel() * 4, "ms_per_step": round(dt * 1e3, 3),
-               "path": "TPDecoderLayer stack (onpu_dense_mv_dev + NCCL all-reduce) from a CUDA graph, pinned host "
+               "path": "TPDecoderLayer stack (onpu_dense_mv_dev; row-parallel o/down fused with the peer all-reduce, or NCCL) from a CUDA graph, pinned host "
                        "input/output copies and a host synchronisation per step"}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -187,6 +187,13 @@ void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t 
  * (llama/ggml-opennpu/onpu_api.cpp:261-278). 0 ok, < 0 error. */
 int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
                      float *y, int64_t ldy, void *stream);
+/* The whole MoE layer in four launches: the router (bf16 wr [E][H], H = the FFN's hidden size;
+ * k, norm as in onpu_route_dev) writes ids [T][k] / w [T][k] and, in its last CTA, the expert job
+ * lists; then the gate_up and down grouped GEMVs and the combine, as onpu_moe_ffn_dev. Same results
+ * as onpu_route_dev followed by onpu_moe_ffn_dev (reference.py:71-84), one launch fewer.
+ * 0 ok, < 0 error. */
+int onpu_moe_layer_dev(void *ffn, const void *wr, const void *x, int64_t ldx, int64_t T, int k, int norm, int32_t *ids,
+                       float *w, float *y, int64_t ldy, void *stream);
 /* Expert parallelism: the same layer when this FFN holds only experts e0 .. e0 + E - 1 of a larger
  * pool. ids are global; slots routed to other experts are skipped, so y[t] is this rank's share of
  * the sum (the ranks' shares add up to onpu_moe_ffn_dev's y). No reference counterpart (the

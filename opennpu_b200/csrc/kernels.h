@@ -111,8 +111,11 @@ cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream);
 
 // logits: fp32 [T][E] (output or scratch); counters: route_counter_slots(T) words, zero before the
 // first launch and left zero by every launch
+// jobs (optional): the last token block to finish also builds the expert job lists (as
+// expert_jobs_launch would, from the ids just written), in the same launch
 cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16_t *wr, int E, int H, int k, int norm,
-                         int32_t *ids, float *w, float *logits, unsigned *counters, cudaStream_t stream);
+                         int32_t *ids, float *w, float *logits, unsigned *counters, cudaStream_t stream,
+                         const ExpertJobsParams *jobs = nullptr);
 int64_t route_counter_slots(int64_t T);
 
 // ---- layout conversion (repack.cu)

@@ -1272,8 +1272,15 @@ void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t 
 namespace {
 // e0 >= 0: expert parallelism, the FFN holds experts e0 .. e0 + E - 1 and the other ids are
 // skipped (their slots contribute nothing to y)
+// route: the router runs first, in the same stream, writing ids / w and building the job lists
+// in its last CTA (one launch fewer than routing and expert_jobs_launch separately)
+struct RouteSpec {
+    const uint16_t *wr;
+    int H, norm;
+};
+
 int moe_ffn_dev_impl(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
-                     int64_t e0, float *y, int64_t ldy, void *stream) {
+                     int64_t e0, float *y, int64_t ldy, void *stream, const RouteSpec *route = nullptr) {
     auto *f = static_cast<FfnH *>(ffn);
     if (T <= 0) return 0;
     if (!f || !f->fused || k < 1) {
@@ -1322,7 +1329,15 @@ int moe_ffn_dev_impl(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     jp.err = c.d_err;
     jp.id_base = e0 >= 0 ? static_cast<int>(e0) : 0;
     jp.skip_foreign = e0 >= 0 ? 1 : 0;
-    ONPU_CUDA(expert_jobs_launch(jp, s), -1);
+    if (route) {
+        if (!grow(c.d_rcnt, c.rcnt_cap, route_counter_slots(T), true) || !grow(c.d_rlg, c.rlg_cap, T * E)) return -1;
+        ONPU_CUDA(route_launch(static_cast<const uint16_t *>(x), ldx, T, route->wr, static_cast<int>(E), route->H, k,
+                               route->norm, const_cast<int32_t *>(ids), const_cast<float *>(w), c.d_rlg, c.d_rcnt, s,
+                               &jp),
+                  -1);
+    } else {
+        ONPU_CUDA(expert_jobs_launch(jp, s), -1);
+    }
     const int mmax = static_cast<int>(std::min<int64_t>(T, per_job)), ntiles = mmax > 8 ? 2 : 1;
     // an expert sees each token at most once (the k experts of a token are distinct); the down
     // projection's jobs hold the same slots, so both lists share the bound
@@ -1346,6 +1361,25 @@ int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int
                      float *y, int64_t ldy, void *stream) {
     clear_err();
     return moe_ffn_dev_impl(ffn, x, ldx, T, ids, w, k, -1, y, ldy, stream);
+}
+
+int onpu_moe_layer_dev(void *ffn, const void *wr, const void *x, int64_t ldx, int64_t T, int k, int norm, int32_t *ids,
+                       float *w, float *y, int64_t ldy, void *stream) {
+    clear_err();
+    auto *f = static_cast<FfnH *>(ffn);
+    if (T <= 0) return 0;
+    if (!f || !f->gu) {
+        set_err("onpu_moe_layer_dev: no FFN handle");
+        return -1;
+    }
+    const int64_t E = f->gu->mat.E, H = f->gu->mat.gm.K;
+    if (k < 1 || k > kMaxRouteK || E < k || E > kMaxRouteExperts || H % 8 || (reinterpret_cast<uintptr_t>(wr) & 15)) {
+        set_err("onpu_moe_layer_dev: the router needs 1 <= k <= %d, k <= E <= %d, a 16-byte aligned bf16 [E][H] "
+                "matrix", kMaxRouteK, kMaxRouteExperts);
+        return -1;
+    }
+    const RouteSpec rs{static_cast<const uint16_t *>(wr), static_cast<int>(H), norm};
+    return moe_ffn_dev_impl(ffn, x, ldx, T, ids, w, k, -1, y, ldy, stream, &rs);
 }
 
 int onpu_moe_ffn_dev_ep(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,

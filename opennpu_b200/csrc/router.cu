@@ -38,58 +38,129 @@ __device__ __forceinline__ float dot8(const uint4 a, const uint4 b, float acc) {
     return fmaf(bf16_hi(a.w), bf16_hi(b.w), acc);
 }
 
-// Grid (experts / 8, tokens / 8). Warp w computes the logits of expert 8*bx + w for the CTA's 8
-// tokens (the expert row is loaded once per 8 tokens; every load of a lane's K slices is
-// independent, so the whole row is in flight at once). The last CTA of a token block to finish
-// (counter per token block, reset by that CTA) runs the softmax and top-k of its 8 tokens, one
-// warp per token, with the E probabilities in registers (E <= 256: 8 per lane).
-__global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h, int64_t ldh, int64_t T,
-                                                               const uint16_t *wr, int E, int H, int k, int norm,
-                                                               int32_t *ids, float *w, float *lg, unsigned *counters) {
-    __shared__ int last;
-    pdl_wait_prerequisites();                              // h (and the counters) of earlier kernels
-    pdl_launch_dependents();
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRouteTokens;
-    const int nt = T - t0 < kRouteTokens ? static_cast<int>(T - t0) : kRouteTokens;
-    const int e = blockIdx.x * kRouteExperts + warp;
-    if (e < E) {
-        const uint16_t *wrow = wr + static_cast<int64_t>(e) * H;
-        float acc[kRouteTokens];
+constexpr int kJobThreads = 1024;
+
+// exclusive block-wide scan of one int per thread (any block of whole warps, <= 1024 threads);
+// returns the block total
+__device__ int block_exclusive_scan(int v, int &total, int *warp_sums) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+    int incl = v;
 #pragma unroll
-        for (int n = 0; n < kRouteTokens; ++n) acc[n] = 0.f;
-#pragma unroll 4
-        for (int d = lane * 8; d < H; d += 32 * 8) {
-            const uint4 b = ld_nc_v4(wrow + d);
-            uint4 a[kRouteTokens];
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < nwarps ? warp_sums[lane] : 0, wi = w;
 #pragma unroll
-            for (int n = 0; n < kRouteTokens; ++n)
-                a[n] = n < nt ? ld_nc_v4(h + (t0 + n) * ldh + d) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-            for (int n = 0; n < kRouteTokens; ++n) acc[n] = dot8(a[n], b, acc[n]);
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, wi, o);
+            if (lane >= o) wi += n;
         }
-#pragma unroll
-        for (int n = 0; n < kRouteTokens; ++n) {
-#pragma unroll
-            for (int o = 16; o; o >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], o);
+        warp_sums[lane] = wi - w;                       // exclusive prefix of the warp totals
+        if (lane == 31) warp_sums[32] = wi;
+    }
+    __syncthreads();
+    const int r = warp_sums[warp] + incl - v;
+    total = warp_sums[32];
+    __syncthreads();
+    return r;
+}
+
+// Routed (token, slot) pairs grouped by expert into GEMV jobs of <= per_job tokens, on the device:
+// the grouping of the host builder (ascending expert id, slots in arrival order), so the whole MoE
+// layer runs without a host round trip. One CTA. jobs0 read token rows (slot / k) against bank 0
+// (gate_up), jobs1 read the per-slot activation rows against bank 1 (down); both write per slot.
+// js: 4E + 1 ints of shared memory; the whole block calls this. ids are read through L2 (the router
+// may have written them earlier in the same launch).
+__device__ void build_jobs(const ExpertJobsParams &p, int *js, int *warp_sums) {
+    int *cnt = js, *start = cnt + p.E, *jstart = start + p.E, *cursor = jstart + p.E + 1;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nwarps = nthr >> 5;
+    for (int e = tid; e < p.E; e += nthr) {
+        cnt[e] = 0;
+        cursor[e] = 0;
+    }
+    __syncthreads();
+    for (int64_t i = tid; i < p.TK; i += nthr) {
+        const int e = __ldcg(p.ids + i) - p.id_base;
+        if (e >= 0 && e < p.E) atomicAdd(&cnt[e], 1);
+        else if (!p.skip_foreign) atomicOr(p.err, 8);
+    }
+    __syncthreads();
+    // slot offsets and job offsets per expert (E may exceed the block: scan in pieces)
+    int base_s = 0, base_j = 0;
+    for (int e0 = 0; e0 < p.E; e0 += nthr) {
+        const int e = e0 + tid;
+        const int c = e < p.E ? cnt[e] : 0, nj = (c + p.per_job - 1) / p.per_job;
+        int ts, tj;
+        const int xs = block_exclusive_scan(c, ts, warp_sums);
+        const int xj = block_exclusive_scan(nj, tj, warp_sums);
+        if (e < p.E) {
+            start[e] = base_s + xs;
+            jstart[e] = base_j + xj;
         }
-        if (lane < nt) {
-            float v = acc[0];
-#pragma unroll
-            for (int n = 1; n < kRouteTokens; ++n)
-                if (lane == n) v = acc[n];
-            lg[(t0 + lane) * E + e] = v;
+        base_s += ts;
+        base_j += tj;
+    }
+    if (tid == 0) jstart[p.E] = base_j;
+    __syncthreads();
+    // stable placement: warps in turn claim consecutive places per expert
+    for (int64_t b = 0; b < p.TK; b += nthr) {
+        const int64_t i = b + tid;
+        const int e = i < p.TK ? __ldcg(p.ids + i) - p.id_base : -1;
+        const bool ok = e >= 0 && e < p.E;
+        const unsigned grp = __match_any_sync(0xffffffffu, ok ? e : -1);
+        const int rank = __popc(grp & ((1u << lane) - 1u)), leader = __ffs(grp) - 1;
+        for (int w = 0; w < nwarps; ++w) {
+            if (warp == w && ok) {
+                int pos = 0;
+                if (lane == leader) {
+                    pos = cursor[e];
+                    cursor[e] = pos + __popc(grp);
+                }
+                pos = __shfl_sync(grp, pos, leader);
+                p.order[start[e] + pos + rank] = static_cast<int>(i);
+            }
+            __syncthreads();
         }
     }
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(counters + blockIdx.y, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    if (threadIdx.x == 0) counters[blockIdx.y] = 0u;          // ready for the next launch
-    if (warp >= nt) return;
-    const int64_t t = t0 + warp;
+    const int NJ = jstart[p.E];
+    for (int jb = tid; jb < NJ; jb += nthr) {
+        int lo = 0, hi = p.E;                             // expert e with jstart[e] <= jb < jstart[e + 1]
+        while (hi - lo > 1) {
+            const int mid = (lo + hi) >> 1;
+            if (jstart[mid] <= jb) lo = mid;
+            else hi = mid;
+        }
+        const int e = lo, part = jb - jstart[e], a = start[e] + part * p.per_job;
+        const int m = min(p.per_job, cnt[e] - part * p.per_job);
+        GemvJob *j0 = p.jobs0 + jb, *j1 = p.jobs1 + jb;
+        j0->w = p.w0 + static_cast<int64_t>(e) * p.bytes0;
+        j1->w = p.w1 + static_cast<int64_t>(e) * p.bytes1;
+        j0->m = j1->m = m;
+        for (int n = 0; n < kMaxTokensPerJob; ++n) {
+            const int slot = n < m ? p.order[a + n] : 0;
+            j0->xrow[n] = slot / p.k;
+            j0->yrow[n] = j1->xrow[n] = j1->yrow[n] = slot;
+        }
+    }
+    if (tid == 0) *p.njobs = NJ;
+}
+
+
+__global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJobsParams p) {
+    extern __shared__ int js[];
+    __shared__ int warp_sums[33];
+    pdl_wait_prerequisites();                              // the routed ids
+    pdl_launch_dependents();
+    build_jobs(p, js, warp_sums);
+}
+
+// softmax and top-k of token t, by one warp, from its E logits
+__device__ __forceinline__ void select_top_k(const float *lg, int64_t t, int E, int k, int norm, int32_t *ids, float *w,
+                                             int lane) {
     const float *row = lg + t * E;
     float v[kMaxRouteExperts / 32];
     float mx = -FLT_MAX;
@@ -141,116 +212,72 @@ __global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h
     if (lane < k) w[t * k + lane] = mine / denom;
 }
 
-constexpr int kJobThreads = 1024;
-
-// exclusive block-wide scan of one int per thread (kJobThreads threads); returns the block total
-__device__ int block_exclusive_scan(int v, int &total, int *warp_sums) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    int incl = v;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
-    }
-    if (lane == 31) warp_sums[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-        int w = warp_sums[lane], wi = w;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int n = __shfl_up_sync(0xffffffffu, wi, o);
-            if (lane >= o) wi += n;
-        }
-        warp_sums[lane] = wi - w;                       // exclusive prefix of the warp totals
-        if (lane == 31) warp_sums[32] = wi;
-    }
-    __syncthreads();
-    const int r = warp_sums[warp] + incl - v;
-    total = warp_sums[32];
-    __syncthreads();
-    return r;
-}
-
-// Routed (token, slot) pairs grouped by expert into GEMV jobs of <= per_job tokens, on the device:
-// the grouping of the host builder (ascending expert id, slots in arrival order), so the whole MoE
-// layer runs without a host round trip. One CTA. jobs0 read token rows (slot / k) against bank 0
-// (gate_up), jobs1 read the per-slot activation rows against bank 1 (down); both write per slot.
-__global__ void __launch_bounds__(kJobThreads) expert_jobs_kernel(const ExpertJobsParams p) {
-    extern __shared__ int js[];
-    int *cnt = js, *start = cnt + p.E, *jstart = start + p.E, *cursor = jstart + p.E + 1;
+// Grid (experts / 8, tokens / 8). Warp w computes the logits of expert 8*bx + w for the CTA's 8
+// tokens (the expert row is loaded once per 8 tokens; every load of a lane's K slices is
+// independent, so the whole row is in flight at once). The last CTA of a token block to finish
+// (counter per token block, reset by that CTA) runs the softmax and top-k of its 8 tokens, one
+// warp per token, with the E probabilities in registers (E <= 256: 8 per lane).
+__global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h, int64_t ldh, int64_t T,
+                                                               const uint16_t *wr, int E, int H, int k, int norm,
+                                                               int32_t *ids, float *w, float *lg, unsigned *counters,
+                                                               const ExpertJobsParams jp) {
+    __shared__ int last;
     __shared__ int warp_sums[33];
-    pdl_wait_prerequisites();                              // the routed ids
+    extern __shared__ int js[];
+    pdl_wait_prerequisites();                              // h (and the counters) of earlier kernels
     pdl_launch_dependents();
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    for (int e = tid; e < p.E; e += kJobThreads) {
-        cnt[e] = 0;
-        cursor[e] = 0;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRouteTokens;
+    const int nt = T - t0 < kRouteTokens ? static_cast<int>(T - t0) : kRouteTokens;
+    const int e = blockIdx.x * kRouteExperts + warp;
+    if (e < E) {
+        const uint16_t *wrow = wr + static_cast<int64_t>(e) * H;
+        float acc[kRouteTokens];
+#pragma unroll
+        for (int n = 0; n < kRouteTokens; ++n) acc[n] = 0.f;
+#pragma unroll 4
+        for (int d = lane * 8; d < H; d += 32 * 8) {
+            const uint4 b = ld_nc_v4(wrow + d);
+            uint4 a[kRouteTokens];
+#pragma unroll
+            for (int n = 0; n < kRouteTokens; ++n)
+                a[n] = n < nt ? ld_nc_v4(h + (t0 + n) * ldh + d) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int n = 0; n < kRouteTokens; ++n) acc[n] = dot8(a[n], b, acc[n]);
+        }
+#pragma unroll
+        for (int n = 0; n < kRouteTokens; ++n) {
+#pragma unroll
+            for (int o = 16; o; o >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], o);
+        }
+        if (lane < nt) {
+            float v = acc[0];
+#pragma unroll
+            for (int n = 1; n < kRouteTokens; ++n)
+                if (lane == n) v = acc[n];
+            lg[(t0 + lane) * E + e] = v;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(counters + blockIdx.y, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x == 0) counters[blockIdx.y] = 0u;          // ready for the next launch
+    if (warp < nt) select_top_k(lg, t0 + warp, E, k, norm, ids, w, lane);
+    if (jp.TK <= 0) return;
+    // the job lists too: the last token block to finish groups every slot by expert
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        last = atomicAdd(counters + gridDim.y, 1u) == gridDim.y - 1;
+        if (last) counters[gridDim.y] = 0u;
     }
     __syncthreads();
-    for (int64_t i = tid; i < p.TK; i += kJobThreads) {
-        const int e = p.ids[i] - p.id_base;
-        if (e >= 0 && e < p.E) atomicAdd(&cnt[e], 1);
-        else if (!p.skip_foreign) atomicOr(p.err, 8);
-    }
-    __syncthreads();
-    // slot offsets and job offsets per expert (E may exceed the block: scan in pieces)
-    int base_s = 0, base_j = 0;
-    for (int e0 = 0; e0 < p.E; e0 += kJobThreads) {
-        const int e = e0 + tid;
-        const int c = e < p.E ? cnt[e] : 0, nj = (c + p.per_job - 1) / p.per_job;
-        int ts, tj;
-        const int xs = block_exclusive_scan(c, ts, warp_sums);
-        const int xj = block_exclusive_scan(nj, tj, warp_sums);
-        if (e < p.E) {
-            start[e] = base_s + xs;
-            jstart[e] = base_j + xj;
-        }
-        base_s += ts;
-        base_j += tj;
-    }
-    if (tid == 0) jstart[p.E] = base_j;
-    __syncthreads();
-    // stable placement: warps in turn claim consecutive places per expert
-    for (int64_t b = 0; b < p.TK; b += kJobThreads) {
-        const int64_t i = b + tid;
-        const int e = i < p.TK ? p.ids[i] - p.id_base : -1;
-        const bool ok = e >= 0 && e < p.E;
-        const unsigned grp = __match_any_sync(0xffffffffu, ok ? e : -1);
-        const int rank = __popc(grp & ((1u << lane) - 1u)), leader = __ffs(grp) - 1;
-        for (int w = 0; w < kJobThreads / 32; ++w) {
-            if (warp == w && ok) {
-                int pos = 0;
-                if (lane == leader) {
-                    pos = cursor[e];
-                    cursor[e] = pos + __popc(grp);
-                }
-                pos = __shfl_sync(grp, pos, leader);
-                p.order[start[e] + pos + rank] = static_cast<int>(i);
-            }
-            __syncthreads();
-        }
-    }
-    const int NJ = jstart[p.E];
-    for (int jb = tid; jb < NJ; jb += kJobThreads) {
-        int lo = 0, hi = p.E;                             // expert e with jstart[e] <= jb < jstart[e + 1]
-        while (hi - lo > 1) {
-            const int mid = (lo + hi) >> 1;
-            if (jstart[mid] <= jb) lo = mid;
-            else hi = mid;
-        }
-        const int e = lo, part = jb - jstart[e], a = start[e] + part * p.per_job;
-        const int m = min(p.per_job, cnt[e] - part * p.per_job);
-        GemvJob *j0 = p.jobs0 + jb, *j1 = p.jobs1 + jb;
-        j0->w = p.w0 + static_cast<int64_t>(e) * p.bytes0;
-        j1->w = p.w1 + static_cast<int64_t>(e) * p.bytes1;
-        j0->m = j1->m = m;
-        for (int n = 0; n < kMaxTokensPerJob; ++n) {
-            const int slot = n < m ? p.order[a + n] : 0;
-            j0->xrow[n] = slot / p.k;
-            j0->yrow[n] = j1->xrow[n] = j1->yrow[n] = slot;
-        }
-    }
-    if (tid == 0) *p.njobs = NJ;
+    if (!last) return;
+    __threadfence();
+    build_jobs(jp, js, warp_sums);
 }
 
 }  // namespace
@@ -262,13 +289,21 @@ cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream) {
 }
 
 cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16_t *wr, int E, int H, int k, int norm,
-                         int32_t *ids, float *w, float *logits, unsigned *counters, cudaStream_t stream) {
+                         int32_t *ids, float *w, float *logits, unsigned *counters, cudaStream_t stream,
+                         const ExpertJobsParams *jobs) {
     if (T <= 0) return cudaSuccess;
     const dim3 grid((E + kRouteExperts - 1) / kRouteExperts, static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens));
-    return launch_pdl(route_kernel, grid, dim3(kRouterThreads), 0, stream, h, ldh, T, wr, E, H, k, norm, ids, w, logits,
-                      counters);
+    ExpertJobsParams jp{};
+    size_t smem = 0;
+    if (jobs) {
+        jp = *jobs;
+        smem = sizeof(int) * (4 * static_cast<size_t>(jp.E) + 1);
+    }
+    return launch_pdl(route_kernel, grid, dim3(kRouterThreads), smem, stream, h, ldh, T, wr, E, H, k, norm, ids, w,
+                      logits, counters, jp);
 }
 
-int64_t route_counter_slots(int64_t T) { return (T + kRouteTokens - 1) / kRouteTokens; }
+// a counter per 8-token block, and one for the blocks that finished (job building)
+int64_t route_counter_slots(int64_t T) { return (T + kRouteTokens - 1) / kRouteTokens + 1; }
 
 }  // namespace onpu_b200

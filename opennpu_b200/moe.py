@@ -73,6 +73,22 @@ class ExpertFFN:
         L.check(rc, "onpu_moe_ffn_dev")
         return out
 
+    def layer(self, x, wr, k=8, norm_topk_prob=True, out=None, ids=None, w=None, stream=None):
+        """The whole layer in one call (onpu_moe_layer_dev): route x with the bf16 router matrix wr
+        [E, H] (the job lists are built by the router's last CTA), then the experts. Returns
+        (y fp32 [T, H], ids int32 [T, k], w fp32 [T, k])."""
+        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+        assert wr.is_cuda and wr.dtype == torch.bfloat16 and wr.is_contiguous() and wr.shape == (self.E, self.H)
+        T = x.shape[0]
+        ids = torch.empty(T, k, dtype=torch.int32, device=x.device) if ids is None else ids
+        w = torch.empty(T, k, device=x.device) if w is None else w
+        out = torch.empty(T, self.Nd, device=x.device) if out is None else out
+        rc = L.load().onpu_moe_layer_dev(self.h, wr.data_ptr(), x.data_ptr(), x.stride(0), T, k, int(norm_topk_prob),
+                                         ids.data_ptr(), w.data_ptr(), out.data_ptr(), out.stride(0),
+                                         _stream_ptr(stream))
+        L.check(rc, "onpu_moe_layer_dev")
+        return out, ids, w
+
     def __del__(self):
         try:
             if getattr(self, "h", None):

@@ -277,3 +277,22 @@ def test_moe_ffn_expert_shard_with_no_routed_tokens():
     torch.cuda.synchronize()
     assert torch.count_nonzero(y).item() == 0
     assert L.load().onpu_check_device() == 0
+
+
+@pytest.mark.parametrize("T", [1, 16, 64, 300])
+def test_moe_layer_one_call_matches_route_then_ffn(config4, T):
+    """onpu_moe_layer_dev (router whose last CTA builds the job lists, then the experts) gives the
+    same ids, weights and outputs, bit for bit, as onpu_route_dev followed by onpu_moe_ffn_dev."""
+    ffn = config4[0]
+    g = torch.Generator(device="cuda").manual_seed(200 + T)
+    x = torch.randn(T, ffn.H, device="cuda", generator=g).to(torch.bfloat16)
+    wr = (torch.randn(ffn.E, ffn.H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    ids, w = route(x, wr, 8)
+    y = ffn(x, ids, w)
+    for _ in range(2):                                 # twice: the counters are left at zero
+        y2, ids2, w2 = ffn.layer(x, wr, 8)
+        torch.cuda.synchronize()
+        assert torch.equal(ids2, ids) and torch.equal(w2, w)
+        assert torch.equal(y2, y)
+    assert L.load().onpu_check_device() == 0, L.last_error()
+
