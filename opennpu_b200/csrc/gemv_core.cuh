@@ -342,6 +342,9 @@ __host__ __device__ inline int64_t xres_stride(int64_t K) { return (K * 2 + 127)
 
 // Convert 32 bf16 activations (4 x 16 B) to fp16, returning their fp16-rounded sum and max |x|
 // (as fp32 bits); inv scales them first (a power of two).
+// SUM: also return the group's sum (only q4nx uses it, for its min term); the pair conversion is
+// one packed cvt, so staging is not held up by the conversion unit
+template <bool SUM>
 __device__ __forceinline__ float group_to_f16(uint4 (&v)[4], float inv, uint32_t &mx) {
     float sum = 0.f;
 #pragma unroll
@@ -351,9 +354,12 @@ __device__ __forceinline__ float group_to_f16(uint4 (&v)[4], float inv, uint32_t
         for (int k = 0; k < 4; ++k) {
             const float lo = __uint_as_float(w4[k] << 16) * inv, hi = __uint_as_float(w4[k] & 0xffff0000u) * inv;
             mx = max(mx, max(__float_as_uint(fabsf(lo)), __float_as_uint(fabsf(hi))));
-            const __half hl = __float2half_rn(lo), hh = __float2half_rn(hi);
-            sum += __half2float(hl) + __half2float(hh);
-            w4[k] = static_cast<uint32_t>(__half_as_ushort(hl)) | (static_cast<uint32_t>(__half_as_ushort(hh)) << 16);
+            const __half2 h2 = __floats2half2_rn(lo, hi);          // .x = lo (low half), .y = hi
+            if constexpr (SUM) {
+                const float2 f = __half22float2(h2);
+                sum += f.x + f.y;
+            }
+            w4[k] = *reinterpret_cast<const uint32_t *>(&h2);
         }
         v[q] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
     }
@@ -410,7 +416,7 @@ __device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, 
             if (e < items) {
                 const int n = e / G, grp = e - n * G;
                 uint32_t mx = 0;
-                const float sum = group_to_f16(v[u], 1.0f, mx);
+                const float sum = group_to_f16<FMT == kFmtQ4NX>(v[u], 1.0f, mx);
                 uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) row[q] = v[u][q];
@@ -433,7 +439,7 @@ __device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, 
 #pragma unroll
             for (int q = 0; q < 4; ++q) v[q] = CG ? ld_cg_v4(src + q * 8) : ld_nc_v4(src + q * 8);
             uint32_t mx = 0;
-            const float sum = group_to_f16(v, inv, mx);
+            const float sum = group_to_f16<FMT == kFmtQ4NX>(v, inv, mx);
             uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
 #pragma unroll
             for (int q = 0; q < 4; ++q) row[q] = v[q];
