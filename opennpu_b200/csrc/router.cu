@@ -39,6 +39,12 @@ __device__ __forceinline__ float dot8(const uint4 a, const uint4 b, float acc) {
 }
 
 constexpr int kJobThreads = 1024;
+constexpr int64_t kJobSmemInts = 11776;          // dynamic shared memory of the job builder: <= 46 KB
+
+// the slot order goes to shared memory when it fits beside the 4 ints per expert (+1)
+__host__ __device__ inline bool order_in_smem(const ExpertJobsParams &p) {
+    return 4 * static_cast<int64_t>(p.E) + 1 + p.TK <= kJobSmemInts;
+}
 
 // exclusive block-wide scan of one int per thread (any block of whole warps, <= 1024 threads);
 // returns the block total
@@ -77,6 +83,8 @@ __device__ int block_exclusive_scan(int v, int &total, int *warp_sums) {
 // may have written them earlier in the same launch).
 __device__ void build_jobs(const ExpertJobsParams &p, int *js, int *warp_sums) {
     int *cnt = js, *start = cnt + p.E, *jstart = start + p.E, *cursor = jstart + p.E + 1;
+    // the slot order stays in shared memory when it fits (read back 16 at a time per job)
+    int *order = order_in_smem(p) ? cursor + p.E : p.order;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nthr = blockDim.x, nwarps = nthr >> 5;
     for (int e = tid; e < p.E; e += nthr) {
         cnt[e] = 0;
@@ -121,7 +129,7 @@ __device__ void build_jobs(const ExpertJobsParams &p, int *js, int *warp_sums) {
                     cursor[e] = pos + __popc(grp);
                 }
                 pos = __shfl_sync(grp, pos, leader);
-                p.order[start[e] + pos + rank] = static_cast<int>(i);
+                order[start[e] + pos + rank] = static_cast<int>(i);
             }
             __syncthreads();
         }
@@ -141,7 +149,7 @@ __device__ void build_jobs(const ExpertJobsParams &p, int *js, int *warp_sums) {
         j1->w = p.w1 + static_cast<int64_t>(e) * p.bytes1;
         j0->m = j1->m = m;
         for (int n = 0; n < kMaxTokensPerJob; ++n) {
-            const int slot = n < m ? p.order[a + n] : 0;
+            const int slot = n < m ? order[a + n] : 0;
             j0->xrow[n] = slot / p.k;
             j0->yrow[n] = j1->xrow[n] = j1->yrow[n] = slot;
         }
@@ -212,9 +220,8 @@ __device__ __forceinline__ void select_top_k(const float *lg, int64_t t, int E, 
     if (lane < k) w[t * k + lane] = mine / denom;
 }
 
-// Grid (experts / 8, tokens / 8). Warp w computes the logits of expert 8*bx + w for the CTA's 8
-// tokens (the expert row is loaded once per 8 tokens; every load of a lane's K slices is
-// independent, so the whole row is in flight at once). The last CTA of a token block to finish
+// Grid (experts / 8, tokens / 8): each CTA computes the logits of 8 experts x 8 tokens, its warps
+// splitting K (see the loop below). The last CTA of a token block to finish
 // (counter per token block, reset by that CTA) runs the softmax and top-k of its 8 tokens, one
 // warp per token, with the E probabilities in registers (E <= 256: 8 per lane).
 __global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h, int64_t ldh, int64_t T,
@@ -229,34 +236,50 @@ __global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t t0 = static_cast<int64_t>(blockIdx.y) * kRouteTokens;
     const int nt = T - t0 < kRouteTokens ? static_cast<int>(T - t0) : kRouteTokens;
-    const int e = blockIdx.x * kRouteExperts + warp;
-    if (e < E) {
-        const uint16_t *wrow = wr + static_cast<int64_t>(e) * H;
-        float acc[kRouteTokens];
+    // Warp w takes the K slices w, w + 8, ... of 256 elements; lane L the 8 elements at 8L of a
+    // slice, for all 8 experts and 8 tokens of the CTA (16 independent 16-byte loads per slice, so
+    // a lane's loads are all in flight together), 64 partial sums per lane.
+    __shared__ float red[kRouterThreads / 32][kRouteExperts * kRouteTokens];
+    const int e0 = blockIdx.x * kRouteExperts;
+    float acc[kRouteExperts * kRouteTokens];
 #pragma unroll
-        for (int n = 0; n < kRouteTokens; ++n) acc[n] = 0.f;
-#pragma unroll 4
-        for (int d = lane * 8; d < H; d += 32 * 8) {
-            const uint4 b = ld_nc_v4(wrow + d);
-            uint4 a[kRouteTokens];
+    for (int q = 0; q < kRouteExperts * kRouteTokens; ++q) acc[q] = 0.f;
+    for (int d = (warp * 32 + lane) * 8; d < H; d += kRouterThreads * 8) {
+        uint4 b[kRouteExperts], a[kRouteTokens];
 #pragma unroll
-            for (int n = 0; n < kRouteTokens; ++n)
-                a[n] = n < nt ? ld_nc_v4(h + (t0 + n) * ldh + d) : make_uint4(0, 0, 0, 0);
+        for (int x = 0; x < kRouteExperts; ++x)
+            b[x] = e0 + x < E ? ld_nc_v4(wr + static_cast<int64_t>(e0 + x) * H + d) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-            for (int n = 0; n < kRouteTokens; ++n) acc[n] = dot8(a[n], b, acc[n]);
+        for (int n = 0; n < kRouteTokens; ++n)
+            a[n] = n < nt ? ld_nc_v4(h + (t0 + n) * ldh + d) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int x = 0; x < kRouteExperts; ++x)
+#pragma unroll
+            for (int n = 0; n < kRouteTokens; ++n) acc[x * kRouteTokens + n] = dot8(a[n], b[x], acc[x * kRouteTokens + n]);
+    }
+    // reduce the 64 sums over the warp's lanes by halving exchanges: after the offsets 16, 8, 4,
+    // 2, 1, lane L holds the complete warp sums of pairs 2L and 2L + 1 (pair = expert * 8 + token)
+#pragma unroll
+    for (int o = 16, half = 32; o; o >>= 1, half >>= 1) {
+        const bool up = lane & o;
+#pragma unroll
+        for (int q = 0; q < 32; ++q) {
+            if (q < half) {
+                const float send = up ? acc[q] : acc[q + half];
+                const float keep = up ? acc[q + half] : acc[q];
+                acc[q] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+            }
         }
+    }
+    red[warp][2 * lane] = acc[0];
+    red[warp][2 * lane + 1] = acc[1];
+    __syncthreads();
+    if (threadIdx.x < kRouteExperts * kRouteTokens) {
+        const int x = threadIdx.x / kRouteTokens, n = threadIdx.x % kRouteTokens;
+        float v = red[0][threadIdx.x];
 #pragma unroll
-        for (int n = 0; n < kRouteTokens; ++n) {
-#pragma unroll
-            for (int o = 16; o; o >>= 1) acc[n] += __shfl_xor_sync(0xffffffffu, acc[n], o);
-        }
-        if (lane < nt) {
-            float v = acc[0];
-#pragma unroll
-            for (int n = 1; n < kRouteTokens; ++n)
-                if (lane == n) v = acc[n];
-            lg[(t0 + lane) * E + e] = v;
-        }
+        for (int ww = 1; ww < kRouterThreads / 32; ++ww) v += red[ww][threadIdx.x];   // warps in order
+        if (e0 + x < E && n < nt) lg[(t0 + n) * E + e0 + x] = v;
     }
     __threadfence();
     __syncthreads();
@@ -280,12 +303,16 @@ __global__ void __launch_bounds__(kRouterThreads) route_kernel(const uint16_t *h
     build_jobs(jp, js, warp_sums);
 }
 
+// 4 ints per expert (+1), and the slot order when it fits
+size_t job_smem_bytes(const ExpertJobsParams &p) {
+    return sizeof(int) * (4 * static_cast<size_t>(p.E) + 1 + (order_in_smem(p) ? p.TK : 0));
+}
+
 }  // namespace
 
 cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream) {
     if (p.TK <= 0) return cudaSuccess;
-    const size_t smem = sizeof(int) * (3 * static_cast<size_t>(p.E) + 1 + p.E);
-    return launch_pdl(expert_jobs_kernel, dim3(1), dim3(kJobThreads), smem, stream, p);
+    return launch_pdl(expert_jobs_kernel, dim3(1), dim3(kJobThreads), job_smem_bytes(p), stream, p);
 }
 
 cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16_t *wr, int E, int H, int k, int norm,
@@ -297,7 +324,7 @@ cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16
     size_t smem = 0;
     if (jobs) {
         jp = *jobs;
-        smem = sizeof(int) * (4 * static_cast<size_t>(jp.E) + 1);
+        smem = job_smem_bytes(jp);
     }
     return launch_pdl(route_kernel, grid, dim3(kRouterThreads), smem, stream, h, ldh, T, wr, E, H, k, norm, ids, w,
                       logits, counters, jp);
