@@ -156,51 +156,51 @@ __device__ __forceinline__ void strip_chunk(uint32_t wsb, const uint32_t (&xa)[N
 }
 
 // ================================================================ fp16 path (resident activations)
-// The resident kernels feed the tensor cores fp16: 1024 + q for strip rows r (mask 0x000F000F)
-// and 1024 + 16 q for rows r+8 (mask 0x00F000F0), one three-register LOP3 each from the packed
-// word or the word >> 8 (fp16's 10-bit mantissa holds both nibbles of a byte), then one HSUB2
-// removes the bias exactly (symmetric: 1032 and 1152 = 1024 + 16 * 8; q4nx: 1024), 9
-// instructions per 8 codes. Rows r+8 carry a factor 16, removed exactly at the end of a segment
-// (finish_rows). The activations are staged as fp16 (scaled per token by a power of two when |x|
-// would leave the fp16 range). Products (q - 8) * x are exact in fp32 and the MMA accumulates
-// sums of the size of the result (subtracting the bias after the MMA instead, from a table of
-// group sums, cancels ~1000x larger partial sums and costs ~10 bits of the fp32 accumulator);
-// q4nx adds m * sum(x) from the table of group sums. The weights are never rounded.
+// The resident kernels feed the tensor cores fp16 subnormals: a code q masked into the low
+// mantissa bits with a zero exponent is the fp16 value q * 2^-24 exactly. Strip rows r take
+// mask 0x000F000F (q * 2^-24), rows r+8 mask 0x00F000F0 (16 q * 2^-24), one AND each from the
+// packed word or the word >> 8: 5 instructions per 8 codes, no bias to remove. Symmetric formats
+// start each group's MMA from -8 * 2^-24 * sum(x) (x 16 on rows r+8), read from a table of group
+// sums written at staging; this offset is of the size of the products' sum (q in 0..15 against
+// 8), so the fp32 accumulation keeps its precision (a 1024 + q encoding with the offset applied
+// the same way cancels ~1000x larger partial sums). q4nx starts from 0 and adds m * sum(x) * 2^-24
+// from the same table. The factors 2^-24 and 16 are removed exactly (powers of two) at the end of
+// a segment (finish_rows). The activations are staged as fp16 (scaled per token by a power of
+// two when |x| would leave the fp16 range). The weights are never rounded.
 struct Unpack {
-    uint32_t mlo, mhi, magic;      // 0x000F000F, 0x00F000F0, 0x64006400 (kernel parameters: kept in registers)
+    uint32_t mlo, mhi, magic;      // 0x000F000F, 0x00F000F0, 0x64006400 (kernel parameters: kept in registers;
+                                   // the fp16 path uses the two masks)
 };
 
-__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
-    uint32_t d;
-    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));   // (a & b) | c
-    return d;
-}
-
-__device__ __forceinline__ uint32_t hsub2_bits(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
-}
-
-// 8 codes -> the A registers as exact centred fp16 values: rows r hold q - 8 (q for q4nx), rows
-// r+8 hold 16 (q - 8) (16 q): one LOP3 gives 1024 + q (1024 + 16 q), one HSUB2 removes the bias
-// exactly, so the MMA sums products of small integers and activations (no large offset to cancel)
-template <int FMT>
+// 8 codes -> the A registers as exact fp16 subnormals: rows r hold q * 2^-24, rows r+8
+// 16 q * 2^-24 (nibbles 0/4 and 1/5 of w, 2/6 and 3/7 of w >> 8)
 __device__ __forceinline__ void codes_to_a_h(uint32_t w, const Unpack &u, uint32_t (&a)[4]) {
-    constexpr uint32_t off_lo = FMT == kFmtQ4NX ? 0x64006400u : 0x64086408u;   // 1024 | 1032
-    constexpr uint32_t off_hi = FMT == kFmtQ4NX ? 0x64006400u : 0x64806480u;   // 1024 | 1152
     const uint32_t s = w >> 8;
-    a[0] = hsub2_bits(lop3_and_or(w, u.mlo, u.magic), off_lo);
-    a[1] = hsub2_bits(lop3_and_or(w, u.mhi, u.magic), off_hi);
-    a[2] = hsub2_bits(lop3_and_or(s, u.mlo, u.magic), off_lo);
-    a[3] = hsub2_bits(lop3_and_or(s, u.mhi, u.magic), off_hi);
+    a[0] = w & u.mlo;
+    a[1] = w & u.mhi;
+    a[2] = s & u.mlo;
+    a[3] = s & u.mhi;
 }
+
+// Group-sum table entry per fp32 sum of a group's fp16 activations: the MMA's starting value on
+// rows r for the symmetric formats (-8 * 2^-24), the min term's factor for q4nx (2^-24)
+template <int FMT>
+__host__ __device__ constexpr float tab_factor() { return FMT == kFmtQ4NX ? 0x1p-24f : -0x1p-21f; }
 
 __device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
         "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// the same from C = {c0, c1, c2, c3}
+__device__ __forceinline__ void mma16816_f16_c(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1,
+                                               float c0, float c1, float c2, float c3) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c0), "f"(c1), "f"(c2), "f"(c3));
 }
 
 // the same with C = 0 (a fresh per-group sum: no register copies of zeros)
@@ -234,20 +234,17 @@ __device__ __forceinline__ void strip_chunk_h(uint32_t wsb, const uint32_t (&xa)
 #pragma unroll
     for (int gi = 0; gi < 2; ++gi) {
         uint32_t a0[4], a1[4];
-        codes_to_a_h<FMT>(gi ? code.z : code.x, u, a0);
-        codes_to_a_h<FMT>(gi ? code.w : code.y, u, a1);
+        codes_to_a_h(gi ? code.z : code.x, u, a0);
+        codes_to_a_h(gi ? code.w : code.y, u, a1);
         float s_lo, s_hi;
         decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            float x0 = 0.f, x1 = 0.f;
-            if constexpr (FMT == kFmtQ4NX) {
-                const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
-                x0 = __uint_as_float(c2.x);
-                x1 = __uint_as_float(c2.y);
-            }
+            const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
+            const float x0 = __uint_as_float(c2.x), x1 = __uint_as_float(c2.y);
             float d[4];
-            mma16816_f16_z(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+            if constexpr (FMT == kFmtQ4NX) mma16816_f16_z(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+            else mma16816_f16_c(d, a0, bx[gi][nt][0], bx[gi][nt][1], x0, x1, 16.0f * x0, 16.0f * x1);
             mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
             acc[nt][0] = fmaf(s_lo, d[0], acc[nt][0]);
             acc[nt][1] = fmaf(s_lo, d[1], acc[nt][1]);
@@ -282,12 +279,9 @@ __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], 
         for (int nt = 0; nt < NT; ++nt) {
             const uint4 v = lds_v4(xa[nt] + gi * 64);
             bx[gi][nt][0] = v.x; bx[gi][nt][1] = v.y; bx[gi][nt][2] = v.z; bx[gi][nt][3] = v.w;
-            xs[gi][nt][0] = xs[gi][nt][1] = 0.f;
-            if constexpr (FMT == kFmtQ4NX) {          // the min term needs the group sums
-                const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
-                xs[gi][nt][0] = __uint_as_float(c2.x);
-                xs[gi][nt][1] = __uint_as_float(c2.y);
-            }
+            const uint2 c2 = lds_v2(ca + (gi * NT + nt) * 32);
+            xs[gi][nt][0] = __uint_as_float(c2.x);
+            xs[gi][nt][1] = __uint_as_float(c2.y);
         }
 #pragma unroll
     for (int s = 0; s < 4; ++s) {
@@ -298,8 +292,8 @@ __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], 
 #pragma unroll
         for (int gi = 0; gi < 2; ++gi) {
             uint32_t a0[4], a1[4];
-            codes_to_a_h<FMT>(gi ? code.z : code.x, u, a0);
-            codes_to_a_h<FMT>(gi ? code.w : code.y, u, a1);
+            codes_to_a_h(gi ? code.z : code.x, u, a0);
+            codes_to_a_h(gi ? code.w : code.y, u, a1);
             float s_lo, s_hi;
             decode_pair<FMT>(gi ? sc.y : sc.x, mul, s_lo, s_hi);
             float m_lo = 0.f, m_hi = 0.f;
@@ -311,7 +305,8 @@ __device__ __forceinline__ void chunk_h(uint32_t wcb, const uint32_t (&xa)[NT], 
             for (int nt = 0; nt < NT; ++nt) {
                 const float x0 = xs[gi][nt][0], x1 = xs[gi][nt][1];
                 float d[4];
-                mma16816_f16_z(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+                if constexpr (FMT == kFmtQ4NX) mma16816_f16_z(d, a0, bx[gi][nt][0], bx[gi][nt][1]);
+                else mma16816_f16_c(d, a0, bx[gi][nt][0], bx[gi][nt][1], x0, x1, 16.0f * x0, 16.0f * x1);
                 mma16816_f16(d, a1, bx[gi][nt][2], bx[gi][nt][3]);
                 acc[s][nt][0] = fmaf(s_lo, d[0], acc[s][nt][0]);
                 acc[s][nt][1] = fmaf(s_lo, d[1], acc[s][nt][1]);
@@ -342,7 +337,7 @@ __host__ __device__ inline int64_t xres_stride(int64_t K) { return (K * 2 + 127)
 
 // Convert 32 bf16 activations (4 x 16 B) to fp16, returning their fp16-rounded sum and max |x|
 // (as fp32 bits); inv scales them first (a power of two).
-// SUM: also return the group's sum (only q4nx uses it, for its min term); the pair conversion is
+// SUM: also return the group's sum (the fp16 path's table of group sums); the pair conversion is
 // one packed cvt, so staging is not held up by the conversion unit
 template <bool SUM>
 __device__ __forceinline__ float group_to_f16(uint4 (&v)[4], float inv, uint32_t &mx) {
@@ -416,11 +411,11 @@ __device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, 
             if (e < items) {
                 const int n = e / G, grp = e - n * G;
                 uint32_t mx = 0;
-                const float sum = group_to_f16<FMT == kFmtQ4NX>(v[u], 1.0f, mx);
+                const float sum = group_to_f16<true>(v[u], 1.0f, mx);
                 uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
 #pragma unroll
                 for (int q = 0; q < 4; ++q) row[q] = v[u][q];
-                tab_at(grp, n) = sum;
+                tab_at(grp, n) = sum * tab_factor<FMT>();
                 if (mx > 0x47000000u) atomicMax(tmax + n, mx);      // only values above 2^15 matter
             }
         }
@@ -439,11 +434,11 @@ __device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, 
 #pragma unroll
             for (int q = 0; q < 4; ++q) v[q] = CG ? ld_cg_v4(src + q * 8) : ld_nc_v4(src + q * 8);
             uint32_t mx = 0;
-            const float sum = group_to_f16<FMT == kFmtQ4NX>(v, inv, mx);
+            const float sum = group_to_f16<true>(v, inv, mx);
             uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
 #pragma unroll
             for (int q = 0; q < 4; ++q) row[q] = v[q];
-            tab_at(grp, n) = sum;
+            tab_at(grp, n) = sum * tab_factor<FMT>();
         }
     }
     if (tid < 16)
@@ -451,7 +446,8 @@ __device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, 
     named_bar_sync(1, nthr);
 }
 
-// End of a segment (fp16 path): rows r+8 lose their factor 16, tokens their staging scale.
+// End of a segment (fp16 path): the sums lose the codes' factor 2^-24 (rows r+8 also their
+// factor 16), tokens their staging scale; all powers of two, so exact.
 template <int NT>
 __device__ __forceinline__ void finish_rows(float (&acc)[NT][4], const float *tscale, int t) {
 #pragma unroll
@@ -459,7 +455,7 @@ __device__ __forceinline__ void finish_rows(float (&acc)[NT][4], const float *ts
 #pragma unroll
         for (int f = 0; f < 4; ++f) {
             const float sc = tscale[nt * 8 + 2 * t + (f & 1)];
-            acc[nt][f] *= f >= 2 ? sc * 0.0625f : sc;
+            acc[nt][f] *= f >= 2 ? sc * 0x1p20f : sc * 0x1p24f;
         }
 }
 
