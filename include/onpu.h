@@ -126,7 +126,7 @@ int onpu_check_device(void);
 void *onpu_dense_new_int4(int64_t N, int64_t K, int gateup);
 /* Fill from host (on_device = 0) or device (on_device = 1) arrays; 0 ok, < 0 error. */
 int onpu_dense_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream);
-/* The load-time search quantisers on the GPU (SURVEY §8(f)): W fp32 [N][ldw] (device, 16-byte
+/* The load-time search quantisers on the GPU: W fp32 [N][ldw] (device, 16-byte
  * aligned, ldw % 4 == 0, K % 32 == 0) -> codes q [N][K] (0..15), 16-bit (bf16) scales [N][K/32] and,
  * for q4nx (sym = 0), mins [N][K/32]; bit-exact with onpu_pack's quantisers
  * (opennpu_core.hpp:103-169, which the reference runs on the host at load time). Asynchronous. */
@@ -271,6 +271,29 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
 /* GPU layout -> plain codes q[N][K] (0..15), scales[N][K/32] (and mins for q4nx), device pointers;
  * for bit-exact verification. */
 int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream);
+
+/* ---- weight blobs: the GPU layout on disk (replaces what the reference's PackCache stores,
+ * npu4/model.py:712-759: the packed upload bytes of one NPU buffer, so a second model load skips
+ * reading and quantising the checkpoint). A blob is self-describing: a 64-byte header (magic
+ * "ONPUB2GL", onpu_layout_version(), kind, matrix count), then per matrix a 64-byte header
+ * (N, K, E, format, flags) and its GPU-layout bytes as they lie in HBM, padded to 64 bytes.
+ * A second load of a blob is one host->device copy per matrix: no quantisation, no repack.
+ *
+ * *_export: dst NULL returns the blob's size; else writes it to host memory dst (cap bytes) and
+ * returns its size, or -1 (cap too small, K % 32 != 0, weights never loaded). Synchronises the
+ * device first (weights loaded asynchronously are complete).
+ * *_import: a new handle (free it with the matching *_free) from a blob in host memory; NULL with
+ * an error message if the magic, the layout version, the kind, a shape or the size does not
+ * match (checked before any device call). Imported dense handles run on every dense entry point
+ * (host and device); like onpu_dense_new_int4 handles they have no stream-order upload buffer. */
+int onpu_layout_version(void);
+int64_t onpu_dense_export(void *h, void *dst, int64_t cap);
+void *onpu_dense_import(const void *src, int64_t nbytes);
+int64_t onpu_bank_export(void *h, void *dst, int64_t cap);
+void *onpu_bank_import(const void *src, int64_t nbytes);
+/* both banks of a routed-expert FFN (gate_up, then down) in one blob */
+int64_t onpu_ffn_export(void *h, void *dst, int64_t cap);
+void *onpu_ffn_import(const void *src, int64_t nbytes);
 
 #ifdef __cplusplus
 }

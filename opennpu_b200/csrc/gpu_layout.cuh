@@ -36,6 +36,10 @@ enum WeightFormat : int {
     kFmtQ4F16 = 2,  // symmetric int4 [-8, 7], fp16 scale     (packed-along-K int4 + fp16 ingest)
 };
 
+// Version of the weights' device layout below (row groups, chunks, strips, code and scale order).
+// Saved weight blobs (onpu_dense_export and friends) carry it; a blob of another version is refused.
+constexpr int kGpuLayoutVersion = 1;
+
 constexpr int kRowGroup = 64;
 constexpr int kStripRows = 16;
 constexpr int kChunkK = 64;

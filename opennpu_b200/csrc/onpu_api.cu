@@ -1980,3 +1980,282 @@ void onpu_chain_free(void *chain) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ weight blobs (the pack cache)
+// A blob is a 64-byte header (magic, layout version, kind, matrix count) and per matrix a 64-byte
+// section header (N, K, E, format, flags, payload bytes) followed by the GPU-layout bytes exactly
+// as they lie in HBM, padded to 64 bytes. Everything is validated before any device call, so a
+// truncated or foreign file is refused with a message instead of being copied.
+namespace {
+constexpr char kBlobMagic[8] = {'O', 'N', 'P', 'U', 'B', '2', 'G', 'L'};
+constexpr uint32_t kBlobDense = 1, kBlobBank = 2, kBlobFfn = 3;
+constexpr uint32_t kMatGateUp = 1, kMatResidual = 2;   // gate/up strip interleave; two-pass pairs
+
+struct BlobHead {
+    char magic[8];
+    uint32_t version, kind, nmats, pad;
+    uint8_t rsv[40];
+};
+struct MatHead {
+    int64_t N, K, E;
+    int32_t fmt;
+    uint32_t flags;
+    int64_t bytes;
+    uint8_t rsv[24];
+};
+static_assert(sizeof(BlobHead) == 64 && sizeof(MatHead) == 64, "blob headers are 64 bytes");
+
+int64_t section_bytes(const GpuMat &m) { return static_cast<int64_t>(sizeof(MatHead)) + round_up(m.gm.bytes * m.E, 64); }
+
+// K of a handle made through the reference upload path must be the GPU layout's K
+bool exportable(const Geometry &geo, const GpuMat &m, const char *who) {
+    if (!m.d_w || (geo.ok && geo.K != m.gm.K)) {
+        set_err("%s: only matrices with K %% 32 == 0 and loaded weights can be exported", who);
+        return false;
+    }
+    return true;
+}
+
+bool write_section(const GpuMat &m, uint32_t flags, uint8_t *dst) {
+    MatHead h{};
+    h.N = m.gm.N;
+    h.K = m.gm.K;
+    h.E = m.E;
+    h.fmt = m.gm.fmt;
+    h.flags = flags;
+    h.bytes = m.gm.bytes * m.E;
+    std::memcpy(dst, &h, sizeof h);
+    const cudaError_t e = cudaMemcpy(dst + sizeof h, m.d_w, static_cast<size_t>(h.bytes), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) {
+        set_err("weight export: %s", cudaGetErrorString(e));
+        return false;
+    }
+    std::memset(dst + sizeof h + h.bytes, 0, static_cast<size_t>(round_up(h.bytes, 64) - h.bytes));
+    return true;
+}
+
+// Validates the blob header; out: the matrix sections' headers and payload pointers.
+bool parse_blob(const void *src, int64_t nbytes, uint32_t kind, uint32_t nmats, MatHead *heads,
+                const uint8_t **payloads, const char *who) {
+    if (!src || nbytes < static_cast<int64_t>(sizeof(BlobHead))) {
+        set_err("%s: blob of %lld bytes is shorter than its header", who, static_cast<long long>(nbytes));
+        return false;
+    }
+    const auto *p = static_cast<const uint8_t *>(src), *end = p + nbytes;
+    BlobHead bh;
+    std::memcpy(&bh, p, sizeof bh);
+    if (std::memcmp(bh.magic, kBlobMagic, sizeof kBlobMagic) != 0) {
+        set_err("%s: not a weight blob (bad magic)", who);
+        return false;
+    }
+    if (bh.version != static_cast<uint32_t>(kGpuLayoutVersion)) {
+        set_err("%s: blob of layout version %u, this library writes version %d", who, bh.version, kGpuLayoutVersion);
+        return false;
+    }
+    if (bh.kind != kind || bh.nmats != nmats) {
+        set_err("%s: blob holds kind %u with %u matrices, expected kind %u with %u", who, bh.kind, bh.nmats, kind,
+                nmats);
+        return false;
+    }
+    p += sizeof bh;
+    for (uint32_t i = 0; i < nmats; ++i) {
+        MatHead h;
+        if (end - p < static_cast<int64_t>(sizeof h)) {
+            set_err("%s: blob truncated in matrix %u's header", who, i);
+            return false;
+        }
+        std::memcpy(&h, p, sizeof h);
+        p += sizeof h;
+        if (h.N <= 0 || h.N > (int64_t{1} << 30) || h.K <= 0 || h.K > (int64_t{1} << 30) || h.K % 32 || h.E <= 0 ||
+            h.E > (int64_t{1} << 16) || h.fmt < kFmtQ4NX || h.fmt > kFmtQ4F16 || (h.flags & ~(kMatGateUp | kMatResidual))) {
+            set_err("%s: matrix %u has an invalid header (N %lld, K %lld, E %lld, format %d, flags %u)", who, i,
+                    static_cast<long long>(h.N), static_cast<long long>(h.K), static_cast<long long>(h.E), h.fmt,
+                    h.flags);
+            return false;
+        }
+        const GpuMatrix g = make_gpu_matrix(h.N, h.K, h.fmt);
+        if (g.bytes > (int64_t{1} << 40) / h.E || h.bytes != g.bytes * h.E) {
+            set_err("%s: matrix %u declares %lld payload bytes, its shape needs %lld", who, i,
+                    static_cast<long long>(h.bytes), static_cast<long long>(g.bytes * h.E));
+            return false;
+        }
+        if (end - p < round_up(h.bytes, 64)) {
+            set_err("%s: blob truncated in matrix %u's weights", who, i);
+            return false;
+        }
+        heads[i] = h;
+        payloads[i] = p;
+        p += round_up(h.bytes, 64);
+    }
+    if (p != end) {
+        set_err("%s: %lld bytes after the last matrix", who, static_cast<long long>(end - p));
+        return false;
+    }
+    return true;
+}
+
+bool load_section(GpuMat &m, const MatHead &h, const uint8_t *payload, const char *who) {
+    if (!alloc_mat(m, h.N, h.K, h.fmt, h.E)) return false;
+    if ((h.flags & (kMatGateUp | kMatResidual)) && !set_gateup_interleave(m)) {
+        set_err("%s: interleaved rows need N %% 2 == 0 and N/2 %% 8 == 0", who);
+        return false;
+    }
+    const cudaError_t e = cudaMemcpy(m.d_w, payload, static_cast<size_t>(h.bytes), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+        set_err("%s: %s", who, cudaGetErrorString(e));
+        return false;
+    }
+    return true;
+}
+
+int64_t write_blob(uint32_t kind, const GpuMat *const *mats, const uint32_t *flags, int n, void *dst, int64_t cap,
+                   const char *who) {
+    int64_t total = sizeof(BlobHead);
+    for (int i = 0; i < n; ++i) total += section_bytes(*mats[i]);
+    if (!dst) return total;
+    if (cap < total) {
+        set_err("%s: the blob needs %lld bytes, the buffer holds %lld", who, static_cast<long long>(total),
+                static_cast<long long>(cap));
+        return -1;
+    }
+    const cudaError_t e = cudaDeviceSynchronize();     // weights loaded on any stream are complete
+    if (e != cudaSuccess) {
+        set_err("%s: %s", who, cudaGetErrorString(e));
+        return -1;
+    }
+    BlobHead bh{};
+    std::memcpy(bh.magic, kBlobMagic, sizeof kBlobMagic);
+    bh.version = kGpuLayoutVersion;
+    bh.kind = kind;
+    bh.nmats = static_cast<uint32_t>(n);
+    auto *p = static_cast<uint8_t *>(dst);
+    std::memcpy(p, &bh, sizeof bh);
+    p += sizeof bh;
+    for (int i = 0; i < n; ++i) {
+        if (!write_section(*mats[i], flags[i], p)) return -1;
+        p += section_bytes(*mats[i]);
+    }
+    return total;
+}
+
+BankH *bank_from_section(const MatHead &h, const uint8_t *payload, const char *who) {
+    auto *b = new BankH;
+    b->fmt = h.fmt;
+    b->owns_buf = false;
+    b->geo.N = h.N;
+    b->geo.K = h.K;
+    if (!load_section(b->mat, h, payload, who)) {
+        delete b;
+        return nullptr;
+    }
+    return b;
+}
+}  // namespace
+
+extern "C" {
+
+int onpu_layout_version(void) { return kGpuLayoutVersion; }
+
+int64_t onpu_dense_export(void *h, void *dst, int64_t cap) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    if (!d || !exportable(d->geo, d->mat, "onpu_dense_export")) return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    const GpuMat *mats[1] = {&d->mat};
+    const uint32_t flags[1] = {(d->gateup ? kMatGateUp : 0u) | (d->residual ? kMatResidual : 0u)};
+    return write_blob(kBlobDense, mats, flags, 1, dst, cap, "onpu_dense_export");
+}
+
+void *onpu_dense_import(const void *src, int64_t nbytes) {
+    clear_err();
+    MatHead h[1];
+    const uint8_t *pl[1];
+    if (!parse_blob(src, nbytes, kBlobDense, 1, h, pl, "onpu_dense_import")) return nullptr;
+    if (h[0].E != 1 || (h[0].flags == (kMatGateUp | kMatResidual))) {
+        set_err("onpu_dense_import: a dense blob holds one matrix, gate/up or two-pass, not both");
+        return nullptr;
+    }
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *d = new DenseH;
+    d->fmt = h[0].fmt;
+    d->gateup = h[0].flags == kMatGateUp;
+    d->residual = h[0].flags == kMatResidual;
+    if (!load_section(d->mat, h[0], pl[0], "onpu_dense_import")) {
+        delete d;
+        return nullptr;
+    }
+    return d;
+}
+
+int64_t onpu_bank_export(void *h, void *dst, int64_t cap) {
+    clear_err();
+    auto *b = static_cast<BankH *>(h);
+    if (!b || !exportable(b->geo, b->mat, "onpu_bank_export")) return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    const GpuMat *mats[1] = {&b->mat};
+    const uint32_t flags[1] = {b->mat.d_row_map ? kMatGateUp : 0u};
+    return write_blob(kBlobBank, mats, flags, 1, dst, cap, "onpu_bank_export");
+}
+
+void *onpu_bank_import(const void *src, int64_t nbytes) {
+    clear_err();
+    MatHead h[1];
+    const uint8_t *pl[1];
+    if (!parse_blob(src, nbytes, kBlobBank, 1, h, pl, "onpu_bank_import")) return nullptr;
+    if (h[0].flags & kMatResidual) {
+        set_err("onpu_bank_import: expert banks have no two-pass form");
+        return nullptr;
+    }
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    return bank_from_section(h[0], pl[0], "onpu_bank_import");
+}
+
+int64_t onpu_ffn_export(void *h, void *dst, int64_t cap) {
+    clear_err();
+    auto *f = static_cast<FfnH *>(h);
+    if (!f || !exportable(f->gu->geo, f->gu->mat, "onpu_ffn_export") ||
+        !exportable(f->dn->geo, f->dn->mat, "onpu_ffn_export"))
+        return -1;
+    std::lock_guard<std::mutex> lk(g_mu);
+    const GpuMat *mats[2] = {&f->gu->mat, &f->dn->mat};
+    const uint32_t flags[2] = {f->gu->mat.d_row_map ? kMatGateUp : 0u, f->dn->mat.d_row_map ? kMatGateUp : 0u};
+    return write_blob(kBlobFfn, mats, flags, 2, dst, cap, "onpu_ffn_export");
+}
+
+void *onpu_ffn_import(const void *src, int64_t nbytes) {
+    clear_err();
+    MatHead h[2];
+    const uint8_t *pl[2];
+    if (!parse_blob(src, nbytes, kBlobFfn, 2, h, pl, "onpu_ffn_import")) return nullptr;
+    if (((h[0].flags | h[1].flags) & kMatResidual) || h[0].E != h[1].E) {
+        set_err("onpu_ffn_import: gate_up and down banks need the same expert count and no two-pass form");
+        return nullptr;
+    }
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto *f = new FfnH;
+    f->gu = bank_from_section(h[0], pl[0], "onpu_ffn_import");
+    f->dn = f->gu ? bank_from_section(h[1], pl[1], "onpu_ffn_import") : nullptr;
+    if (!f->gu || !f->dn) {
+        delete f;
+        return nullptr;
+    }
+    f->fused = (h[0].flags & kMatGateUp) && h[1].K * 2 == h[0].N;
+    return f;
+}
+
+}  // extern "C"

@@ -75,6 +75,24 @@ class DenseMatrix:
             raise L.OnpuError(f"onpu_dense_new_residual_f32_dev: {L.last_error()}")
         return cls(h, 2 * N, K, FMT_Q4S if sym else FMT_Q4NX, residual=True)
 
+    # ---------------------------------------------------------------- weight blobs
+    def export(self):
+        """The matrix as a self-describing blob of its GPU layout (uint8 numpy array; the bytes a
+        PackCache stores)."""
+        return L.export_blob(L.load().onpu_dense_export, self.h, "onpu_dense_export")
+
+    @classmethod
+    def from_blob(cls, blob):
+        """A matrix from an ``export`` blob: one host->device copy, no quantisation or repack."""
+        lib = L.require_device()
+        b = L.as_blob(blob)
+        h = lib.onpu_dense_import(b.ctypes.data, b.size)
+        if not h:
+            raise L.OnpuError(f"onpu_dense_import: {L.last_error()}")
+        sec = L.blob_sections(b)[1][0]
+        return cls(h, sec["N"], sec["K"], sec["fmt"], gateup=sec["flags"] == L.BLOB_GATEUP,
+                   residual=sec["flags"] == L.BLOB_RESIDUAL)
+
     @classmethod
     def from_stream(cls, N, K, sym, packed):
         """The reference upload protocol: onpu_dense_new2 + fill onpu_dense_buf + onpu_dense_sync."""

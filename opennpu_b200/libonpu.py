@@ -64,6 +64,13 @@ SIGNATURES = {
     "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mm_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
+    "onpu_layout_version": (I32, []),
+    "onpu_dense_export": (I64, [P, P, I64]),
+    "onpu_dense_import": (P, [P, I64]),
+    "onpu_bank_export": (I64, [P, P, I64]),
+    "onpu_bank_import": (P, [P, I64]),
+    "onpu_ffn_export": (I64, [P, P, I64]),
+    "onpu_ffn_import": (P, [P, I64]),
     "onpu_route_dev": (I32, [P, I64, I64, P, I64, I64, I32, I32, P, P, P, P]),
     "onpu_bank_new_int4": (P, [I64, I64, I64, I32]),
     "onpu_bank_load_int4": (I32, [P, P, P, I32, P]),
@@ -113,6 +120,47 @@ def load():
 def last_error():
     e = load().onpu_last_error()
     return e.decode() if e else None
+
+
+BLOB_MAGIC = b"ONPUB2GL"
+BLOB_DENSE, BLOB_BANK, BLOB_FFN = 1, 2, 3
+BLOB_GATEUP, BLOB_RESIDUAL = 1, 2
+
+
+def blob_sections(blob):
+    """The matrix headers of a weight blob (onpu_*_export): (kind, [{N, K, E, fmt, flags, bytes}]).
+    Reads only the headers; the library validates the whole blob on import."""
+    import struct
+    mv = memoryview(blob).cast("B")
+    if len(mv) < 64 or bytes(mv[:8]) != BLOB_MAGIC:
+        raise OnpuError("not a weight blob")
+    version, kind, nmats = struct.unpack_from("<III", mv, 8)
+    mats, off = [], 64
+    for _ in range(nmats):
+        if len(mv) < off + 64:
+            raise OnpuError("weight blob truncated")
+        N, K, E, fmt, flags, nbytes = struct.unpack_from("<qqqiIq", mv, off)
+        mats.append(dict(N=N, K=K, E=E, fmt=fmt, flags=flags, bytes=nbytes, version=version))
+        off += 64 + (nbytes + 63) // 64 * 64
+    return kind, mats
+
+
+def export_blob(fn, h, what):
+    """Run an onpu_*_export entry twice (size, then contents) -> the blob as a uint8 numpy array."""
+    import numpy as np
+    n = fn(h, None, 0)
+    check(n, what)
+    buf = np.empty(n, dtype=np.uint8)
+    check(fn(h, buf.ctypes.data, n), what)
+    return buf
+
+
+def as_blob(blob):
+    """bytes / bytearray / memoryview / numpy -> a contiguous uint8 numpy array (no copy when possible)."""
+    import numpy as np
+    if isinstance(blob, np.ndarray):
+        return np.ascontiguousarray(blob.view(np.uint8).reshape(-1))
+    return np.frombuffer(blob, dtype=np.uint8)
 
 
 def check(rc, what="libonpu call"):

@@ -43,6 +43,23 @@ class ExpertFFN:
         self._load(lib.onpu_ffn_gu(self.h), gu_qk, gu_s, stream)
         self._load(lib.onpu_ffn_dn(self.h), dn_qk, dn_s, stream)
 
+    def export(self):
+        """Both banks as one self-describing blob of their GPU layout (uint8 numpy array)."""
+        return L.export_blob(L.load().onpu_ffn_export, self.h, "onpu_ffn_export")
+
+    @classmethod
+    def from_blob(cls, blob):
+        """An FFN from an ``export`` blob: one host->device copy per bank, no repack."""
+        lib = L.require_device()
+        b = L.as_blob(blob)
+        h = lib.onpu_ffn_import(b.ctypes.data, b.size)
+        if not h:
+            raise L.OnpuError(f"onpu_ffn_import: {L.last_error()}")
+        gu, dn = L.blob_sections(b)[1]
+        f = cls.__new__(cls)
+        f.h, f.E, f.H, f.I, f.Nd = h, gu["E"], gu["K"], gu["N"] // 2, dn["N"]
+        return f
+
     @staticmethod
     def _load(bank, qk, s, stream):
         lib = L.load()
