@@ -79,6 +79,16 @@ void onpu_moe_act(const float *h, int64_t rows, int64_t Ng, const int32_t *ids, 
                   float alpha, float limit, float *a);
 void onpu_moe_sum(const float *o, int64_t T, int k, int64_t N, const int32_t *ids, const float *w, const float *bias,
                   float *y);
+/* One decode token of softmax attention (onpu_cpu.cpp:173-229, same arguments): q [Hq][D] fp32;
+ * K, V: Hkv heads of S rows of D values (fp32, or bf16 for *_bf16), head stride hs and row stride
+ * rs in elements; mask [S] additive or NULL; sinks [Hq] extra logits or NULL; out [Hq][D] fp32.
+ * Host pointers, as in the reference; runs on the GPU (the cache rows are copied up each call).
+ * Needs Hq % Hkv == 0 with Hq / Hkv <= 16 and D <= 256 with D * (4 or 2) % 16 == 0; otherwise
+ * out is untouched and onpu_last_error() says why. */
+void onpu_attn_step(const float *q, int Hq, int D, const float *K, const float *V, int Hkv, int64_t S, int64_t hs,
+                    int64_t rs, const float *mask, const float *sinks, float scale, float *out);
+void onpu_attn_step_bf16(const float *q, int Hq, int D, const uint16_t *K, const uint16_t *V, int Hkv, int64_t S,
+                         int64_t hs, int64_t rs, const float *mask, const float *sinks, float scale, float *out);
 
 /* ---- fused routed-expert FFN (onpu_api.cpp:292-496) */
 void *onpu_ffn_new(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t E, int sym);
@@ -271,6 +281,14 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
 /* GPU layout -> plain codes q[N][K] (0..15), scales[N][K/32] (and mins for q4nx), device pointers;
  * for bit-exact verification. */
 int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream);
+
+/* onpu_attn_step on device pointers (a KV cache resident in HBM), asynchronous on `stream`:
+ * kv_bf16 selects a bf16 cache. K, V 16-byte aligned with hs and rs multiples of 16 bytes.
+ * 0 ok, < 0 error. Split-KV: each CTA streams a range of one kv head's rows once for all the
+ * query heads that share it; a second kernel merges the ranges. */
+int onpu_attn_step_dev(const float *q, int Hq, int D, const void *K, const void *V, int Hkv, int64_t S, int64_t hs,
+                       int64_t rs, const float *mask, const float *sinks, float scale, float *out, int kv_bf16,
+                       void *stream);
 
 /* ---- weight blobs: the GPU layout on disk (replaces what the reference's PackCache stores,
  * npu4/model.py:712-759: the packed upload bytes of one NPU buffer, so a second model load skips

@@ -161,4 +161,20 @@ cudaError_t moe_combine_launch(const float *o, int64_t ldo, int64_t T, int k, in
                                const float *w, const float *bias, float *y, int64_t ldy, cudaStream_t stream,
                                int id_lo = INT32_MIN, int id_hi = INT32_MAX);
 
+// ---- decode attention (attn.cu)
+struct AttnParams {
+    const float *q;                   // [Hq][D]
+    const void *k, *v;                // fp32 or bf16 cache: head kh, row j at kh * hs + j * rs (elements)
+    const float *mask, *sinks;        // [S] additive / [Hq] extra logits, or null
+    float *out;                       // [Hq][D]
+    int Hq, D, Hkv;
+    int64_t S, hs, rs;
+    float scale;
+    int tile_rows, rows_per_split, splits;
+    float *part_ml, *part_o;          // [Hq][splits][2] (max, sum), [Hq][splits][D]
+};
+int attn_tile_rows(int D, bool bf16);
+int attn_smem_bytes(int D, int rep, int R, bool bf16);
+cudaError_t attn_launch(const AttnParams &p, bool bf16, cudaStream_t stream);
+
 }  // namespace onpu_b200

@@ -2152,7 +2152,136 @@ BankH *bank_from_section(const MatHead &h, const uint8_t *payload, const char *w
 }
 }  // namespace
 
+// ------------------------------------------------------------------ decode attention
+namespace {
+struct AttnScratch {
+    float *part = nullptr;
+    int64_t part_cap = 0;
+    float *host_in = nullptr;         // staging of host-pointer calls (q, mask, sinks, K, V)
+    int64_t host_cap = 0;
+    float *host_out = nullptr;
+    int64_t out_cap = 0;
+};
+AttnScratch &attn_scratch() {
+    static AttnScratch a;
+    return a;
+}
+
+int attn_dev(const float *q, int Hq, int D, const void *K, const void *V, int Hkv, int64_t S, int64_t hs, int64_t rs,
+             const float *mask, const float *sinks, float scale, float *out, bool bf16, cudaStream_t s) {
+    const int elt = bf16 ? 2 : 4;
+    if (Hq <= 0 || Hkv <= 0 || Hq % Hkv || Hq / Hkv > 16 || D <= 0 || D > 256 || (D * elt) % 16 || S < 0 ||
+        S > (int64_t{1} << 31)) {
+        set_err("onpu_attn_step: need Hq %% Hkv == 0 with Hq / Hkv <= 16, 0 < D <= 256 with D * %d %% 16 == 0, "
+                "0 <= S < 2^31 (got Hq %d, Hkv %d, D %d, S %lld)", elt, Hq, Hkv, D, static_cast<long long>(S));
+        return -1;
+    }
+    if (S > 0 && ((reinterpret_cast<uintptr_t>(K) | reinterpret_cast<uintptr_t>(V)) & 15 || (hs * elt) % 16 ||
+                  (rs * elt) % 16 || rs < D)) {
+        set_err("onpu_attn_step: K and V must be 16-byte aligned with hs and rs multiples of 16 bytes and rs >= D");
+        return -1;
+    }
+    Ctx &c = ctx();
+    AttnScratch &a = attn_scratch();
+    AttnParams p{};
+    p.q = q;
+    p.k = K;
+    p.v = V;
+    p.mask = mask;
+    p.sinks = sinks;
+    p.out = out;
+    p.Hq = Hq;
+    p.D = D;
+    p.Hkv = Hkv;
+    p.S = S;
+    p.hs = hs;
+    p.rs = rs;
+    p.scale = scale;
+    p.tile_rows = attn_tile_rows(D, bf16);
+    // about two CTAs per SM over all kv heads, each split a whole number of tiles
+    const int64_t target = 2 * static_cast<int64_t>(c.nsm);
+    int64_t rows = (S * Hkv + target - 1) / target;
+    rows = std::max<int64_t>(p.tile_rows, (rows + p.tile_rows - 1) / p.tile_rows * p.tile_rows);
+    p.rows_per_split = static_cast<int>(std::min<int64_t>(rows, int64_t{1} << 30));
+    p.splits = S > 0 ? static_cast<int>((S + rows - 1) / rows) : 1;
+    if (!grow(a.part, a.part_cap, static_cast<int64_t>(Hq) * p.splits * (D + 2))) return -1;
+    p.part_ml = a.part;
+    p.part_o = a.part + static_cast<int64_t>(Hq) * p.splits * 2;
+    ONPU_CUDA(attn_launch(p, bf16, s), -1);
+    return 0;
+}
+
+// host-pointer form: stage q, mask, sinks and the cache rows [Hkv][S][D] on the device
+void attn_host(const float *q, int Hq, int D, const void *K, const void *V, int Hkv, int64_t S, int64_t hs, int64_t rs,
+               const float *mask, const float *sinks, float scale, float *out, bool bf16) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return;
+    }
+    if (Hq <= 0 || D <= 0 || S < 0 || Hkv <= 0 || (S > 0 && rs < D)) {
+        set_err("onpu_attn_step: bad sizes (Hq %d, D %d, Hkv %d, S %lld, rs %lld)", Hq, D, Hkv,
+                static_cast<long long>(S), static_cast<long long>(rs));
+        return;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    AttnScratch &a = attn_scratch();
+    const int elt = bf16 ? 2 : 4;
+    const int64_t nq = static_cast<int64_t>(Hq) * D, nkv = (static_cast<int64_t>(Hkv) * S * D * elt + 15) / 16 * 4;
+    const int64_t total = nq + (mask ? S : 0) + (sinks ? Hq : 0) + 2 * nkv + 16;
+    if (!grow(a.host_in, a.host_cap, total) || !grow(a.host_out, a.out_cap, nq)) return;
+    float *dq = a.host_in, *dm = dq + nq, *dsk = dm + (mask ? S : 0);
+    float *dk = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(dsk + (sinks ? Hq : 0)) + 15) & ~uintptr_t{15});
+    float *dv = dk + nkv;
+    cudaStream_t s = c.stream;
+    ONPU_CUDA(cudaMemcpyAsync(dq, q, nq * 4, cudaMemcpyHostToDevice, s), );
+    if (mask) ONPU_CUDA(cudaMemcpyAsync(dm, mask, S * 4, cudaMemcpyHostToDevice, s), );
+    if (sinks) ONPU_CUDA(cudaMemcpyAsync(dsk, sinks, Hq * 4, cudaMemcpyHostToDevice, s), );
+    const size_t row = static_cast<size_t>(D) * elt;
+    for (int kh = 0; kh < Hkv && S > 0; ++kh) {        // one strided copy per kv head and tensor
+        const auto *ks = static_cast<const uint8_t *>(K) + static_cast<int64_t>(kh) * hs * elt;
+        const auto *vs = static_cast<const uint8_t *>(V) + static_cast<int64_t>(kh) * hs * elt;
+        auto *kd = reinterpret_cast<uint8_t *>(dk) + static_cast<int64_t>(kh) * S * row;
+        auto *vd = reinterpret_cast<uint8_t *>(dv) + static_cast<int64_t>(kh) * S * row;
+        ONPU_CUDA(cudaMemcpy2DAsync(kd, row, ks, static_cast<size_t>(rs) * elt, row, static_cast<size_t>(S),
+                                    cudaMemcpyHostToDevice, s), );
+        ONPU_CUDA(cudaMemcpy2DAsync(vd, row, vs, static_cast<size_t>(rs) * elt, row, static_cast<size_t>(S),
+                                    cudaMemcpyHostToDevice, s), );
+    }
+    if (attn_dev(dq, Hq, D, dk, dv, Hkv, S, S * D, D, mask ? dm : nullptr, sinks ? dsk : nullptr, scale, a.host_out,
+                 bf16, s) != 0)
+        return;
+    ONPU_CUDA(cudaMemcpyAsync(out, a.host_out, nq * 4, cudaMemcpyDeviceToHost, s), );
+    ONPU_CUDA(cudaStreamSynchronize(s), );
+}
+}  // namespace
+
 extern "C" {
+
+void onpu_attn_step(const float *q, int Hq, int D, const float *K, const float *V, int Hkv, int64_t S, int64_t hs,
+                    int64_t rs, const float *mask, const float *sinks, float scale, float *out) {
+    attn_host(q, Hq, D, K, V, Hkv, S, hs, rs, mask, sinks, scale, out, false);
+}
+
+void onpu_attn_step_bf16(const float *q, int Hq, int D, const uint16_t *K, const uint16_t *V, int Hkv, int64_t S,
+                         int64_t hs, int64_t rs, const float *mask, const float *sinks, float scale, float *out) {
+    attn_host(q, Hq, D, K, V, Hkv, S, hs, rs, mask, sinks, scale, out, true);
+}
+
+int onpu_attn_step_dev(const float *q, int Hq, int D, const void *K, const void *V, int Hkv, int64_t S, int64_t hs,
+                       int64_t rs, const float *mask, const float *sinks, float scale, float *out, int kv_bf16,
+                       void *stream) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return -1;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    return attn_dev(q, Hq, D, K, V, Hkv, S, hs, rs, mask, sinks, scale, out, kv_bf16 != 0,
+                    static_cast<cudaStream_t>(stream));
+}
 
 int onpu_layout_version(void) { return kGpuLayoutVersion; }
 

@@ -40,6 +40,9 @@ SIGNATURES = {
     "onpu_moe_ffn": (None, [P, P, F, I64, I32P, I32, F, I32, C.c_float, C.c_float, F, F, F]),
     "onpu_moe_act": (None, [F, I64, I64, I32P, F, I32, C.c_float, C.c_float, F]),
     "onpu_moe_sum": (None, [F, I64, I32, I64, I32P, F, F, F]),
+    # same argtypes as the reference's binding (npu4/model.py:394-396)
+    "onpu_attn_step": (None, [F, I32, I32, F, F, I32, I64, I64, I64, F, F, C.c_float, F]),
+    "onpu_attn_step_bf16": (None, [F, I32, I32, F, F, I32, I64, I64, I64, F, F, C.c_float, F]),
     "onpu_ffn_new": (P, [I64, I64, I64, I64, I64, I32]),
     "onpu_ffn_gu": (P, [P]),
     "onpu_ffn_dn": (P, [P]),
@@ -64,6 +67,7 @@ SIGNATURES = {
     "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mm_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
+    "onpu_attn_step_dev": (I32, [P, I32, I32, P, P, I32, I64, I64, I64, P, P, C.c_float, P, I32, P]),
     "onpu_layout_version": (I32, []),
     "onpu_dense_export": (I64, [P, P, I64]),
     "onpu_dense_import": (P, [P, I64]),

@@ -15,6 +15,7 @@ packer). Reference lines followed (paths relative to the reference project root)
 - ``route``            opennpu/native/reference.py:71-76 (softmax -> topk -> renormalise)
 - ``moe_ffn``          opennpu/native/reference.py:77-84 (per-expert SwiGLU, weighted sum)
 - ``moe_act/moe_sum``  llama/ggml-opennpu/onpu_cpu.cpp:233-274
+- ``attn_step``        llama/ggml-opennpu/onpu_cpu.cpp:173-218 (decode attention, GQA, mask, sinks)
 
 Parity pin: tests/test_oracle.py checks these against the reference's own code — its Python
 imported in the container that generated tests/golden/*.npz (tests/golden/make_golden.py) and its
@@ -336,4 +337,55 @@ def ref_lib():
     L.onpu_quant_dequant.argtypes = [FP, I64, I64, C.c_int, FP, C.c_int]
     L.onpu_moe_act.argtypes = [FP, I64, I64, C.POINTER(C.c_int32), FP, C.c_int, C.c_float, C.c_float, FP]
     L.onpu_moe_sum.argtypes = [FP, I64, C.c_int, I64, C.POINTER(C.c_int32), FP, FP, FP]
+    at = [FP, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, I64, I64, I64, FP, FP, C.c_float, FP]
+    L.onpu_attn_step.argtypes = at
+    L.onpu_attn_step_bf16.argtypes = at
     return L
+
+
+# ------------------------------------------------------------------ decode attention
+def attn_step(q, K, V, mask=None, sinks=None, scale=None):
+    """One decode token of softmax attention, llama/ggml-opennpu/onpu_cpu.cpp:185-218, in float64
+    (a truth for the GPU's fp32 sums). q [Hq, D]; K, V [Hkv, S, D] (fp32 values; a bf16 cache is
+    passed widened); mask [S] additive; sinks [Hq]: an extra logit per head that takes probability
+    mass and has no value. Query head h reads kv head h // (Hq // Hkv). S = 0 gives zeros; every
+    score -inf with no sink gives NaN, as the reference's exp(-inf - -inf)."""
+    q = np.asarray(q, np.float64)
+    K = np.asarray(K, np.float64)
+    V = np.asarray(V, np.float64)
+    Hq, D = q.shape
+    Hkv, S, _ = K.shape
+    rep = Hq // Hkv
+    scale = D ** -0.5 if scale is None else scale
+    out = np.zeros((Hq, D), np.float64)
+    with np.errstate(invalid="ignore", over="ignore"):
+        for h in range(Hq):
+            s = (K[h // rep] @ q[h]) * scale
+            if mask is not None:
+                s = s + np.asarray(mask, np.float64)
+            mx = max([float(sinks[h])] if sinks is not None else [-np.inf])
+            if S:
+                mx = max(mx, float(s.max()))
+            p = np.exp(s - mx)
+            tot = p.sum() + (np.exp(float(sinks[h]) - mx) if sinks is not None else 0.0)
+            if S:
+                out[h] = (p / tot) @ V[h // rep]
+    return out
+
+
+def attn_step_ref(L, q, K, V, mask=None, sinks=None, scale=None, bf16=False):
+    """The reference's own onpu_attn_step(_bf16) from oracle/_ref on contiguous [Hkv, S, D] arrays
+    (K, V float32, or uint16 bf16 bits with bf16=True)."""
+    q = np.ascontiguousarray(q, np.float32)
+    K = np.ascontiguousarray(K)
+    V = np.ascontiguousarray(V)
+    Hq, D = q.shape
+    Hkv, S, _ = K.shape
+    out = np.zeros((Hq, D), np.float32)
+    fp = lambda a: None if a is None else np.ascontiguousarray(a, np.float32).ctypes.data_as(C.POINTER(C.c_float))
+    m = None if mask is None else np.ascontiguousarray(mask, np.float32)
+    sk = None if sinks is None else np.ascontiguousarray(sinks, np.float32)
+    f = L.onpu_attn_step_bf16 if bf16 else L.onpu_attn_step
+    f(fp(q), Hq, D, K.ctypes.data, V.ctypes.data, Hkv, S, S * D, D, fp(m), fp(sk),
+      float(D ** -0.5 if scale is None else scale), fp(out))
+    return out
