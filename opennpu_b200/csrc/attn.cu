@@ -55,7 +55,7 @@ struct Chunk<false> {
         const float4 v = *reinterpret_cast<const float4 *>(p);
         f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w;
     }
-    __device__ static float one(const float *p) { return *p; }
+    __device__ static float2 two(const float *p) { return *reinterpret_cast<const float2 *>(p); }
 };
 template <>
 struct Chunk<true> {
@@ -70,16 +70,20 @@ struct Chunk<true> {
             f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
         }
     }
-    __device__ static float one(const uint16_t *p) { return __uint_as_float(static_cast<uint32_t>(*p) << 16); }
+    __device__ static float2 two(const uint16_t *p) {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(p);
+        return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+    }
 };
 
-template <bool BF16>
+// DC: the head size as a compile-time constant (64, 128, 256), or 0 for any other (read from p)
+template <bool BF16, int DC>
 __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnParams p) {
     using C = Chunk<BF16>;
     using T = typename C::T;
     constexpr int kN = C::kN;
     extern __shared__ __align__(16) uint8_t smem[];
-    const int D = p.D, rep = p.Hq / p.Hkv, R = p.tile_rows, cpr = D / kN;   // 16-byte chunks per row
+    const int D = DC ? DC : p.D, rep = p.Hq / p.Hkv, R = p.tile_rows, cpr = D / kN;   // 16-byte chunks per row
     const int kh = blockIdx.y, split = blockIdx.x, tid = threadIdx.x;
     const int64_t j0 = static_cast<int64_t>(split) * p.rows_per_split;
     const int64_t j1 = min(p.S, j0 + p.rows_per_split);
@@ -133,15 +137,24 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnPara
             if (r < rows) {
                 const float *qh = qs + h * D;
                 const T *kr = kt + r * D;
-                float acc = 0.f;
+                float acc[4] = {0.f, 0.f, 0.f, 0.f};        // independent chains
+                const int rot = r % cpr;                      // once per score, not per chunk
+#pragma unroll(DC ? DC / kN : 1)
                 for (int c0 = 0; c0 < cpr; ++c0) {
-                    const int c = (c0 + r) % cpr;
+                    int c = c0 + rot;
+                    c -= c >= cpr ? cpr : 0;
                     float f[kN];
                     C::get(kr + c * kN, f);
 #pragma unroll
-                    for (int e = 0; e < kN; ++e) acc = fmaf(qh[c * kN + e], f[e], acc);
+                    for (int e = 0; e < kN; e += 4) {
+                        const float4 qv = *reinterpret_cast<const float4 *>(qh + c * kN + e);
+                        acc[0] = fmaf(qv.x, f[e], acc[0]);
+                        acc[1] = fmaf(qv.y, f[e + 1], acc[1]);
+                        acc[2] = fmaf(qv.z, f[e + 2], acc[2]);
+                        acc[3] = fmaf(qv.w, f[e + 3], acc[3]);
+                    }
                 }
-                s = acc * p.scale + (p.mask ? p.mask[t0 + r] : 0.f);
+                s = ((acc[0] + acc[1]) + (acc[2] + acc[3])) * p.scale + (p.mask ? p.mask[t0 + r] : 0.f);
             }
             sc[i] = s;
         }
@@ -167,13 +180,29 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnPara
             }
         }
         __syncthreads();
-        // outputs: one (head, d) per thread, rescaled by the new max, plus this tile's p . V
-        for (int i = tid; i < rep * D; i += kAttnThreads) {
-            const int h = i / D, d = i - h * D;
+        // outputs: two adjacent (head, d) per thread, rescaled by the new max, plus this tile's
+        // p . V (even and odd rows in separate sums)
+        for (int i = tid; i < rep * D / 2; i += kAttnThreads) {
+            const int h = (2 * i) / D, d = 2 * i - h * D;
             const float *ph = sc + h * R;
-            float o = os[i] * alpha[h];
-            for (int r = 0; r < rows; ++r) o = fmaf(ph[r], C::one(vt + r * D + d), o);
-            os[i] = o;
+            float2 ev = make_float2(0.f, 0.f), od = make_float2(0.f, 0.f);
+            int r = 0;
+            for (; r + 1 < rows; r += 2) {
+                const float2 v0 = C::two(vt + r * D + d), v1 = C::two(vt + (r + 1) * D + d);
+                const float p0 = ph[r], p1 = ph[r + 1];
+                ev.x = fmaf(p0, v0.x, ev.x);
+                ev.y = fmaf(p0, v0.y, ev.y);
+                od.x = fmaf(p1, v1.x, od.x);
+                od.y = fmaf(p1, v1.y, od.y);
+            }
+            if (r < rows) {
+                const float2 v0 = C::two(vt + r * D + d);
+                ev.x = fmaf(ph[r], v0.x, ev.x);
+                ev.y = fmaf(ph[r], v0.y, ev.y);
+            }
+            float2 *o = reinterpret_cast<float2 *>(os + h * D + d);
+            const float a = alpha[h];
+            *o = make_float2(fmaf(o->x, a, ev.x + od.x), fmaf(o->y, a, ev.y + od.y));
         }
         __syncthreads();        // the buffer read here is refilled by the next iteration's issue
     }
@@ -189,36 +218,79 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnPara
     }
 }
 
-// per query head: merge the splits' (max, sum, output) and the sink
-__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
-    const int h = blockIdx.x, D = p.D, splits = p.splits;
+// per query head: merge the splits' (max, sum, output) and the sink. The splits' weights
+// exp(m_s - m) go to shared memory once; each warp then sums a share of the splits for 128
+// outputs at a time (4 per lane, float4 loads all in flight), and the warps' sums are added
+// in shared memory.
+constexpr int kCombineThreads = 256, kCombineWarps = kCombineThreads / 32;
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float *red) {
+    v = is_max ? warp_max(v) : warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();                      // red is reused between calls
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float r = red[0];
+    for (int w = 1; w < kCombineWarps; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+    return r;
+}
+
+__global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const AttnParams p) {
+    extern __shared__ float wsm[];        // [splits] weights
+    __shared__ float red[kCombineWarps];
+    __shared__ float4 acc[kCombineWarps][32];
+    const int h = blockIdx.x, D = p.D, splits = p.splits, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const float *ml = p.part_ml + static_cast<int64_t>(h) * splits * 2;
     const float *po = p.part_o + static_cast<int64_t>(h) * splits * D;
     float *out = p.out + static_cast<int64_t>(h) * D;
     if (p.S == 0) {                       // no rows: the reference's output stays zero
-        for (int d = threadIdx.x; d < D; d += blockDim.x) out[d] = 0.f;
+        for (int d = tid; d < D; d += kCombineThreads) out[d] = 0.f;
         return;
     }
     const float sink = p.sinks ? p.sinks[h] : -INFINITY;
-    float m = sink;
-    for (int s = 0; s < splits; ++s) m = fmaxf(m, ml[2 * s]);
+    float m = -INFINITY;
+    for (int s = tid; s < splits; s += kCombineThreads) m = fmaxf(m, ml[2 * s]);
+    m = fmaxf(block_reduce(m, true, red), sink);
     if (m == -INFINITY) {                 // every score -inf and no sink: exp(-inf - -inf) in the reference
-        for (int d = threadIdx.x; d < D; d += blockDim.x) out[d] = NAN;
+        for (int d = tid; d < D; d += kCombineThreads) out[d] = NAN;
         return;
     }
-    float l = p.sinks ? expf(sink - m) : 0.f;
-    for (int s = 0; s < splits; ++s) {
-        const float ms = ml[2 * s];
-        if (ms != -INFINITY) l += ml[2 * s + 1] * expf(ms - m);
+    float l = 0.f;
+    for (int s = tid; s < splits; s += kCombineThreads) {
+        const float ms = ml[2 * s], w = ms == -INFINITY ? 0.f : expf(ms - m);
+        wsm[s] = w;
+        l = fmaf(ml[2 * s + 1], w, l);
     }
+    l = block_reduce(l, false, red) + (p.sinks ? expf(sink - m) : 0.f);   // also publishes wsm
     const float inv = 1.0f / l;
-    for (int d = threadIdx.x; d < D; d += blockDim.x) {
-        float o = 0.f;
-        for (int s = 0; s < splits; ++s) {
-            const float ms = ml[2 * s];
-            if (ms != -INFINITY) o = fmaf(po[static_cast<int64_t>(s) * D + d], expf(ms - m), o);
+    for (int d0 = 0; d0 < D; d0 += 128) {                 // D % 4 == 0
+        const int d = d0 + 4 * lane;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (d < D) {
+#pragma unroll 4
+            for (int s = warp; s < splits; s += kCombineWarps) {
+                const float4 v = *reinterpret_cast<const float4 *>(po + static_cast<int64_t>(s) * D + d);
+                const float w = wsm[s];
+                o.x = fmaf(v.x, w, o.x);
+                o.y = fmaf(v.y, w, o.y);
+                o.z = fmaf(v.z, w, o.z);
+                o.w = fmaf(v.w, w, o.w);
+            }
         }
-        out[d] = o * inv;
+        acc[warp][lane] = o;
+        __syncthreads();
+        if (warp == 0 && d < D) {
+            float4 t = acc[0][lane];
+            for (int w = 1; w < kCombineWarps; ++w) {
+                const float4 u = acc[w][lane];
+                t.x += u.x; t.y += u.y; t.z += u.z; t.w += u.w;
+            }
+            out[d] = t.x * inv;           // scalar stores: out is only 4-byte aligned
+            out[d + 1] = t.y * inv;
+            out[d + 2] = t.z * inv;
+            out[d + 3] = t.w * inv;
+        }
+        __syncthreads();
     }
 }
 
@@ -226,7 +298,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
 
 int attn_tile_rows(int D, bool bf16) {
     const int row = D * (bf16 ? 2 : 4);
-    const int r = 16384 / row / 8 * 8;    // four tiles (two buffers of K and V) in <= 64 KB
+    const int r = 8192 / row / 8 * 8;     // four tiles (two buffers of K and V) in <= 32 KB: ~6 CTAs per SM
     return r < 8 ? 8 : (r > 64 ? 64 : r);
 }
 
@@ -239,19 +311,20 @@ cudaError_t attn_launch(const AttnParams &p, bool bf16, cudaStream_t stream) {
     if (p.S > 0) {
         const dim3 grid(p.splits, p.Hkv);
         cudaError_t e;
-        if (bf16) {
-            e = cudaFuncSetAttribute(attn_split_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (e != cudaSuccess) return e;
-            attn_split_kernel<true><<<grid, kAttnThreads, smem, stream>>>(p);
-        } else {
-            e = cudaFuncSetAttribute(attn_split_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-            if (e != cudaSuccess) return e;
-            attn_split_kernel<false><<<grid, kAttnThreads, smem, stream>>>(p);
+        void (*k)(AttnParams) = nullptr;
+        switch (p.D) {
+            case 64: k = bf16 ? attn_split_kernel<true, 64> : attn_split_kernel<false, 64>; break;
+            case 128: k = bf16 ? attn_split_kernel<true, 128> : attn_split_kernel<false, 128>; break;
+            case 256: k = bf16 ? attn_split_kernel<true, 256> : attn_split_kernel<false, 256>; break;
+            default: k = bf16 ? attn_split_kernel<true, 0> : attn_split_kernel<false, 0>; break;
         }
+        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        k<<<grid, kAttnThreads, smem, stream>>>(p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    attn_combine_kernel<<<p.Hq, 128, 0, stream>>>(p);
+    attn_combine_kernel<<<p.Hq, kCombineThreads, p.splits * sizeof(float), stream>>>(p);
     return cudaGetLastError();
 }
 

@@ -171,7 +171,7 @@ struct AttnParams {
     int64_t S, hs, rs;
     float scale;
     int tile_rows, rows_per_split, splits;
-    float *part_ml, *part_o;          // [Hq][splits][2] (max, sum), [Hq][splits][D]
+    float *part_ml, *part_o;          // [Hq][splits][2] (max, sum), [Hq][splits][D] (16-byte aligned)
 };
 int attn_tile_rows(int D, bool bf16);
 int attn_smem_bytes(int D, int rep, int R, bool bf16);

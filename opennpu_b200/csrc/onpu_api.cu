@@ -2198,15 +2198,16 @@ int attn_dev(const float *q, int Hq, int D, const void *K, const void *V, int Hk
     p.rs = rs;
     p.scale = scale;
     p.tile_rows = attn_tile_rows(D, bf16);
-    // about two CTAs per SM over all kv heads, each split a whole number of tiles
-    const int64_t target = 2 * static_cast<int64_t>(c.nsm);
+    // about four CTAs per SM over all kv heads, each split a whole number of tiles
+    const int64_t target = 4 * static_cast<int64_t>(c.nsm);
     int64_t rows = (S * Hkv + target - 1) / target;
     rows = std::max<int64_t>(p.tile_rows, (rows + p.tile_rows - 1) / p.tile_rows * p.tile_rows);
     p.rows_per_split = static_cast<int>(std::min<int64_t>(rows, int64_t{1} << 30));
     p.splits = S > 0 ? static_cast<int>((S + rows - 1) / rows) : 1;
-    if (!grow(a.part, a.part_cap, static_cast<int64_t>(Hq) * p.splits * (D + 2))) return -1;
+    const int64_t nml = round_up(static_cast<int64_t>(Hq) * p.splits * 2, 4);   // keeps part_o 16-byte aligned
+    if (!grow(a.part, a.part_cap, nml + static_cast<int64_t>(Hq) * p.splits * D)) return -1;
     p.part_ml = a.part;
-    p.part_o = a.part + static_cast<int64_t>(Hq) * p.splits * 2;
+    p.part_o = a.part + nml;
     ONPU_CUDA(attn_launch(p, bf16, s), -1);
     return 0;
 }
