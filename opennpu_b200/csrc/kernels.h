@@ -173,6 +173,12 @@ struct AttnParams {
     int tile_rows, rows_per_split, splits;
     float *part_ml, *part_o;          // [Hq][splits][2] (max, sum), [Hq][splits][D] (16-byte aligned)
 };
+// tensor-core form (bf16 cache, D 64 / 128, <= 8 query heads per kv head): each CTA of
+// attn_tc_warps() warps covers rows_per_split rows (a multiple of warps * attn_tc_rows())
+bool attn_use_tc(int D, int rep, bool bf16);
+int attn_tc_warps();
+int attn_tc_rows();
+int attn_ctas_per_sm(int D, int rep, bool bf16);
 int attn_tile_rows(int D, bool bf16);
 int attn_smem_bytes(int D, int rep, int R, bool bf16);
 cudaError_t attn_launch(const AttnParams &p, bool bf16, cudaStream_t stream);

@@ -2197,9 +2197,11 @@ int attn_dev(const float *q, int Hq, int D, const void *K, const void *V, int Hk
     p.hs = hs;
     p.rs = rs;
     p.scale = scale;
-    p.tile_rows = attn_tile_rows(D, bf16);
-    // about four CTAs per SM over all kv heads, each split a whole number of tiles
-    const int64_t target = 4 * static_cast<int64_t>(c.nsm);
+    const bool tc = attn_use_tc(D, Hq / Hkv, bf16);
+    p.tile_rows = tc ? attn_tc_warps() * attn_tc_rows() : attn_tile_rows(D, bf16);
+    // one wave of resident CTAs over all kv heads, each split a whole number of tiles
+    // (tensor-core form: of 16-row blocks for each of its warps)
+    const int64_t target = static_cast<int64_t>(attn_ctas_per_sm(D, Hq / Hkv, bf16)) * c.nsm;
     int64_t rows = (S * Hkv + target - 1) / target;
     rows = std::max<int64_t>(p.tile_rows, (rows + p.tile_rows - 1) / p.tile_rows * p.tile_rows);
     p.rows_per_split = static_cast<int>(std::min<int64_t>(rows, int64_t{1} << 30));
