@@ -350,6 +350,150 @@ def run_prefill(args):
 
 M_E, M_K, M_HIDDEN, M_INTER, M_LAYERS = 128, 8, 2048, 768, 48
 
+# ------------------------------------------------------------------ decode attention
+A_HQ, A_HKV, A_D, A_LAYERS = 32, 8, 128, 36          # Qwen3-8B
+
+
+def attn_step_bytes(S, layers=A_LAYERS):
+    return 2 * A_HKV * S * A_D * 2 * layers               # every layer's bf16 K and V read once
+
+
+def cpu_attn_sample(S, seconds=10.0, seed=0):
+    """The reference's own onpu_attn_step_bf16 (onpu_cpu.cpp:173-229, compiled into oracle/_ref;
+    its thread pool uses every host core) on one layer's cache of the same shape, repeated for
+    about `seconds`. Falls back to the oracle's numpy restatement when oracle/_ref is absent.
+    Returns (GB/s of cache read, cores, kind, sample)."""
+    from oracle import oracle as O
+    rng = np.random.default_rng(seed)
+    q = rng.normal(size=(A_HQ, A_D)).astype(np.float32)
+    K = O.f32_to_bf16_bits(rng.normal(size=(A_HKV, S, A_D)).astype(np.float32))
+    V = O.f32_to_bf16_bits(rng.normal(size=(A_HKV, S, A_D)).astype(np.float32))
+    L = O.ref_lib()
+    if L is not None:
+        run, kind = (lambda: O.attn_step_ref(L, q, K, V, bf16=True)), "reference"
+    else:
+        Kf, Vf = O.bf16_bits_to_f32(K), O.bf16_bits_to_f32(V)
+        run, kind = (lambda: O.attn_step(q, Kf, Vf)), "port"
+    run()
+    n, t0 = 0, time.perf_counter()
+    while True:
+        run()
+        n += 1
+        dt = time.perf_counter() - t0
+        if dt >= seconds:
+            break
+    gbs = attn_step_bytes(S, 1) * n / dt / 1e9
+    sample = f"{n} x one Qwen3-8B layer's decode attention (Hq 32, Hkv 8, D 128, S {S}, bf16 cache)"
+    return gbs, os.cpu_count(), kind, sample
+
+
+def run_attn(args):
+    """Config attn: one decode token's attention over all 36 layers of Qwen3-8B at `--context`
+    tokens (bf16 KV caches, 604 MB at 4k: larger than L2), through onpu_attn_step_dev, the step's
+    36 calls captured in a CUDA graph as the other configs' steps are."""
+    from opennpu_b200 import libonpu as L
+    from opennpu_b200.attn import attn_step
+    rank, world, local = dist_setup(args.gpus)
+    hbm_peak, _, peak_kind = peaks()
+    S = args.context
+    g = torch.Generator(device="cuda").manual_seed(3000 + rank)
+    q = torch.randn(A_HQ, A_D, device="cuda", generator=g)
+    ks = [torch.randn(A_HKV, S, A_D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(A_LAYERS)]
+    vs = [torch.randn(A_HKV, S, A_D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(A_LAYERS)]
+    out = torch.empty(A_HQ, A_D, device="cuda")
+    s = torch.cuda.Stream()
+
+    def step():
+        for k, v in zip(ks, vs):
+            attn_step(q, k, v, out=out, stream=s)
+
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            step()
+    s.synchronize()
+    assert L.load().onpu_check_device() == 0, L.last_error()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        step()
+    with torch.cuda.stream(s):
+        for _ in range(args.warmup):
+            graph.replay()
+    s.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(args.steps):
+            graph.replay()
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1)
+    clk = clocks.stop()
+    assert L.load().onpu_check_device() == 0, L.last_error()
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_step = ms / args.steps
+    nbytes = attn_step_bytes(S)
+    gbs = nbytes * world / (ms_step * 1e-3) / 1e9
+    us_call = ms_step * 1e3 / A_LAYERS
+
+    e2e = None
+    if not args.no_e2e:
+        # the reference ABI: host q, host caches (copied up by the library each call), host out
+        lib = L.load()
+        hk = [k.cpu().view(torch.int16).numpy() for k in ks[:4]]
+        hv = [v.cpu().view(torch.int16).numpy() for v in vs[:4]]
+        hq = q.cpu().numpy()
+        ho = np.empty((A_HQ, A_D), np.float32)
+        fp = lambda a: a.ctypes.data_as(L.F)
+        n_e2e, t0 = 0, None
+        for i in range(2 + 3):
+            if i == 2:
+                t0 = time.perf_counter()
+            for l in range(A_LAYERS):
+                lib.onpu_attn_step_bf16(fp(hq), A_HQ, A_D, fp(hk[l % 4]), fp(hv[l % 4]), A_HKV, S, S * A_D, A_D,
+                                        None, None, A_D ** -0.5, fp(ho))
+            n_e2e += i >= 2
+        assert L.last_error() is None, L.last_error()
+        dt = (time.perf_counter() - t0) / n_e2e
+        e2e = {"value": round(nbytes / dt / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": A_LAYERS * (2 * A_HKV * S * A_D * 2 + A_HQ * A_D * 4),
+               "d2h_bytes_per_step": A_LAYERS * A_HQ * A_D * 4, "ms_per_step": round(dt * 1e3, 3),
+               "path": "onpu_attn_step_bf16 (the reference ABI: host q, host caches copied up each call, "
+                       "host out), 36 calls per step"}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, kind, sample = cpu_attn_sample(S, seconds=args.cpu_seconds)
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": sample}
+    if rank == 0:
+        achieved = attn_step_bytes(S, 1) / (us_call * 1e-6) / 1e9
+        traffic = json.loads((ROOT / "profiles" / "traffic.json").read_text()).get(f"attn/{S}")
+        line = {
+            "metric": "decode attention KV-cache GB/s (Qwen3-8B, 36 layers, bf16 cache)", "value": round(gbs, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 cache, fp32 arithmetic (q and P as three bf16 parts on the tensor cores)",
+            "data": "synthetic (seeded N(0,1) q and caches)",
+            "config": {"workload": "qwen3-8b-decode-attention", "context": S, "layers": A_LAYERS,
+                       "heads": f"{A_HQ} query / {A_HKV} kv, D {A_D}", "parallelism": f"replicas{world}",
+                       "l2": "36 distinct caches, larger than L2 (no flush needed)", "cuda_graph": True},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                         "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": "attn_split_tc_kernel<128> + attn_combine_kernel (one call, one layer)",
+                         "algorithmic_bytes_per_launch": attn_step_bytes(S, 1), "us_per_launch": round(us_call, 3)},
+            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": 2 * A_LAYERS * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
 
 def moe_expert_bytes():
     """int4 codes + fp16 scales of one expert's gate_up (1536x2048) and down (2048x768)."""
@@ -1061,7 +1205,7 @@ def run_reference(args):
     n_steps = args.warmup + args.steps
     per = max(0.2, min(1.0, 120.0 / n_steps))                # the whole arm stays near two minutes
     cfg = args.config
-    vals, sample, cores = [], None, None
+    vals, sample, cores, kind = [], None, None, "port"
     for i in range(n_steps):
         if cfg in ("qwen3-8b", "gemv"):
             v, _, cores, sample = cpu_reference_sample(M, seconds=per, seed=i)
@@ -1069,6 +1213,8 @@ def run_reference(args):
             v, cores, sample = cpu_prefill_sample(seconds=per)
         elif cfg == "moe":
             v, cores, sample = cpu_moe_sample(max(M, 1), seconds=per)
+        elif cfg == "attn":
+            v, cores, kind, sample = cpu_attn_sample(args.context, seconds=per, seed=i)
         else:
             gbs, cores, sample = cpu_tp_sample(M, seconds=per)
             from opennpu_b200 import tp
@@ -1088,12 +1234,16 @@ def run_reference(args):
                 "qwen3-30b-a3b-moe-layer"),
         "qwen2.5-32b": ("int4 dense decode stack tokens/s (Qwen2.5-32B, tensor-parallel)", "tokens/s",
                         "qwen2.5-32b-decode-projections-tp"),
+        "attn": ("decode attention KV-cache GB/s (Qwen3-8B, 36 layers, bf16 cache)", "GB/s",
+                 "qwen3-8b-decode-attention"),
     }[cfg]
     line = {"impl": "reference", "metric": metric, "value": round(v, 4), "unit": unit,
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int4 dequantised to fp32",
-            "data": "synthetic", "config": {"workload": workload, "M": M},
-            "cpu_baseline": {"value": round(v, 4), "unit": unit, "cores": cores, "kind": "port",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 cache, fp32 arithmetic" if cfg == "attn" else "int4 dequantised to fp32",
+            "data": "synthetic",
+            "config": {"workload": workload, "M": M, **({"context": args.context} if cfg == "attn" else {})},
+            "cpu_baseline": {"value": round(v, 4), "unit": unit, "cores": cores, "kind": kind,
                              "sample": f"per step ({per:.2f} s): {sample}"},
             "e2e": {"value": round(v, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -1105,7 +1255,8 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill", "moe", "qwen2.5-32b"])
+    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill", "moe", "qwen2.5-32b", "attn"])
+    ap.add_argument("--context", type=int, default=4096, help="attn: KV-cache length (tokens)")
     ap.add_argument("--m", "--rows", dest="m", type=int, default=1,
                     help="tokens (M / T); spell it --rows under torchrun, which claims --m")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
@@ -1128,6 +1279,8 @@ def main():
         run_moe(args)
     elif args.config == "qwen2.5-32b":
         run_tp(args)
+    elif args.config == "attn":
+        run_attn(args)
     else:
         run_ours(args)
 

@@ -567,23 +567,35 @@ cudaError_t attn_launch(const AttnParams &p, bool bf16, cudaStream_t stream) {
         const dim3 grid(p.splits, p.Hkv);
         const int tsm = kTcWarps * (4 * kTcRows * p.D * 2 + 8 * kTcRows * 2 * 4);
         void (*k)(AttnParams) = p.D == 64 ? attn_split_tc_kernel<64> : attn_split_tc_kernel<128>;
-        cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tsm);
-        if (e != cudaSuccess) return e;
+        static bool attr[2] = {false, false};       // set once per kernel (no call during a graph capture)
+        if (!attr[p.D == 128]) {
+            const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, tsm);
+            if (e != cudaSuccess) return e;
+            attr[p.D == 128] = true;
+        }
         k<<<grid, kTcWarps * 32, tsm, stream>>>(p);
-        e = cudaGetLastError();
+        const cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     } else if (p.S > 0) {
         const dim3 grid(p.splits, p.Hkv);
         cudaError_t e;
         void (*k)(AttnParams) = nullptr;
+        int slot = 0;
         switch (p.D) {
-            case 64: k = bf16 ? attn_split_kernel<true, 64> : attn_split_kernel<false, 64>; break;
-            case 128: k = bf16 ? attn_split_kernel<true, 128> : attn_split_kernel<false, 128>; break;
-            case 256: k = bf16 ? attn_split_kernel<true, 256> : attn_split_kernel<false, 256>; break;
-            default: k = bf16 ? attn_split_kernel<true, 0> : attn_split_kernel<false, 0>; break;
+            case 64: k = bf16 ? attn_split_kernel<true, 64> : attn_split_kernel<false, 64>; slot = 0; break;
+            case 128: k = bf16 ? attn_split_kernel<true, 128> : attn_split_kernel<false, 128>; slot = 1; break;
+            case 256: k = bf16 ? attn_split_kernel<true, 256> : attn_split_kernel<false, 256>; slot = 2; break;
+            default: k = bf16 ? attn_split_kernel<true, 0> : attn_split_kernel<false, 0>; slot = 3; break;
         }
-        e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess) return e;
+        // set once per kernel, to the most any head size and head grouping it serves can use
+        static bool attr[2][4] = {};
+        if (!attr[bf16][slot]) {
+            const int dmax = slot == 0 ? 64 : slot == 1 ? 128 : 256;
+            e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     attn_smem_bytes(dmax, 16, attn_tile_rows(dmax, bf16), bf16));
+            if (e != cudaSuccess) return e;
+            attr[bf16][slot] = true;
+        }
         k<<<grid, kAttnThreads, smem, stream>>>(p);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
