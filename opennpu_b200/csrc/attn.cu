@@ -18,6 +18,7 @@
 #include <cstdint>
 
 #include "kernels.h"
+#include "ptx.cuh"
 
 namespace onpu_b200 {
 namespace {
@@ -84,6 +85,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_split_kernel(const AttnPara
     using T = typename C::T;
     constexpr int kN = C::kN;
     extern __shared__ __align__(16) uint8_t smem[];
+    pdl_launch_dependents();              // the combine may launch now; it waits for this grid's end
     const int D = DC ? DC : p.D, rep = p.Hq / p.Hkv, R = p.tile_rows, cpr = D / kN;   // 16-byte chunks per row
     const int kh = blockIdx.y, split = blockIdx.x, tid = threadIdx.x;
     const int64_t j0 = static_cast<int64_t>(split) * p.rows_per_split;
@@ -264,6 +266,7 @@ __global__ void __launch_bounds__(kTcWarps * 32) attn_split_tc_kernel(const Attn
     constexpr int KS = D / 16;                      // k-steps of the score MMA, m-blocks of P . V
     constexpr int BLK = kTcRows * D;                // elements of one 16-row block
     extern __shared__ __align__(128) uint8_t smem[];
+    pdl_launch_dependents();              // the combine may launch now; it waits for this grid's end
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
     const int rep = p.Hq / p.Hkv, kh = blockIdx.y, split = blockIdx.x;
     // per warp: [2 stages][K, V][16 rows][D] bf16, then a 8 x 16 float transpose buffer
@@ -470,6 +473,7 @@ __device__ __forceinline__ float block_reduce(float v, bool is_max, float *red) 
 }
 
 __global__ void __launch_bounds__(kCombineThreads) attn_combine_kernel(const AttnParams p) {
+    pdl_wait_prerequisites();             // launched early (programmatic dependent launch): wait for the partials
     extern __shared__ float wsm[];        // [splits] weights
     __shared__ float red[kCombineWarps];
     __shared__ float4 acc[kCombineWarps][32];
@@ -600,8 +604,7 @@ cudaError_t attn_launch(const AttnParams &p, bool bf16, cudaStream_t stream) {
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
-    attn_combine_kernel<<<p.Hq, kCombineThreads, p.splits * sizeof(float), stream>>>(p);
-    return cudaGetLastError();
+    return launch_pdl(attn_combine_kernel, dim3(p.Hq), dim3(kCombineThreads), p.splits * sizeof(float), stream, p);
 }
 
 }  // namespace onpu_b200
