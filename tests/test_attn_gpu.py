@@ -112,3 +112,29 @@ def test_rejects_unsupported_shapes():
         attn_step(q, K, K)
     torch.cuda.synchronize()
     assert L.load().onpu_check_device() == 0, L.last_error()
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,S", [(64, 8, 64, 3000), (28, 4, 128, 2000), (8, 8, 64, 257)])
+def test_tensor_core_form_masks_and_sinks(Hq, Hkv, D, S):
+    """The bf16 tensor-core form at its limits (8 and 7 query heads per kv head, D 64 and 128) with
+    sinks and masks whose -inf runs blank whole splits, and a cache masked everywhere (NaN without
+    sinks, as the reference; zeros with them)."""
+    g = torch.Generator(device="cuda").manual_seed(Hq * S)
+    q = torch.randn(Hq, D, device="cuda", generator=g)
+    K = torch.randn(Hkv, S, D, device="cuda", generator=g).to(torch.bfloat16)
+    V = torch.randn(Hkv, S, D, device="cuda", generator=g).to(torch.bfloat16)
+    sk = torch.randn(Hq, device="cuda", generator=g)
+    mask = torch.zeros(S, device="cuda")
+    mask[: S // 2] = float("-inf")                       # the first half of the rows: many whole splits
+    mask[S // 2 + 3::7] = float("-inf")
+    Kf, Vf = K.float().cpu().numpy(), V.float().cpu().numpy()
+    for m, s in ((mask, sk), (mask, None), (None, sk)):
+        y = attn_step(q, K, V, m, s)
+        ref = O.attn_step(q.cpu().numpy(), Kf, Vf, None if m is None else m.cpu().numpy(),
+                          None if s is None else s.cpu().numpy())
+        assert_attn_close(y.cpu().numpy(), ref, TOL)
+    full = torch.full((S,), float("-inf"), device="cuda")
+    assert torch.isnan(attn_step(q, K, V, full)).all()
+    assert torch.equal(attn_step(q, K, V, full, sk), torch.zeros(Hq, D, device="cuda"))
+    torch.cuda.synchronize()
+    assert L.load().onpu_check_device() == 0, L.last_error()
