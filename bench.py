@@ -65,9 +65,13 @@ class DecodeStack:
     step is one GEMV chain (onpu_chain_*), every link ordered after its predecessor as in a real
     decode step; mode "launches": one onpu_dense_mv_dev launch per matrix."""
 
-    def __init__(self, M, seed, layers=LAYERS, mode="launches"):
+    def __init__(self, M, seed, layers=LAYERS, mode="launches", act="f32"):
         from opennpu_b200 import dense
         self.dense = dense
+        # act: the MLP activation between gate/up and down. "f32": the SwiGLU epilogue writes fp32
+        # and the down GEMV stages it as two fp16 halves per value (the reference's fp32 chain,
+        # reference.py:55-57, :84); "bf16": rounded once to bf16 (the reference's NPU input rounding)
+        self.act = "bf16" if mode == "chain" else act
         self.M, self.mode = M, mode
         gen = torch.Generator(device="cuda")
         gen.manual_seed(seed)
@@ -80,15 +84,19 @@ class DecodeStack:
                 del qk, s
             self.layers.append(mats)
         torch.cuda.synchronize()
+        if M > self.layers[0]["down"].max_f32_rows():
+            self.act = "bf16"                 # the fp32 rows would not fit in shared memory
         self.x_all = torch.randn(layers, M, HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
         self.x = [self.x_all[l] for l in range(layers)]
         self.y_qkv = torch.empty(M, QKV_N, device="cuda")
-        self.a = torch.empty(M, INTER, device="cuda", dtype=torch.bfloat16)
+        self.a = torch.empty(M, INTER, device="cuda", dtype=torch.float32 if self.act == "f32" else torch.bfloat16)
+        self.epi_gu = dense.EPI_SWIGLU_F32 if self.act == "f32" else dense.EPI_SWIGLU
         self.y = torch.empty(M, HIDDEN, device="cuda")
         per_layer = 0
         for name, N, K, gu in qwen3_8b_matrices():
             per_layer += int4_param_bytes(N, K) + M * K * 2
-        per_layer += M * QKV_N * 4 + M * INTER * 2 + M * HIDDEN * 4
+        per_layer += M * QKV_N * 4 + M * INTER * self.a.element_size() + M * HIDDEN * 4
+        per_layer += M * INTER * (self.a.element_size() - 2)          # down reads the activation
         self.bytes_per_step = per_layer * layers
         self.weight_bytes_per_step = sum(int4_param_bytes(N, K) for _, N, K, _ in qwen3_8b_matrices()) * layers
         self.chain = None
@@ -110,21 +118,20 @@ class DecodeStack:
         if self.chain is not None:
             return self.chain.run, self.bytes_per_step, 1, "gemv_chain_kernel (one launch = the whole step)"
         N, K = 2 * INTER, HIDDEN
-        nbytes = int4_param_bytes(N, K) + self.M * K * 2 + self.M * INTER * 2
+        nbytes = int4_param_bytes(N, K) + self.M * K * 2 + self.M * INTER * self.a.element_size()
 
         def run():
             for l, mats in enumerate(self.layers):
-                mats["gate_up"].mv(self.x[l], out=self.a, epi=d.EPI_SWIGLU)
+                mats["gate_up"].mv(self.x[l], out=self.a, epi=self.epi_gu)
         return run, nbytes, len(self.layers), "gemv_int4_kernel gate_up 24576x4096 + SwiGLU"
 
     def step(self):
         if self.chain is not None:
             self.chain.run()
             return
-        d = self.dense
         for l, mats in enumerate(self.layers):
             mats["qkv"].mv(self.x[l], out=self.y_qkv)
-            mats["gate_up"].mv(self.x[l], out=self.a, epi=d.EPI_SWIGLU)
+            mats["gate_up"].mv(self.x[l], out=self.a, epi=self.epi_gu)
             mats["down"].mv(self.a, out=self.y)
 
     def step_e2e(self, hx, hy_qkv, hy):
@@ -722,7 +729,9 @@ class TPStack:
     """Qwen2.5-32B decode projections, 64 layers of random int4 weights, tensor-parallel
     over the ranks: q/k/v and gate/up column-parallel (row blocks), o and down row-parallel (K
     blocks on 32-group boundaries) with an all-reduce of the fp32 partial outputs after each. Each
-    rank generates only its own shards. The layer input of layer l+1 is layer l's output (bf16)."""
+    rank generates only its own shards. The layer input of layer l+1 is layer l's output: fp32 for
+    decode (M <= 8: every activation stays fp32, each GEMV stages it as two fp16 halves), else
+    rounded to bf16."""
 
     def __init__(self, M, rank, world, group, seed, layers=T_LAYERS, allreduce=None):
         from opennpu_b200 import tp
@@ -741,19 +750,25 @@ class TPStack:
             del qkv, o, gu, dn
         torch.cuda.synchronize()
         self.M, self.world = M, world
-        self.x = torch.randn(M, T_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+        self.f32 = M <= min(lay.f32_rows for lay in self.layers)
+        x = torch.randn(M, T_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+        self.x = x.float() if self.f32 else x
         self.xs = [torch.empty(M, T_HIDDEN, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
         self.bufs = self.layers[0].buffers(M)
         shards = [(q + 2 * kv, T_HIDDEN), (T_HIDDEN, h_r), (2 * i_r, T_HIDDEN), (T_HIDDEN, i_r)]
-        self.bytes_per_layer = sum(int4_param_bytes(N, K) + M * K * 2 + M * N * 4 for N, K in shards)
+        xb = 4 if self.f32 else 2
+        self.bytes_per_layer = sum(int4_param_bytes(N, K) + M * K * xb + M * N * 4 for N, K in shards)
         self.launches_per_step = 4 * layers                   # our GEMVs (plus NCCL all-reduces, casts)
 
     def step(self):
         x = self.x
         for i, lay in enumerate(self.layers):
-            nx = self.xs[i & 1]
-            lay(x, self.bufs, y_bf16=nx)
-            x = nx
+            if self.f32:
+                x = lay(x, self.bufs)               # fp32 output, the next layer's input
+            else:
+                nx = self.xs[i & 1]
+                lay(x, self.bufs, y_bf16=nx)
+                x = nx
         return self.bufs["y"]
 
 
@@ -837,7 +852,7 @@ def run_tp(args):
 
     e2e = None
     if not args.no_e2e:
-        hx = torch.empty(work.x.shape, dtype=torch.bfloat16, pin_memory=True)
+        hx = torch.empty(work.x.shape, dtype=work.x.dtype, pin_memory=True)
         hx.copy_(work.x)
         hy = torch.empty(work.bufs["y"].shape, dtype=torch.float32, pin_memory=True)
         with torch.cuda.stream(s):
@@ -855,7 +870,7 @@ def run_tp(args):
             t = torch.tensor([dt], device="cuda")
             torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
             dt = float(t.item())
-        e2e = {"value": round(M / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": hx.numel() * 2,
+        e2e = {"value": round(M / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": hx.numel() * hx.element_size(),
                "d2h_bytes_per_step": hy.numel() * 4, "ms_per_step": round(dt * 1e3, 3),
                "path": "TPDecoderLayer stack (onpu_dense_mv_dev; row-parallel o/down fused with the peer all-reduce, or NCCL) from a CUDA graph, pinned host "
                        "input/output copies and a host synchronisation per step"}
@@ -868,7 +883,8 @@ def run_tp(args):
             "metric": "int4 dense decode stack tokens/s (Qwen2.5-32B, tensor-parallel)", "value": round(tok_s, 2),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "dtype": "int4 weights, " + ("fp32 activations (two fp16 halves)" if work.f32 else "bf16 activations")
+                     + ", fp32 accumulate",
             "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1))",
             "config": {"workload": "qwen2.5-32b-decode-projections-tp", "M": M, "layers": layers,
                        "parallelism": f"tp{world}", "gb_per_s_all_ranks": round(gbs_rank * world, 1),
@@ -1041,7 +1057,8 @@ def run_ours(args):
     rank, world, local = dist_setup(args.gpus)
     hbm, _, peak_kind = peaks()
     M = args.m
-    work = (DecodeStack(M, seed=1000 + rank, layers=args.layers, mode=args.mode) if args.config == "qwen3-8b"
+    work = (DecodeStack(M, seed=1000 + rank, layers=args.layers, mode=args.mode, act=args.act)
+            if args.config == "qwen3-8b"
             else GemvRotation(M, seed=1000 + rank))
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
@@ -1178,7 +1195,8 @@ def run_ours(args):
                        "weight_bytes_per_step_per_gpu": work.weight_bytes_per_step,
                        "parallelism": f"replicas{world}", "l2": "inputs larger than L2 (no flush needed)",
                        "cuda_graph": graph is not None,
-                       "mode": args.mode if args.config == "qwen3-8b" else "launches"},
+                       "mode": args.mode if args.config == "qwen3-8b" else "launches",
+                       "mlp_activation": getattr(work, "act", None)},
             "tokens_per_s": round(M * world / (ms_step * 1e-3), 1) if args.config == "qwen3-8b" else None,
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic,
@@ -1264,6 +1282,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--act", default="f32", choices=["f32", "bf16"],
+                    help="qwen3-8b: the MLP activation between gate/up and down (fp32, or rounded to bf16)")
     ap.add_argument("--mode", default="launches", choices=["chain", "launches"],
                     help="chain: the step as one persistent GEMV-chain launch; launches: one launch per matrix")
     ap.add_argument("--layers", type=int, default=LAYERS,

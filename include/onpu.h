@@ -123,6 +123,8 @@ void onpu_quant_dequant(const float *W, int64_t N, int64_t K, int sym, float *ou
                           /* matrix created with onpu_dense_new_int4(..., gateup = 1)     */
 #define ONPU_EPI_PAIRSUM 3 /* y[i] = acc[row i] + acc[residual of row i], fp32; needs a    */
                            /* matrix from onpu_dense_new_residual_f32_dev                 */
+#define ONPU_EPI_SWIGLU_F32 5 /* as ONPU_EPI_SWIGLU with fp32 y: the activation keeps full     */
+                              /* precision for an fp32-input down projection (onpu_dense_mv_f32_dev) */
 
 /* Last error message of this thread (NULL if the last failing-capable call succeeded). */
 const char *onpu_last_error(void);
@@ -160,6 +162,18 @@ int onpu_dense_info(void *h, int64_t *out4);
  * device (by epi). A first call for a given row count allocates (call it outside stream capture);
  * later calls with that row count allocate nothing. 0 ok, < 0 error. */
 int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream);
+/* onpu_dense_mv_dev with fp32 activations x [rows][ldx] (device, 16-byte aligned rows, ldx % 4 ==
+ * 0), rows <= 8: each value is staged as two fp16 halves (x rounded, then its rounding error) on
+ * two tensor-core columns whose products are added, so the products keep ~22 bits of x instead of
+ * bf16's 8: the down projection of a decode MLP can take ONPU_EPI_SWIGLU_F32's output and match
+ * the reference's fp32 dequantise-then-matmul path (opennpu/native/reference.py:55-57, :84)
+ * without rounding the activation. Same epilogues, outputs and allocation rule. 0 ok, < 0 error. */
+int onpu_dense_mv_f32_dev(void *h, const float *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi,
+                          void *stream);
+/* The most rows (0..8) onpu_dense_mv_f32_dev takes for this matrix: each CTA keeps its part of
+ * the two fp16 rows per token in shared memory (e.g. 3 for a 4096 x 12288 down projection on one
+ * B200, 8 for its tensor-parallel shards). 0 without a usable device. */
+int onpu_dense_max_f32_rows(void *h);
 /* Y = X . W^T for many tokens (prefill) on the tensor cores (tcgen05, fp32 accumulators in tensor
  * memory); same arguments as onpu_dense_mv_dev, any rows >= 1. The weights are dequantised to
  * fp16 (one rounding per weight) and the activations copied to fp16 first (a token beyond the fp16
@@ -191,7 +205,8 @@ void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t 
  * x bf16 [T][ldx], ids/w from onpu_route_dev (device), y fp32 [T][ldy]. Four launches on `stream`,
  * no host synchronisation (capturable in a CUDA graph once a first call has sized the scratch):
  * the token-sorted expert jobs are built on the device from the ids, then gate_up (fused SwiGLU,
- * bf16 activations), down and the weighted combine. An id outside [0, E) drops that (token, slot)
+ * fp32 activation), down (the activation staged as two fp16 halves per value, so it is not
+ * rounded to 16 bits) and the weighted combine. An id outside [0, E) drops that (token, slot)
  * pair and sets the device status (onpu_check_device reports it). At most 2048 experts. Replaces
  * opennpu/native/reference.py:77-84 and the device part of onpu_moe_ffn
  * (llama/ggml-opennpu/onpu_api.cpp:261-278). 0 ok, < 0 error. */
@@ -235,6 +250,9 @@ void onpu_comm_free(void *comm);
  * them in rank order. Same call-sequence rule as onpu_comm_allreduce. 0 ok, < 0 error. */
 int onpu_dense_mv_allreduce_dev(void *h, void *comm, const void *x, int64_t ldx, int64_t rows, float *y,
                                 void *y_bf16, void *stream);
+/* The same with fp32 activations (rows <= 8, staged as in onpu_dense_mv_f32_dev). */
+int onpu_dense_mv_allreduce_f32_dev(void *h, void *comm, const float *x, int64_t ldx, int64_t rows, float *y,
+                                    void *y_bf16, void *stream);
 /* ---- GEMV chains: a decode step's dense GEMVs recorded once on fixed device buffers and run as
  * ONE persistent launch (the GPU analogue of the reference's instruction stream per call,
  * llama/ggml-opennpu/opennpu_core.hpp:418-505, and of onpu_ffn_run's gate_up -> act -> down
@@ -270,12 +288,14 @@ void onpu_chain_free(void *chain);
 int onpu_gemv_trace(uint64_t *stamps, int64_t ctas);
 
 /* onpu_dense_mv_dev with no allocation in the call: no reference counterpart (the NPU library
- * has no device scratch). Same arguments and result as onpu_dense_mv_dev, but the split-row
- * scratch and descriptors live in one static device array shared by every call on a device, for
- * callers that cannot let the library allocate (all free HBM handed to their own pool, or a fixed
- * device footprint). rows <= 256 per call, else -1 with an error message. The first call on a
- * device looks up the array (cudaGetSymbolAddress) and clears it; make that first call before any
- * stream capture. Overlapping calls race: order them on one stream. */
+ * has no device scratch). Same arguments, epilogues (ONPU_EPI_PAIRSUM and ONPU_EPI_SWIGLU_F32
+ * included) and bit-identical results as onpu_dense_mv_dev (the same grid, so the same summation
+ * order), but the split-row scratch and descriptors live in one static device array shared by
+ * every call on a device, for callers that cannot let the library allocate (all free HBM handed to
+ * their own pool, or a fixed device footprint). rows <= 256 per call, else -1 with an error
+ * message. The descriptors are written on the device by a small kernel on `stream` before the
+ * GEMV. The first call on a device looks up the array (cudaGetSymbolAddress) and clears it; make
+ * that first call before any stream capture. Overlapping calls race: order them on one stream. */
 int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi,
                               void *stream);
 /* GPU layout -> plain codes q[N][K] (0..15), scales[N][K/32] (and mins for q4nx), device pointers;

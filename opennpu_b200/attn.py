@@ -25,49 +25,3 @@ def attn_step(q, k, v, mask=None, sinks=None, scale=None, out=None, stream=None)
         float(D ** -0.5 if scale is None else scale), out.data_ptr(), int(k.dtype == torch.bfloat16), s.cuda_stream)
     L.check(rc, "onpu_attn_step_dev")
     return out
-
-
-def _main():
-    """Time onpu_attn_step_dev: CUDA events over many calls queued behind a GPU sleep (so the
-    host's call rate does not bound them), distinct caches per call so the working set exceeds
-    the L2. Prints one JSON line per shape: microseconds per call and cache GB/s."""
-    import argparse
-    import json
-    ap = argparse.ArgumentParser(description=_main.__doc__)
-    ap.add_argument("--shapes", nargs="*", default=["32,8,128,4096,bf16", "32,8,128,32768,bf16",
-                                                    "40,8,128,8192,bf16", "64,8,64,8192,f32"],
-                    help="Hq,Hkv,D,S,dtype (bf16 or f32)")
-    ap.add_argument("--caches", type=int, default=16)
-    ap.add_argument("--iters", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=3)
-    a = ap.parse_args()
-    for spec in a.shapes:
-        Hq, Hkv, D, S, dt = spec.split(",")
-        Hq, Hkv, D, S = int(Hq), int(Hkv), int(D), int(S)
-        dtype = torch.bfloat16 if dt == "bf16" else torch.float32
-        g = torch.Generator(device="cuda").manual_seed(S)
-        q = torch.randn(Hq, D, device="cuda", generator=g)
-        ks = [torch.randn(Hkv, S, D, device="cuda", generator=g).to(dtype) for _ in range(a.caches)]
-        vs = [torch.randn(Hkv, S, D, device="cuda", generator=g).to(dtype) for _ in range(a.caches)]
-        out = torch.empty(Hq, D, device="cuda")
-        for _ in range(a.warmup):
-            for k, v in zip(ks, vs):
-                attn_step(q, k, v, out=out)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda._sleep(200_000_000)
-        e0.record()
-        for _ in range(a.iters):
-            for k, v in zip(ks, vs):
-                attn_step(q, k, v, out=out)
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (a.iters * a.caches)
-        nbytes = 2 * Hkv * S * D * ks[0].element_size()
-        print(json.dumps(dict(Hq=Hq, Hkv=Hkv, D=D, S=S, cache=dt, us_per_call=round(us, 2),
-                              cache_GBs=round(nbytes / us / 1e3, 1), launches_per_call=2)))
-        del ks, vs
-
-
-if __name__ == "__main__":
-    _main()

@@ -258,8 +258,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_chain_kernel(const __grid_co
             named_bar_sync(1, kConsumers * 32);       // also: every warp is done with the previous link's x
             if (trace) trace[1] = global_timer_ns();
             const int m = opp->m, xstride = opp->xstride, ctab_off = opp->ctab_off;
-            stage_activations<FMT, NT, true>(opp->x, opp->ldx, [](int n) { return n; }, m, m, opp->K, xstride, smem + p.off_x,
-                                   threadIdx.x, kConsumers * 32);
+            stage_activations<FMT, NT, true, false, 4>(opp->x, opp->ldx, [](int n) { return n; }, m, m, opp->K, 0,
+                                                       chunks, chunks, xstride, smem + p.off_x, threadIdx.x,
+                                                       kConsumers * 32);
             if (trace) trace[2] = global_timer_ns();
 
             // ---- this lane's activation rows, output rows

@@ -34,6 +34,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "gemv_core.cuh"
 #include "gpu_layout.cuh"
 #include "kernels.h"
@@ -54,8 +56,13 @@ __device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, in
         const int i = g * (kRowGroup / 2) + s * 8 + r;       // row r and row r+8 of the strip pair up
         if (i < p.N / 2) {
             const int64_t o = static_cast<int64_t>(yr) * p.ldy + i;
-            if constexpr (EPI == kEpiSwiGLU) reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(silu_f(v_lo) * v_hi);
-            else reinterpret_cast<float *>(p.y)[o] = v_lo + v_hi;
+            if constexpr (EPI == kEpiSwiGLU) {
+                const float a = silu_f(v_lo) * v_hi;
+                if (p.yf32) reinterpret_cast<float *>(p.y)[o] = a;
+                else reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(a);
+            } else {
+                reinterpret_cast<float *>(p.y)[o] = v_lo + v_hi;
+            }
         }
     } else if constexpr (EPI == kEpiPeer) {
         // row-parallel projection: each finished value goes straight to every rank's all-reduce
@@ -91,7 +98,9 @@ __device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, in
     }
 }
 
-template <int FMT, int NT, int EPI, bool CI>
+// XS: fp32 activations staged as two fp16 rows per token (resident only); a template parameter so
+// the bf16 kernels keep their register allocation
+template <int FMT, int NT, int EPI, bool CI, bool XS>
 __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams p) {
     constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT), STAGE_W = stage_w_bytes(FMT);
     extern __shared__ __align__(128) uint8_t smem[];
@@ -224,29 +233,44 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
 
     const int mslots = p.xslots - 1;                  // rows the activation region is laid out for
     // resident activations: fp16 rows, a zero block, the offset table, token scales; staged
-    // again (after every consumer is done with them) when the range enters the next job
+    // again (after every consumer is done with them) when the range enters the next job.
+    // kwin (one job): only this CTA's part of K, window chunk i = the range's i-th chunk
+    const bool win = xres && p.kwin;
+    const int kc0 = win ? lo % p.chunks : 0, nch = win ? hi - lo : p.chunks;
+    constexpr bool split = XS;
     auto row_of = [](const GemvJob *jb) { return [jb](int n) { return jb->xrow[n]; }; };
-    if (xres) {
-        const GemvJob *jb = p.jobs + j;
-        stage_activations<FMT, NT, false>(p.x, p.ldx, row_of(jb), jb->m, mslots, p.K, p.xstride,
-                                          smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
-    }
+    auto stage = [&](int jj, auto su) {
+        const GemvJob *jb = p.jobs + jj;
+        constexpr int SU = decltype(su)::value;
+        if constexpr (XS)
+            stage_activations<FMT, NT, false, true, SU>(p.xf, p.ldx, row_of(jb), jb->m, mslots, p.K, kc0, nch,
+                                                        p.wchunks, p.xstride, smem + kNS * STAGE_W, threadIdx.x,
+                                                        kConsumers * 32);
+        else
+            stage_activations<FMT, NT, false, false, SU>(p.x, p.ldx, row_of(jb), jb->m, mslots, p.K, kc0, nch,
+                                                         p.wchunks, p.xstride, smem + kNS * STAGE_W, threadIdx.x,
+                                                         kConsumers * 32);
+    };
+    if (xres) stage(j, std::integral_constant<int, 4>{});
     if (tr) trace[3] = global_timer_ns();
     uint64_t waited = 0;
     // inside the chunk loop: fewer loads in flight per thread, so the loop keeps its registers
-    auto restage = [&](int jj) {
-        const GemvJob *jb = p.jobs + jj;
-        stage_activations<FMT, NT, false, decltype(row_of(jb)), 1>(p.x, p.ldx, row_of(jb), jb->m, mslots, p.K,
-                                                                   p.xstride, smem + kNS * STAGE_W, threadIdx.x,
-                                                                   kConsumers * 32);
-    };
+    auto restage = [&](int jj) { stage(jj, std::integral_constant<int, 1>{}); };
     const float *tscale = reinterpret_cast<const float *>(smem + kNS * STAGE_W + p.ctab_off +
-                                                          p.chunks * tab_chunk_bytes(NT));
+                                                          p.wchunks * tab_chunk_bytes(NT));
 
+    // m counts activation rows (MMA columns): the job's tokens, twice that when split (rows 2n and
+    // 2n + 1 carry token n, so lane t's two columns are one token's halves)
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int f = 0; f < 4; ++f) acc[nt][f] = 0.f;
     int yr[NT][2];
     uint32_t xrb[NT], xkm[NT];                        // activation base and per-chunk stride of this lane
     auto load_rows = [&]() {
-        m = p.jobs[j].m;
+        const int mt = p.jobs[j].m;
+        m = split ? 2 * mt : mt;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int tok = nt * 8 + r;
@@ -257,30 +281,39 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
                 xrb[nt] = xregion + (tok < m ? tok : p.xslots - 1) * kXSlot + t * 16;
                 xkm[nt] = 0u;
             }
+            if (split) {
+                const int tk = nt * 4 + t;
+                yr[nt][0] = tk < mt ? p.jobs[j].yrow[tk] : -1;
+                yr[nt][1] = -1;
+            } else {
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int tk = nt * 8 + 2 * t + h;
-                yr[nt][h] = tk < m ? p.jobs[j].yrow[tk] : -1;
+                for (int h = 0; h < 2; ++h) {
+                    const int tk = nt * 8 + 2 * t + h;
+                    yr[nt][h] = tk < mt ? p.jobs[j].yrow[tk] : -1;
+                }
+            }
+        }
+    };
+    // the finished sums of this lane's rows r, r + 8 (split: one token's two halves added)
+    auto store_rows = [&]() {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            if (split) {
+                store_pair<EPI>(p, g, s, r, yr[nt][0], acc[nt][0] + acc[nt][1], acc[nt][2] + acc[nt][3]);
+            } else {
+#pragma unroll
+                for (int h = 0; h < 2; ++h) store_pair<EPI>(p, g, s, r, yr[nt][h], acc[nt][h], acc[nt][2 + h]);
             }
         }
     };
     load_rows();
-
-    float acc[NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-        for (int f = 0; f < 4; ++f) acc[nt][f] = 0.f;
 
     // Close segment [a, b) of row group (j, g) for this strip.
     auto flush = [&](int a, int b) {
         if (xres) finish_rows<NT>(acc, tscale, t);
         const int gstart = (j * p.row_groups + g) * p.chunks;
         if (a == gstart && b == gstart + p.chunks) {          // the whole row group is here
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) store_pair<EPI>(p, g, s, r, yr[nt][h], acc[nt][h], acc[nt][2 + h]);
+            store_rows();
             return;
         }
         const int cf = worker_of(gstart, W, T), cl = worker_of(gstart + p.chunks - 1, W, T);
@@ -328,10 +361,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
                     acc[nt][f] = v;
                 }
             }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-            for (int h = 0; h < 2; ++h) store_pair<EPI>(p, g, s, r, yr[nt][h], acc[nt][h], acc[nt][2 + h]);
+        store_rows();
     };
     (void)flag;
 
@@ -390,23 +420,26 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         const uint32_t wsb = wring + slot * STAGE_W + s * SB, xstage = slot * xstage_bytes;
         // after a timed-out wait (failed is per thread) only the math is skipped: the bookkeeping
         // and every named barrier in flush() stay the same in all consumer threads
+        // resident activations of chunk c sit at window chunk c - lo (kwin) or at its k chunk
         if (n == kCPS && kc + kCPS < p.chunks) {
             // the common case: a full stage inside one row group
             if (!failed) {
+                const int xb = win ? c0 - lo : kc;
 #pragma unroll
                 for (int ci = 0; ci < kCPS; ++ci) {
                     uint32_t xa[NT];
-                    xaddr(xa, xstage, ci, kc + ci);
-                    chunk_math(wsb + ci * CB, xa, kc + ci);
+                    xaddr(xa, xstage, ci, xb + ci);
+                    chunk_math(wsb + ci * CB, xa, xb + ci);
                 }
             }
             kc += kCPS;
         } else {
             for (int ci = 0; ci < n; ++ci) {
                 if (!failed) {
+                    const int xb = win ? c0 + ci - lo : kc;
                     uint32_t xa[NT];
-                    xaddr(xa, xstage, ci, kc);
-                    chunk_math(wsb + ci * CB, xa, kc);
+                    xaddr(xa, xstage, ci, xb);
+                    chunk_math(wsb + ci * CB, xa, xb);
                 }
                 advance(c0 + ci);
             }
@@ -422,21 +455,21 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     }
 }
 
-template <int FMT, int NT, int EPI, bool CI>
+template <int FMT, int NT, int EPI, bool CI, bool XS>
 struct GemvKernel {
     static void prepare() {
         static bool done = false;
         if (!done) {
             done = true;
-            cudaFuncSetAttribute(gemv_int4_kernel<FMT, NT, EPI, CI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(gemv_int4_kernel<FMT, NT, EPI, CI, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  227 * 1024);
         }
     }
     static int occupancy(int smem) {
         prepare();
         int o = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_int4_kernel<FMT, NT, EPI, CI>, kThreads, smem) !=
-            cudaSuccess)
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_int4_kernel<FMT, NT, EPI, CI, XS>, kThreads,
+                                                          smem) != cudaSuccess)
             o = 1;
         return o > 0 ? o : 1;
     }
@@ -452,24 +485,37 @@ struct GemvKernel {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = pdl ? 1 : 0;
-        return cudaLaunchKernelEx(&cfg, gemv_int4_kernel<FMT, NT, EPI, CI>, p);
+        return cudaLaunchKernelEx(&cfg, gemv_int4_kernel<FMT, NT, EPI, CI, XS>, p);
     }
 };
 
 template <int FMT, int NT, bool CI>
 cudaError_t dispatch_epi_ci(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
     switch (epi) {
-        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, CI>::launch(p, smem, s, pdl);
-        case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16, CI>::launch(p, smem, s, pdl);
-        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, CI>::launch(p, smem, s, pdl);
-        case kEpiPairSum: return GemvKernel<FMT, NT, kEpiPairSum, CI>::launch(p, smem, s, pdl);
-        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, CI>::launch(p, smem, s, pdl);
+        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, CI, false>::launch(p, smem, s, pdl);
+        case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16, CI, false>::launch(p, smem, s, pdl);
+        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, CI, false>::launch(p, smem, s, pdl);
+        case kEpiPairSum: return GemvKernel<FMT, NT, kEpiPairSum, CI, false>::launch(p, smem, s, pdl);
+        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, CI, false>::launch(p, smem, s, pdl);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+// fp32 (split) activations: the epilogues of the projections that take them (a down or o
+// projection, a gate/up fed by one, a row-parallel projection); resident activations only
+template <int FMT, int NT>
+cudaError_t dispatch_split(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
+    switch (epi) {
+        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, true, true>::launch(p, smem, s, pdl);
+        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, true, true>::launch(p, smem, s, pdl);
+        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, true, true>::launch(p, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
 
 template <int FMT, int NT>
 cudaError_t dispatch_epi(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
+    if (p.xsplit) return p.xres ? dispatch_split<FMT, NT>(epi, p, smem, s, pdl) : cudaErrorInvalidValue;
     return p.xres ? dispatch_epi_ci<FMT, NT, true>(epi, p, smem, s, pdl)
                   : dispatch_epi_ci<FMT, NT, false>(epi, p, smem, s, pdl);
 }
@@ -481,28 +527,32 @@ cudaError_t dispatch_nt(int nt, int epi, const GemvParams &p, int smem, cudaStre
 
 template <int FMT>
 int occ_fmt(int nt, int smem) {
-    return nt == 1 ? GemvKernel<FMT, 1, kEpiF32, true>::occupancy(smem) : GemvKernel<FMT, 2, kEpiF32, true>::occupancy(smem);
+    return nt == 1 ? GemvKernel<FMT, 1, kEpiF32, true, false>::occupancy(smem)
+                   : GemvKernel<FMT, 2, kEpiF32, true, false>::occupancy(smem);
 }
 
 }  // namespace
 
-GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K) {
+GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks) {
     GemvLayout L{};
-    const int64_t xstride = xres_stride(K);
-    const int64_t res_bytes = xres_bytes(mmax, K, mmax > 8 ? 2 : 1, xstride);   // rows, zero block, table, scales
+    const int chunks = static_cast<int>((K + kChunkK - 1) / kChunkK);
+    if (wchunks <= 0 || wchunks > chunks) wchunks = chunks;
+    const int64_t xstride = xres_stride(static_cast<int64_t>(wchunks) * kChunkK);
+    // rows, zero block, table, scales
+    const int64_t res_bytes = xres_bytes(mrows, static_cast<int64_t>(wchunks) * kChunkK, mrows > 8 ? 2 : 1, xstride);
     L.xres = res_bytes <= kResidentXBudget;       // several jobs: staged again per job
-    (void)njobs;
+    L.wchunks = wchunks;
     L.xstride = static_cast<int>(xstride);
-    L.ctab_off = static_cast<int>(mmax * xstride + 128);
-    L.xslots = mmax + 1;
+    L.ctab_off = static_cast<int>(mrows * xstride + 128);
+    L.xslots = mrows + 1;
     const int64_t xbytes = L.xres ? res_bytes : static_cast<int64_t>(kNS) * kCPS * L.xslots * kXSlot;
     L.off_bar = static_cast<int>(kNS * stage_w_bytes(fmt) + (xbytes + 15) / 16 * 16);
     L.smem = L.off_bar + 2 * kNS * 8 + 16;
     return L;
 }
 
-bool gemv_resident(int mmax, int64_t K) {
-    return xres_bytes(mmax, K, mmax > 8 ? 2 : 1, xres_stride(K)) <= kResidentXBudget;
+bool gemv_resident(int mrows, int64_t K) {
+    return xres_bytes(mrows, K, mrows > 8 ? 2 : 1, xres_stride(K)) <= kResidentXBudget;
 }
 
 int gemv_ctas_per_sm(int fmt, int ntiles, int smem) {

@@ -361,62 +361,137 @@ __device__ __forceinline__ float group_to_f16(uint4 (&v)[4], float inv, uint32_t
     return sum;
 }
 
-// Stage m activation rows as fp16 + the offset table, by the nthr consumer threads (every one
-// must call this; named barrier 1 synchronises them). The region is laid out for mslots >= m
-// rows: rows, a 128-B zero block at mslots * xstride, the table, the token scales. Row n is x + row_of(n) * ldx (bf16,
-// 16-byte aligned). CG: load through L2 only (rows written earlier in the same launch).
-// One pass: the (token, 32-group) items are spread evenly over the threads, each thread issues
-// the loads of kSU groups before converting, stores fp16 and writes the group's sum.
-// A token whose |x| exceeds 2^15 is redone scaled by 2^-e (rare) and tscale[n] = 2^e.
-template <int FMT, int NT, bool CG, typename RowOf, int kSU = 4>
-__device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, int m, int mslots, int K, int xstride,
-                                  uint8_t *xs, int tid, int nthr) {
-    constexpr int MT = 8 * NT;
-    const int chunks = (K + kChunkK - 1) / kChunkK, G = K / 32;
-    float *tab = reinterpret_cast<float *>(xs + mslots * xstride + 128);
-    float *tscale = reinterpret_cast<float *>(xs + mslots * xstride + 128 + chunks * tab_chunk_bytes(NT));
-    unsigned *tmax = reinterpret_cast<unsigned *>(tscale + 16);
-    auto tab_at = [&](int grp, int tok) -> float & {
-        return tab[((grp * NT + tok / 8) * 4 + (tok % 8) / 2) * 2 + (tok & 1)];
-    };
-    // zeros: row tails, the zero block, table entries of absent tokens and of a group past K
-    const int rowb = K * 2, tail16 = (xstride - rowb) / 16;
-    for (int e = tid; e < m * tail16; e += nthr) {
-        const int n = e / tail16, q = e - n * tail16;
-        *reinterpret_cast<uint4 *>(xs + n * xstride + rowb + q * 16) = make_uint4(0, 0, 0, 0);
+// 8 fp32 activations (2 x 16 B) -> 16 B of each fp16 row: h = fp16(x * inv), l = fp16(x * inv - h),
+// so h + l carries x to ~22 significant bits; sh / sl accumulate their fp32 sums, mx the max
+// |x * inv| (fp32 bits)
+__device__ __forceinline__ void split8_f16(const uint4 &a4, const uint4 &b4, float inv, uint32_t &mx, uint4 &h,
+                                           uint4 &l, float &sh, float &sl) {
+    const float f[8] = {__uint_as_float(a4.x), __uint_as_float(a4.y), __uint_as_float(a4.z), __uint_as_float(a4.w),
+                        __uint_as_float(b4.x), __uint_as_float(b4.y), __uint_as_float(b4.z), __uint_as_float(b4.w)};
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float a = f[2 * k] * inv, b = f[2 * k + 1] * inv;
+        mx = max(mx, max(__float_as_uint(fabsf(a)), __float_as_uint(fabsf(b))));
+        const __half2 h2 = __floats2half2_rn(a, b);
+        const float2 hf = __half22float2(h2);
+        const __half2 l2 = __floats2half2_rn(a - hf.x, b - hf.y);      // exact differences
+        const float2 lf = __half22float2(l2);
+        sh += hf.x + hf.y;
+        sl += lf.x + lf.y;
+        hw[k] = *reinterpret_cast<const uint32_t *>(&h2);
+        lw[k] = *reinterpret_cast<const uint32_t *>(&l2);
     }
+    h = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    l = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+}
+
+// Stage m tokens' activations as fp16 rows + the offset table, by the nthr consumer threads (every
+// one must call this; named barrier 1 synchronises them). Only a window of the K axis is staged:
+// window chunk i (0 <= i < nch) holds K chunk (kc0 + i) mod chunks, so a CTA whose chunk range
+// covers part of a row group stages just that part (its chunk at range position i sits at window
+// chunk i); kc0 = 0, nch = chunks stages all of K. The region is laid out for mslots >= rows rows
+// and a table of tabch >= nch chunks: rows, a 128-B zero block at mslots * xstride, the table, the
+// token scales. Token n is x + row_of(n) * ldx (16-byte aligned). CG: load through L2 only (rows
+// written earlier in the same launch).
+// SPLIT false: x is bf16, token n is row n. SPLIT true: x is fp32 and token n becomes rows 2n
+// (fp16(x)) and 2n + 1 (fp16(x - fp16(x))): a lane's two MMA columns hold the halves of one token,
+// whose products are added when the segment is stored (2m <= mslots).
+// The (token, 32-group) items are spread evenly over the threads; each thread issues the loads of
+// kSU groups before converting, stores fp16 and writes the group sums. A token whose |x| exceeds
+// 2^15 is redone scaled by 2^-e (rare) and the scale of its rows is 2^e.
+template <int FMT, int NT, bool CG, bool SPLIT, int kSU, typename RowOf>
+__device__ void stage_activations(const void *xv, int64_t ldx, RowOf row_of, int m, int mslots, int K, int kc0,
+                                  int nch, int tabch, int xstride, uint8_t *xs, int tid, int nthr) {
+    constexpr int MT = 8 * NT;
+    constexpr int LQ = SPLIT ? 8 : 4;                   // 16-B loads per (token, group)
+    constexpr int SU = SPLIT ? 1 : kSU;                 // fp32 groups: 128 B of loads each
+    const int chunks = (K + kChunkK - 1) / kChunkK, G = K / 32, GW = 2 * nch;
+    const int mv = SPLIT ? 2 * m : m;                   // rows
+    float *tab = reinterpret_cast<float *>(xs + mslots * xstride + 128);
+    float *tscale = reinterpret_cast<float *>(xs + mslots * xstride + 128 + tabch * tab_chunk_bytes(NT));
+    unsigned *tmax = reinterpret_cast<unsigned *>(tscale + 16);
+    auto tab_at = [&](int grp, int row) -> float & {
+        return tab[((grp * NT + row / 8) * 4 + (row % 8) / 2) * 2 + (row & 1)];
+    };
+    auto kgroup = [&](int gw) {                         // window group -> K group (>= G: past K)
+        int kc = kc0 + (gw >> 1);
+        if (kc >= chunks) kc -= chunks;
+        return 2 * kc + (gw & 1);
+    };
+    auto src_of = [&](int n, int gk) {
+        const uint8_t *b = static_cast<const uint8_t *>(xv);
+        return reinterpret_cast<const uint4 *>(b + (static_cast<int64_t>(row_of(n)) * ldx + gk * 32) * (SPLIT ? 4 : 2));
+    };
+    // the zero block (absent tokens) and the table entries of absent rows
     if (tid < 8) *reinterpret_cast<uint4 *>(xs + mslots * xstride + tid * 16) = make_uint4(0, 0, 0, 0);
-    for (int e = tid; e < chunks * 2 * MT; e += nthr) {
-        const int tok = e % MT, grp = e / MT;
-        if (tok >= m || grp >= G) tab_at(grp, tok) = 0.f;
+    for (int e = tid; e < nch * 2 * MT; e += nthr) {
+        const int row = e % MT, grp = e / MT;
+        if (row >= mv) tab_at(grp, row) = 0.f;
     }
     if (tid < 16) tmax[tid] = 0u;
     named_bar_sync(1, nthr);
-    const int items = m * G;
-    for (int e0 = 0; e0 < items; e0 += nthr * kSU) {
-        uint4 v[kSU][4];
+    const uint4 z4 = make_uint4(0, 0, 0, 0);
+    // convert one (token, window group) and store it with its table entries
+    auto convert = [&](uint4 (&v)[LQ], float inv, uint32_t &mx, int n, int gw) {
+        if constexpr (SPLIT) {
+            uint4 *rh = reinterpret_cast<uint4 *>(xs + 2 * n * xstride + gw * 64);
+            uint4 *rl = reinterpret_cast<uint4 *>(xs + (2 * n + 1) * xstride + gw * 64);
+            float sh = 0.f, sl = 0.f;
 #pragma unroll
-        for (int u = 0; u < kSU; ++u) {
+            for (int q = 0; q < 4; ++q) {
+                uint4 h, l;
+                split8_f16(v[2 * q], v[2 * q + 1], inv, mx, h, l, sh, sl);
+                rh[q] = h;
+                rl[q] = l;
+            }
+            tab_at(gw, 2 * n) = sh * tab_factor<FMT>();
+            tab_at(gw, 2 * n + 1) = sl * tab_factor<FMT>();
+        } else {
+            const float sum = group_to_f16<true>(v, inv, mx);
+            uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + gw * 64);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) row[q] = v[q];
+            tab_at(gw, n) = sum * tab_factor<FMT>();
+        }
+    };
+    auto zero = [&](int n, int gw) {                    // the half chunk past K
+#pragma unroll
+        for (int h = 0; h < (SPLIT ? 2 : 1); ++h) {
+            const int row = SPLIT ? 2 * n + h : n;
+            uint4 *r = reinterpret_cast<uint4 *>(xs + row * xstride + gw * 64);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) r[q] = z4;
+            tab_at(gw, row) = 0.f;
+        }
+    };
+    const int items = m * GW;
+    for (int e0 = 0; e0 < items; e0 += nthr * SU) {
+        uint4 v[SU][LQ];
+#pragma unroll
+        for (int u = 0; u < SU; ++u) {
             const int e = e0 + u * nthr + tid;
             if (e < items) {
-                const int n = e / G, grp = e - n * G;
-                const uint16_t *src = x + static_cast<int64_t>(row_of(n)) * ldx + grp * 32;
+                const int n = e / GW, gk = kgroup(e - n * GW);
+                if (gk < G) {
+                    const uint4 *src = src_of(n, gk);
 #pragma unroll
-                for (int q = 0; q < 4; ++q) v[u][q] = CG ? ld_cg_v4(src + q * 8) : ld_nc_v4(src + q * 8);
+                    for (int q = 0; q < LQ; ++q) v[u][q] = CG ? ld_cg_v4(src + q) : ld_nc_v4(src + q);
+                }
             }
         }
 #pragma unroll
-        for (int u = 0; u < kSU; ++u) {
+        for (int u = 0; u < SU; ++u) {
             const int e = e0 + u * nthr + tid;
             if (e < items) {
-                const int n = e / G, grp = e - n * G;
-                uint32_t mx = 0;
-                const float sum = group_to_f16<true>(v[u], 1.0f, mx);
-                uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) row[q] = v[u][q];
-                tab_at(grp, n) = sum * tab_factor<FMT>();
-                if (mx > 0x47000000u) atomicMax(tmax + n, mx);      // only values above 2^15 matter
+                const int n = e / GW, gw = e - n * GW;
+                if (kgroup(gw) < G) {
+                    uint32_t mx = 0;
+                    convert(v[u], 1.0f, mx, n, gw);
+                    if (mx > 0x47000000u) atomicMax(tmax + n, mx);      // only values above 2^15 matter
+                } else {
+                    zero(n, gw);
+                }
             }
         }
     }
@@ -426,23 +501,21 @@ __device__ void stage_activations(const uint16_t *x, int64_t ldx, RowOf row_of, 
     for (int n = 0; n < m; ++n) big |= tmax[n] != 0u;
     if (big) {   // rare: redo the tokens beyond the fp16 range, scaled by 2^-e
         for (int e = tid; e < items; e += nthr) {
-            const int n = e / G, grp = e - n * G;
-            if (tmax[n] == 0u) continue;
+            const int n = e / GW, gw = e - n * GW, gk = kgroup(gw);
+            if (tmax[n] == 0u || gk >= G) continue;
             const float inv = exp2f(-ceilf(log2f(__uint_as_float(tmax[n]) * (1.0f / 32768.0f))));
-            const uint16_t *src = x + static_cast<int64_t>(row_of(n)) * ldx + grp * 32;
-            uint4 v[4];
+            const uint4 *src = src_of(n, gk);
+            uint4 v[LQ];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) v[q] = CG ? ld_cg_v4(src + q * 8) : ld_nc_v4(src + q * 8);
+            for (int q = 0; q < LQ; ++q) v[q] = CG ? ld_cg_v4(src + q) : ld_nc_v4(src + q);
             uint32_t mx = 0;
-            const float sum = group_to_f16<true>(v, inv, mx);
-            uint4 *row = reinterpret_cast<uint4 *>(xs + n * xstride + grp * 64);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) row[q] = v[q];
-            tab_at(grp, n) = sum * tab_factor<FMT>();
+            convert(v, inv, mx, n, gw);
         }
     }
-    if (tid < 16)
-        tscale[tid] = tid < m && tmax[tid] ? exp2f(ceilf(log2f(__uint_as_float(tmax[tid]) * (1.0f / 32768.0f)))) : 1.0f;
+    if (tid < 16) {
+        const unsigned tm = tmax[SPLIT ? tid >> 1 : tid];
+        tscale[tid] = tid < mv && tm ? exp2f(ceilf(log2f(__uint_as_float(tm) * (1.0f / 32768.0f)))) : 1.0f;
+    }
     named_bar_sync(1, nthr);
 }
 

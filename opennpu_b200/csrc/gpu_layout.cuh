@@ -80,7 +80,7 @@ struct GemvJob {
 enum GemvEpilogue : int {
     kEpiF32 = 0,      // y[yrow][n] = acc (fp32)
     kEpiBF16 = 1,     // y[yrow][n] = bf16(acc)
-    kEpiSwiGLU = 2,   // strip rows 0-7 gate, 8-15 up: y[yrow][i] = bf16(silu(gate_i) * up_i)
+    kEpiSwiGLU = 2,   // strip rows 0-7 gate, 8-15 up: y[yrow][i] = bf16(silu(gate_i) * up_i) (fp32 with yf32)
     kEpiPairSum = 3,  // strip rows 0-7 a row, 8-15 its residual: y[yrow][i] = row_i + residual_i (fp32)
     kEpiPeer = 4,     // fp32 y[yrow][n] sent to every rank's all-reduce buffer (8-byte {value, call} words)
 };
@@ -118,6 +118,14 @@ struct GemvParams {
     int xstride;                       // resident: bytes per token row
     int ctab_off;                      // resident: offset table position in the activation region
     int off_bar;                       // shared-memory offset of the mbarriers
+    int wchunks;                       // resident: 64-K chunks the activation region holds per row
+    int kwin;                          // resident, one job: each CTA stages only its own chunk range's
+                                       // part of K (every range is at most wchunks long)
+    int xsplit;                        // resident: activations are fp32 (xf); token n is staged as two fp16
+                                       // rows (x rounded, and the rounding error) whose sums are added at
+                                       // the store; jobs hold at most 8 tokens
+    const float *xf;                   // xsplit: fp32 activations, row stride ldx (elements)
+    int yf32;                          // kEpiSwiGLU: fp32 outputs instead of bf16
     // kEpiPeer: every output value goes, with the all-reduce call number, into slot [parity][rank]
     // of each rank's buffer (comm.cu layout); the call number is the buffer's counter + 1
     void *peer[kPeerMaxRanks];

@@ -16,15 +16,18 @@ constexpr int64_t kResidentXBudget = 40 * 1024;
 
 struct GemvLayout {
     int xres;          // activations resident
-    int xstride;       // resident: bytes per token row (padded)
+    int xstride;       // resident: bytes per activation row (padded)
     int ctab_off;      // resident: offset of the per-group offset table in the activation region
+    int wchunks;       // resident: 64-K chunks per row (all of K, or a CTA's window of it)
     int xslots;        // per-stage: token slots per chunk (max tokens + 1 zero slot)
     int off_bar;       // byte offset of the mbarriers in shared memory
     int smem;          // dynamic shared memory per CTA
 };
-GemvLayout gemv_layout(int fmt, int njobs, int mmax, int64_t K);
-// true when jobs of up to mmax tokens keep their activations resident (fp16 path) for this K
-bool gemv_resident(int mmax, int64_t K);
+// mrows: activation rows of the largest job (twice its tokens for fp32 split activations);
+// wchunks: chunks of K each resident row holds (0 = all of K)
+GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks = 0);
+// true when jobs of up to mrows activation rows stay resident (fp16 path) for this K
+bool gemv_resident(int mrows, int64_t K);
 int gemv_ctas_per_sm(int fmt, int ntiles, int smem);
 int gemv_chunks_per_stage();
 int64_t gemv_part_floats_per_worker(int ntiles);
@@ -147,13 +150,18 @@ cudaError_t unpack_gpu_launch(const uint8_t *src, int64_t N, int64_t K, int fmt,
                               uint16_t *m, cudaStream_t stream);
 
 // ---- small elementwise kernels (misc.cu)
+// jobs[0 .. ceil(rows / 16)) = the descriptors of a dense GEMV over rows consecutive rows of weights
+// w (16 rows per job), and flags[0 .. nflags) = 0; one small launch
+cudaError_t dense_jobs_launch(GemvJob *jobs, const uint8_t *w, int rows, unsigned *flags, int nflags,
+                              cudaStream_t stream);
 // fp32 -> bf16 bits with the reference's rounding (RNE; NaN -> quiet NaN), rows x cols with strides.
 cudaError_t f32_to_bf16_launch(const float *x, int64_t rows, int64_t cols, int64_t ldx, uint16_t *out, int64_t ldo,
                                cudaStream_t stream);
-// a[r][i] = bf16(act(h[r] + gu_bias[ids[r]])), act 0 = silu(gate) * up, 1 = gpt-oss clamped gate.
-cudaError_t moe_act_launch(const float *h, int64_t ldh, int64_t rows, int64_t Ng, const int32_t *ids,
-                           const float *gu_bias, int act, float alpha, float limit, uint16_t *a, int64_t lda,
-                           cudaStream_t stream);
+// a[r][i] = act(h[r] + gu_bias[ids[r]]) in fp32 (the reference's moe_act output type), act 0 =
+// silu(gate) * up, 1 = gpt-oss clamped gate.
+cudaError_t moe_act_f32_launch(const float *h, int64_t ldh, int64_t rows, int64_t Ng, const int32_t *ids,
+                               const float *gu_bias, int act, float alpha, float limit, float *a, int64_t lda,
+                               cudaStream_t stream);
 // y[t][n] = sum_j w[t][j] * (o[(t*k + j)][n] + bias[ids[t*k+j]][n]) in slot order.
 // Only slots whose expert id lies in [id_lo, id_hi) contribute (expert parallelism: this rank's
 // experts); the default range takes every slot.

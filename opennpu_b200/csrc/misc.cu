@@ -48,11 +48,11 @@ __global__ void moe_combine_kernel(const float *o, int64_t ldo, int64_t T, int k
     }
 }
 
-// a[r][i] = act(h[r] + gu_bias[ids[r]]) as bf16 bits (onpu_cpu.cpp:233-256 semantics): act 0
+// a[r][i] = act(h[r] + gu_bias[ids[r]]) in fp32 (onpu_cpu.cpp:233-256 semantics): act 0
 // silu(h[:I]) * h[I:]; act 1 (gpt-oss) interleaved gate/up, gate <= limit, |up| <= limit,
 // (up + 1) * gate * sigmoid(alpha * gate).
 __global__ void moe_act_kernel(const float *h, int64_t ldh, int64_t rows, int64_t Ng, const int32_t *ids,
-                               const float *gu_bias, int act, float alpha, float limit, uint16_t *a, int64_t lda) {
+                               const float *gu_bias, int act, float alpha, float limit, float *a, int64_t lda) {
     const int64_t I = Ng / 2, n = rows * I;
     for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < n;
          idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
@@ -69,8 +69,26 @@ __global__ void moe_act_kernel(const float *h, int64_t ldh, int64_t rows, int64_
             const float g = hr[i] + (b ? b[i] : 0.f), u = hr[I + i] + (b ? b[I + i] : 0.f);
             out = g / (1.f + expf(-g)) * u;
         }
-        a[r * lda + i] = to_bf16_bits(out);
+        a[r * lda + i] = out;
     }
+}
+
+// GEMV descriptors of a dense call (jobs of 16 consecutive rows) written on the device, and the
+// split-row ready flags of the launch cleared: the arguments travel by value in the launch.
+__global__ void dense_jobs_kernel(GemvJob *jobs, const uint8_t *w, int rows, unsigned *flags, int nflags) {
+    const int njobs = (rows + kMaxTokensPerJob - 1) / kMaxTokensPerJob;
+    for (int i = threadIdx.x; i < njobs * kMaxTokensPerJob; i += blockDim.x) {
+        const int j = i / kMaxTokensPerJob, n = i - j * kMaxTokensPerJob;
+        GemvJob &jb = jobs[j];
+        const int m = min(kMaxTokensPerJob, rows - j * kMaxTokensPerJob);
+        if (n == 0) {
+            jb.w = w;
+            jb.m = m;
+            jb.pad_ = 0;
+        }
+        jb.xrow[n] = jb.yrow[n] = n < m ? j * kMaxTokensPerJob + n : 0;
+    }
+    for (int i = threadIdx.x; i < nflags; i += blockDim.x) flags[i] = 0u;
 }
 
 unsigned grid_for(int64_t n, int block) {
@@ -80,12 +98,18 @@ unsigned grid_for(int64_t n, int block) {
 
 }  // namespace
 
-cudaError_t moe_act_launch(const float *h, int64_t ldh, int64_t rows, int64_t Ng, const int32_t *ids,
-                           const float *gu_bias, int act, float alpha, float limit, uint16_t *a, int64_t lda,
-                           cudaStream_t stream) {
+cudaError_t moe_act_f32_launch(const float *h, int64_t ldh, int64_t rows, int64_t Ng, const int32_t *ids,
+                               const float *gu_bias, int act, float alpha, float limit, float *a, int64_t lda,
+                               cudaStream_t stream) {
     if (rows * (Ng / 2) == 0) return cudaSuccess;
     moe_act_kernel<<<grid_for(rows * (Ng / 2), 256), 256, 0, stream>>>(h, ldh, rows, Ng, ids, gu_bias, act, alpha,
                                                                         limit, a, lda);
+    return cudaGetLastError();
+}
+
+cudaError_t dense_jobs_launch(GemvJob *jobs, const uint8_t *w, int rows, unsigned *flags, int nflags,
+                              cudaStream_t stream) {
+    dense_jobs_kernel<<<1, 256, 0, stream>>>(jobs, w, rows, flags, nflags);
     return cudaGetLastError();
 }
 

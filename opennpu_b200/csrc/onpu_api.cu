@@ -96,6 +96,8 @@ struct Ctx {
     int64_t h_cap = 0;
     uint16_t *d_a = nullptr;
     int64_t a_cap = 0;
+    float *d_af = nullptr;              // MoE: the fp32 activation between the projections
+    int64_t af_cap = 0;
     float *d_o = nullptr;
     int64_t o_cap = 0;
     float *d_y = nullptr;
@@ -233,16 +235,63 @@ bool ensure_scratch(Ctx &c, int workers, int ntiles, int counters) {
     return true;
 }
 
+// Activation and output forms of a GEMV launch beyond bf16 in / the epilogue's own type.
+struct GemvOpts {
+    const float *xf = nullptr;    // fp32 activations (row stride ldx), staged as two fp16 halves
+                                  // per value; jobs of at most 8 tokens, resident only
+    bool yf32 = false;            // kEpiSwiGLU: fp32 outputs
+};
+
+// The resident activation layout of a launch of T chunks, and its CTA count: one resident wave,
+// trimmed to whole CTAs per row group (host-known job count). A one-job launch whose CTAs each
+// cover less than a row group stages only its own part of K (kwin) when that layout keeps the wave
+// resident.
+struct GemvPlan {
+    GemvLayout lay;
+    int workers = 0, ntiles = 1;
+    bool kwin = false;
+};
+GemvPlan plan_gemv(const Ctx &c, const GpuMatrix &gm, int njobs, int mrows, bool device_count) {
+    GemvPlan pl;
+    const int T = njobs * gm.row_groups * gm.chunks;
+    pl.ntiles = mrows > 8 ? 2 : 1;
+    pl.lay = gemv_layout(gm.fmt, mrows, gm.K);
+    int W = choose_workers(c, gm.fmt, pl.ntiles, T, pl.lay.smem);
+    if (!device_count) W = align_workers(W, njobs, gm.row_groups);
+    pl.workers = W;
+    if (njobs == 1 && !device_count && W > 0) {
+        const int len = (T + W - 1) / W;
+        if (len < gm.chunks) {
+            const GemvLayout lw = gemv_layout(gm.fmt, mrows, gm.K, len);
+            if (lw.xres && c.nsm * gemv_ctas_per_sm(gm.fmt, pl.ntiles, lw.smem) >= W) {
+                pl.lay = lw;
+                pl.kwin = true;
+            }
+        }
+    }
+    return pl;
+}
+
 // mmax: the largest token count of any job (the kernel sizes its activation slots by it)
 // d_njobs: the job count is written on the device by the previous kernel (njobs is its bound)
-int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntiles, int mmax, int epi,
-             const uint16_t *x, int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl,
-             const int *d_njobs = nullptr, const PeerOut *peer = nullptr) {
+int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int mmax, int epi, const uint16_t *x,
+             int64_t ldx, void *y, int64_t ldy, cudaStream_t s, bool pdl, const int *d_njobs = nullptr,
+             const PeerOut *peer = nullptr, const GemvOpts &o = GemvOpts{}) {
     const int T = njobs * m.gm.row_groups * m.gm.chunks;
     if (T == 0) return 0;
-    const GemvLayout lay = gemv_layout(m.gm.fmt, njobs, mmax, m.gm.K);
-    int W = choose_workers(c, m.gm.fmt, ntiles, T, lay.smem);
-    if (!d_njobs) W = align_workers(W, njobs, m.gm.row_groups);
+    const bool split = o.xf != nullptr;
+    const GemvPlan pl = plan_gemv(c, m.gm, njobs, split ? 2 * mmax : mmax, d_njobs != nullptr);
+    const GemvLayout &lay = pl.lay;
+    const int W = pl.workers, ntiles = pl.ntiles;
+    if (split && epi != kEpiF32 && epi != kEpiSwiGLU && epi != kEpiPeer) {
+        set_err("fp32 activations take the fp32, SwiGLU and peer epilogues (epilogue %d given)", epi);
+        return -1;
+    }
+    if (split && (!lay.xres || mmax > 8)) {
+        set_err("fp32 activations need jobs of at most 8 tokens whose rows fit in shared memory (K = %lld)",
+                static_cast<long long>(m.gm.K));
+        return -1;
+    }
     if (!ensure_scratch(c, W, ntiles, W)) return -1;
     GemvParams p{};
     p.jobs = d_jobs;
@@ -258,6 +307,11 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int ntil
     p.y = y;
     p.ldy = ldy;
     p.row_map = epi == kEpiSwiGLU || epi == kEpiPairSum ? nullptr : m.d_row_map;
+    p.wchunks = lay.wchunks;
+    p.kwin = pl.kwin ? 1 : 0;
+    p.xsplit = split ? 1 : 0;
+    p.xf = o.xf;
+    p.yf32 = o.yf32 ? 1 : 0;
     p.part = c.d_part;
     p.counters = c.d_cnt;
     p.err = c.d_err;
@@ -346,11 +400,10 @@ bool finish(Ctx &c) {
     return check_device_err(c) == 0;
 }
 
-// (token, slot) pairs grouped by expert (ascending id, then arrival order), <= 16 per job
+// (token, slot) pairs grouped by expert (ascending id, then arrival order), <= per_job per job
 void build_expert_jobs(const GpuMat &m, const int32_t *ids, int64_t T, int k, bool x_per_slot, bool x_by_slot,
-                       std::vector<GemvJob> &jobs, int &ntiles, int &mmax) {
+                       std::vector<GemvJob> &jobs, int &mmax, int per_job = kMaxTokensPerJob) {
     jobs.clear();
-    ntiles = 1;
     mmax = 1;
     std::vector<int64_t> count(static_cast<size_t>(m.E) + 1, 0);
     for (int64_t i = 0; i < T * k; ++i) ++count[ids[i] + 1];
@@ -359,16 +412,15 @@ void build_expert_jobs(const GpuMat &m, const int32_t *ids, int64_t T, int k, bo
     std::vector<int64_t> pos(count.begin(), count.end() - 1);
     for (int64_t i = 0; i < T * k; ++i) order[pos[ids[i]]++] = i;
     for (int64_t e = 0; e < m.E; ++e) {
-        for (int64_t a = count[e]; a < count[e + 1]; a += kMaxTokensPerJob) {
+        for (int64_t a = count[e]; a < count[e + 1]; a += per_job) {
             GemvJob jb{};
             jb.w = m.d_w + e * m.gm.bytes;
-            jb.m = static_cast<int>(std::min<int64_t>(kMaxTokensPerJob, count[e + 1] - a));
+            jb.m = static_cast<int>(std::min<int64_t>(per_job, count[e + 1] - a));
             for (int n = 0; n < jb.m; ++n) {
                 const int64_t slot = order[a + n];
                 jb.xrow[n] = static_cast<int>(x_by_slot ? slot : (x_per_slot ? slot : slot / k));
                 jb.yrow[n] = static_cast<int>(slot);
             }
-            if (jb.m > 8) ntiles = 2;
             mmax = std::max(mmax, jb.m);
             jobs.push_back(jb);
         }
@@ -527,7 +579,9 @@ bool valid_ids(const int32_t *ids, int64_t n, int64_t E) {
 }
 
 // routed-expert FFN on the device; inputs already validated. fused: gate_up bank interleaved,
-// SwiGLU in the GEMV epilogue (act 0 and no biases only).
+// SwiGLU in the GEMV epilogue (act 0 and no biases only). The activation between the projections
+// stays fp32 (the reference's moe_act output, onpu_cpu.cpp:233-256): the down GEMV stages it as
+// two fp16 halves per value, so its products keep ~22 bits of the activation.
 bool moe_ffn_impl(BankH *gu, BankH *dn, const float *x, int64_t T, const int32_t *ids, int k, const float *w, int act,
                   float alpha, float limit, const float *gu_bias, const float *dn_bias, float *y, bool fused) {
     Ctx &c = ctx();
@@ -537,20 +591,27 @@ bool moe_ffn_impl(BankH *gu, BankH *dn, const float *x, int64_t T, const int32_t
         set_err("down bank K (%lld) != gate_up N/2 (%lld)", static_cast<long long>(dn->geo.K), static_cast<long long>(I));
         return false;
     }
+    // down jobs: the most tokens (<= 8) whose two fp16 rows each stay resident
+    int dn_per_job = 8;
+    while (dn_per_job > 1 && !gemv_resident(2 * dn_per_job, Kdp)) dn_per_job /= 2;
+    if (!gemv_resident(2 * dn_per_job, Kdp)) {
+        set_err("down projection K = %lld is too long for one resident fp32 activation row", static_cast<long long>(Kdp));
+        return false;
+    }
     if (!stage_x(c, x, T, Kg, Kgp)) return false;
     std::vector<GemvJob> jg, jd;
-    int ntg = 1, ntd = 1, mg = 1, md = 1;
-    build_expert_jobs(gu->mat, ids, T, k, false, false, jg, ntg, mg);
-    build_expert_jobs(dn->mat, ids, T, k, false, true, jd, ntd, md);
+    int mg = 1, md = 1;
+    build_expert_jobs(gu->mat, ids, T, k, false, false, jg, mg);
+    build_expert_jobs(dn->mat, ids, T, k, false, true, jd, md, dn_per_job);
     std::vector<GemvJob> all(jg);
     all.insert(all.end(), jd.begin(), jd.end());
     if (!upload_jobs(c, all)) return false;
-    if (!grow(c.d_a, c.a_cap, TK * Kdp) || !grow(c.d_o, c.o_cap, TK * Nd) || !grow(c.d_y, c.y_cap, T * Nd) ||
+    if (!grow(c.d_af, c.af_cap, TK * Kdp) || !grow(c.d_o, c.o_cap, TK * Nd) || !grow(c.d_y, c.y_cap, T * Nd) ||
         !grow(c.d_ids, c.ids_cap, TK) || !grow(c.d_w, c.w_cap, TK))
         return false;
     ONPU_CUDA(cudaMemcpyAsync(c.d_ids, ids, sizeof(int32_t) * TK, cudaMemcpyHostToDevice, c.stream), false);
     ONPU_CUDA(cudaMemcpyAsync(c.d_w, w, sizeof(float) * TK, cudaMemcpyHostToDevice, c.stream), false);
-    if (Kdp != I) ONPU_CUDA(cudaMemsetAsync(c.d_a, 0, sizeof(uint16_t) * TK * Kdp, c.stream), false);
+    if (Kdp != I) ONPU_CUDA(cudaMemsetAsync(c.d_af, 0, sizeof(float) * TK * Kdp, c.stream), false);
     const float *d_gb = nullptr, *d_db = nullptr;
     if (gu_bias) {
         if (!grow(c.d_gb, c.gb_cap, gu->mat.E * Ng)) return false;
@@ -563,18 +624,22 @@ bool moe_ffn_impl(BankH *gu, BankH *dn, const float *x, int64_t T, const int32_t
         d_db = c.d_db;
     }
     if (fused && act == 0 && !gu_bias) {
-        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, mg, kEpiSwiGLU, c.d_x, Kgp, c.d_a, Kdp,
-                     c.stream, false))
+        GemvOpts o;
+        o.yf32 = true;
+        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), mg, kEpiSwiGLU, c.d_x, Kgp, c.d_af, Kdp,
+                     c.stream, false, nullptr, nullptr, o))
             return false;
     } else {
         if (!grow(c.d_h, c.h_cap, TK * Ng)) return false;
-        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), ntg, mg, kEpiF32, c.d_x, Kgp, c.d_h, Ng, c.stream,
+        if (run_gemv(c, gu->mat, c.d_jobs, static_cast<int>(jg.size()), mg, kEpiF32, c.d_x, Kgp, c.d_h, Ng, c.stream,
                      false))
             return false;
-        ONPU_CUDA(moe_act_launch(c.d_h, Ng, TK, Ng, c.d_ids, d_gb, act, alpha, limit, c.d_a, Kdp, c.stream), false);
+        ONPU_CUDA(moe_act_f32_launch(c.d_h, Ng, TK, Ng, c.d_ids, d_gb, act, alpha, limit, c.d_af, Kdp, c.stream), false);
     }
-    if (run_gemv(c, dn->mat, c.d_jobs + jg.size(), static_cast<int>(jd.size()), ntd, md, kEpiF32, c.d_a, Kdp, c.d_o, Nd,
-                 c.stream, false))
+    GemvOpts od;
+    od.xf = c.d_af;
+    if (run_gemv(c, dn->mat, c.d_jobs + jg.size(), static_cast<int>(jd.size()), md, kEpiF32, nullptr, Kdp, c.d_o, Nd,
+                 c.stream, false, nullptr, nullptr, od))
         return false;
     ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, c.d_ids, c.d_w, d_db, c.d_y, Nd, c.stream), false);
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * T * Nd, cudaMemcpyDeviceToHost, c.stream), false);
@@ -669,7 +734,7 @@ void onpu_dense_mv(void *h, const float *x, int64_t rows, float *y) {
     const int64_t Kin = d->geo.ok ? d->geo.K : K;
     JobSet *js = dense_jobs(d, rows);
     if (!js || !stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
-    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
+    if (run_gemv(c, d->mat, js->d, js->n, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * rows * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
 }
@@ -713,10 +778,10 @@ void onpu_bank_run(void *h, const float *x, int x_per_slot, int64_t T, const int
     const int64_t xrows = x_per_slot ? T * k : T;
     if (!stage_x(c, x, xrows, b->geo.K, Kp)) return;
     std::vector<GemvJob> jobs;
-    int nt = 1, mm = 1;
-    build_expert_jobs(b->mat, ids, T, k, x_per_slot != 0, false, jobs, nt, mm);
+    int mm = 1;
+    build_expert_jobs(b->mat, ids, T, k, x_per_slot != 0, false, jobs, mm);
     if (!upload_jobs(c, jobs) || !grow(c.d_y, c.y_cap, T * k * N)) return;
-    if (run_gemv(c, b->mat, c.d_jobs, static_cast<int>(jobs.size()), nt, mm, kEpiF32, c.d_x, Kp, c.d_y, N, c.stream, false))
+    if (run_gemv(c, b->mat, c.d_jobs, static_cast<int>(jobs.size()), mm, kEpiF32, c.d_x, Kp, c.d_y, N, c.stream, false))
         return;
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * T * k * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
@@ -1071,39 +1136,78 @@ int onpu_dense_prepare(void *h, int64_t rows) {
     std::lock_guard<std::mutex> lk(g_mu);
     JobSet *js = dense_jobs(d, rows);
     if (!js) return -1;
-    const int T = js->n * d->mat.gm.row_groups * d->mat.gm.chunks;
-    const GemvLayout lay = gemv_layout(d->mat.gm.fmt, js->n, js->mmax, d->mat.gm.K);
-    const int W = choose_workers(c, d->mat.gm.fmt, js->ntiles, T, lay.smem);
-    return ensure_scratch(c, W, js->ntiles, W) ? 0 : -1;
+    // the larger of the bf16 and the fp32 (split) activation plans
+    const GemvPlan a = plan_gemv(c, d->mat.gm, js->n, js->mmax, false);
+    const GemvPlan b = plan_gemv(c, d->mat.gm, js->n, 2 * js->mmax, false);
+    const int W = std::max(a.workers, b.workers);
+    return ensure_scratch(c, W, 2, W) ? 0 : -1;
 }
 
-int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream) {
-    clear_err();
+}  // extern "C"
+
+namespace {
+// onpu_dense_mv_dev / onpu_dense_mv_f32_dev: x is bf16, or fp32 when xf32 (at most 8 rows)
+int dense_mv_dev_impl(const char *who, void *h, const void *x, bool xf32, int64_t ldx, int64_t rows, void *y,
+                      int64_t ldy, int epi, void *stream) {
     auto *d = static_cast<DenseH *>(h);
     if (rows <= 0) return 0;
+    const bool yf32 = epi == ONPU_EPI_SWIGLU_F32;
+    if (yf32) epi = kEpiSwiGLU;
     if (epi < kEpiF32 || epi > kEpiPairSum || (epi == kEpiSwiGLU && !d->gateup) ||
         (epi == kEpiPairSum && !d->residual)) {
-        set_err("onpu_dense_mv_dev: bad epilogue %d for this matrix", epi);
+        set_err("%s: bad epilogue %d for this matrix", who, yf32 ? ONPU_EPI_SWIGLU_F32 : epi);
         return -1;
     }
     if (d->geo.ok && d->geo.K != d->mat.gm.K) {
-        set_err("onpu_dense_mv_dev: K must be a multiple of 32");
+        set_err("%s: K must be a multiple of 32", who);
         return -1;
     }
-    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < d->mat.gm.K) {
-        set_err("onpu_dense_mv_dev: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & (xf32 ? 3 : 7)) || ldx < d->mat.gm.K) {
+        set_err("%s: x rows must be 16-byte aligned (ldx a multiple of 16 bytes) with ldx >= K", who);
+        return -1;
+    }
+    if (xf32 && rows > 8) {
+        set_err("%s: fp32 activations take at most 8 rows per call (%lld given)", who, static_cast<long long>(rows));
         return -1;
     }
     if (ldy < (epi >= kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
-        set_err("onpu_dense_mv_dev: y row stride %lld is shorter than the output row", static_cast<long long>(ldy));
+        set_err("%s: y row stride %lld is shorter than the output row", who, static_cast<long long>(ldy));
         return -1;
     }
     Ctx &c = ctx();
     std::lock_guard<std::mutex> lk(g_mu);
     JobSet *js = dense_jobs(d, rows);
     if (!js) return -1;
-    return run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, epi, static_cast<const uint16_t *>(x), ldx, y, ldy,
-                    static_cast<cudaStream_t>(stream), pdl_enabled());
+    GemvOpts o;
+    o.yf32 = yf32;
+    if (xf32) o.xf = static_cast<const float *>(x);
+    return run_gemv(c, d->mat, js->d, js->n, js->mmax, epi, xf32 ? nullptr : static_cast<const uint16_t *>(x), ldx, y,
+                    ldy, static_cast<cudaStream_t>(stream), pdl_enabled(), nullptr, nullptr, o);
+}
+}  // namespace
+
+extern "C" {
+
+int onpu_dense_mv_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream) {
+    clear_err();
+    return dense_mv_dev_impl("onpu_dense_mv_dev", h, x, false, ldx, rows, y, ldy, epi, stream);
+}
+
+int onpu_dense_mv_f32_dev(void *h, const float *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi,
+                          void *stream) {
+    clear_err();
+    return dense_mv_dev_impl("onpu_dense_mv_f32_dev", h, x, true, ldx, rows, y, ldy, epi, stream);
+}
+
+int onpu_dense_max_f32_rows(void *h) {
+    clear_err();
+    auto *d = static_cast<DenseH *>(h);
+    Ctx &c = ctx();
+    if (!d || !c.ok) return 0;
+    std::lock_guard<std::mutex> lk(g_mu);
+    for (int rows = 8; rows >= 1; --rows)
+        if (plan_gemv(c, d->mat.gm, 1, 2 * rows, false).lay.xres) return rows;
+    return 0;
 }
 
 int onpu_dense_mm_dev(void *h, const void *x, int64_t ldx, int64_t rows, void *y, int64_t ldy, int epi, void *stream) {
@@ -1318,13 +1422,19 @@ int moe_ffn_dev_impl(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     Ctx &c = ctx();
     std::lock_guard<std::mutex> lk(g_mu);
     auto s = static_cast<cudaStream_t>(stream);
-    // job lists are built on the device from the routed ids: no host round trip, capturable
-    // jobs of 8 tokens when 16 would not keep their activations resident (fp16 path, one staging
-    // per job instead of a copy per token and chunk)
-    const int per_job = gemv_resident(16, std::max(Kg, Kd)) || !gemv_resident(8, std::max(Kg, Kd)) ? 16 : 8;
+    // job lists are built on the device from the routed ids: no host round trip, capturable.
+    // Tokens per job: the most (<= 8) for which gate_up's bf16 rows and down's fp32 activations
+    // (two fp16 rows per token) both stay resident in shared memory (one staging per job)
+    int per_job = 8;
+    while (per_job > 1 && !(gemv_resident(per_job, Kg) && gemv_resident(2 * per_job, Kd))) per_job /= 2;
+    if (!gemv_resident(per_job, Kg) || !gemv_resident(2 * per_job, Kd)) {
+        set_err("onpu_moe_ffn_dev: K = %lld / %lld is too long for resident activation rows",
+                static_cast<long long>(Kg), static_cast<long long>(Kd));
+        return -1;
+    }
     const int64_t njmax = std::min(E, TK) + TK / per_job;
     if (!grow(c.d_jobs, c.jobs_cap, 2 * njmax) || !grow(c.d_order, c.order_cap, TK) ||
-        !grow(c.d_njobs, c.njobs_cap, 1) || !grow(c.d_a, c.a_cap, TK * Kd) || !grow(c.d_o, c.o_cap, TK * Nd))
+        !grow(c.d_njobs, c.njobs_cap, 1) || !grow(c.d_af, c.af_cap, TK * Kd) || !grow(c.d_o, c.o_cap, TK * Nd))
         return -1;
     ExpertJobsParams jp{};
     jp.ids = ids;
@@ -1352,14 +1462,18 @@ int moe_ffn_dev_impl(void *ffn, const void *x, int64_t ldx, int64_t T, const int
     } else {
         ONPU_CUDA(expert_jobs_launch(jp, s), -1);
     }
-    const int mmax = static_cast<int>(std::min<int64_t>(T, per_job)), ntiles = mmax > 8 ? 2 : 1;
+    const int mmax = static_cast<int>(std::min<int64_t>(T, per_job));
     // an expert sees each token at most once (the k experts of a token are distinct); the down
-    // projection's jobs hold the same slots, so both lists share the bound
-    if (run_gemv(c, gu->mat, jp.jobs0, static_cast<int>(njmax), ntiles, mmax, kEpiSwiGLU,
-                 static_cast<const uint16_t *>(x), ldx, c.d_a, Kd, s, true, c.d_njobs))
+    // projection's jobs hold the same slots, so both lists share the bound. The activation between
+    // the projections stays fp32 (SwiGLU epilogue -> fp32, staged by down as two fp16 halves)
+    GemvOpts og, od;
+    og.yf32 = true;
+    od.xf = c.d_af;
+    if (run_gemv(c, gu->mat, jp.jobs0, static_cast<int>(njmax), mmax, kEpiSwiGLU, static_cast<const uint16_t *>(x), ldx,
+                 c.d_af, Kd, s, true, c.d_njobs, nullptr, og))
         return -1;
-    if (run_gemv(c, dn->mat, jp.jobs1, static_cast<int>(njmax), ntiles, mmax, kEpiF32, c.d_a, Kd, c.d_o, Nd, s, true,
-                 c.d_njobs))
+    if (run_gemv(c, dn->mat, jp.jobs1, static_cast<int>(njmax), mmax, kEpiF32, nullptr, Kd, c.d_o, Nd, s, true,
+                 c.d_njobs, nullptr, od))
         return -1;
     if (e0 >= 0)
         ONPU_CUDA(moe_combine_launch(c.d_o, Nd, T, k, Nd, ids, w, nullptr, y, ldy, s, static_cast<int>(e0),
@@ -1495,8 +1609,11 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
                 static_cast<long long>(rows), kStaticMaxRows);
         return -1;
     }
-    if (epi < kEpiF32 || epi > kEpiSwiGLU || (epi == kEpiSwiGLU && !d->gateup)) {
-        set_err("onpu_dense_mv_dev_noalloc: bad epilogue %d for this matrix", epi);
+    const bool yf32 = epi == ONPU_EPI_SWIGLU_F32;
+    if (yf32) epi = kEpiSwiGLU;
+    if (epi < kEpiF32 || epi > kEpiPairSum || (epi == kEpiSwiGLU && !d->gateup) ||
+        (epi == kEpiPairSum && !d->residual)) {
+        set_err("onpu_dense_mv_dev_noalloc: bad epilogue %d for this matrix", yf32 ? ONPU_EPI_SWIGLU_F32 : epi);
         return -1;
     }
     if (d->geo.ok && d->geo.K != d->mat.gm.K) {
@@ -1507,7 +1624,7 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
         set_err("onpu_dense_mv_dev_noalloc: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
         return -1;
     }
-    if (ldy < (epi == kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
+    if (ldy < (epi >= kEpiSwiGLU ? d->mat.gm.N / 2 : d->mat.gm.N) || (reinterpret_cast<uintptr_t>(y) & 3)) {
         set_err("onpu_dense_mv_dev_noalloc: y row stride %lld is shorter than the output row",
                 static_cast<long long>(ldy));
         return -1;
@@ -1531,26 +1648,23 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
     unsigned *flags = reinterpret_cast<unsigned *>(base + kStaticPartBytes);
     GemvJob *d_jobs = reinterpret_cast<GemvJob *>(base + kStaticPartBytes + kStaticFlagBytes);
 
-    // descriptors built on the host stack, copied into the array on the caller's stream
-    GemvJob jobs[kStaticMaxJobs];
+    // the same launch plan (grid, activation window) as onpu_dense_mv_dev for this row count, so
+    // both entries add the split rows in the same order and agree bit for bit
     const int njobs = static_cast<int>((rows + kMaxTokensPerJob - 1) / kMaxTokensPerJob);
-    int ntiles = 1, mmax = 0;
-    for (int j = 0; j < njobs; ++j) {
-        GemvJob &jb = jobs[j];
-        std::memset(&jb, 0, sizeof jb);
-        jb.w = d->mat.d_w;
-        jb.m = static_cast<int>(std::min<int64_t>(kMaxTokensPerJob, rows - static_cast<int64_t>(j) * kMaxTokensPerJob));
-        for (int n = 0; n < jb.m; ++n) jb.xrow[n] = jb.yrow[n] = j * kMaxTokensPerJob + n;
-        if (jb.m > 8) ntiles = 2;
-        mmax = std::max(mmax, jb.m);
-    }
+    const int mmax = static_cast<int>(std::min<int64_t>(rows, kMaxTokensPerJob));
     const int T = njobs * d->mat.gm.row_groups * d->mat.gm.chunks;
     if (T == 0) return 0;
-    const GemvLayout lay = gemv_layout(d->mat.gm.fmt, njobs, mmax, d->mat.gm.K);
-    const int W = std::min(kStaticWorkers, choose_workers(c, d->mat.gm.fmt, ntiles, T, lay.smem));
+    const GemvPlan pl = plan_gemv(c, d->mat.gm, njobs, mmax, false);
+    const GemvLayout &lay = pl.lay;
+    const int W = pl.workers;
+    if (W > kStaticWorkers) {
+        set_err("onpu_dense_mv_dev_noalloc: %d CTAs exceed the static scratch's %d", W, kStaticWorkers);
+        return -1;
+    }
     auto s = static_cast<cudaStream_t>(stream);
-    ONPU_CUDA(cudaMemcpyAsync(d_jobs, jobs, sizeof(GemvJob) * njobs, cudaMemcpyHostToDevice, s), -1);
-    ONPU_CUDA(cudaMemsetAsync(flags, 0, sizeof(unsigned) * W, s), -1);
+    // descriptors written and the flags this launch uses cleared by a small kernel on the caller's
+    // stream: every argument is passed by value, nothing is read from host memory
+    ONPU_CUDA(dense_jobs_launch(d_jobs, d->mat.d_w, static_cast<int>(rows), flags, W, s), -1);
 
     GemvParams p{};
     p.jobs = d_jobs;
@@ -1565,7 +1679,7 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
     p.ldx = ldx;
     p.y = y;
     p.ldy = ldy;
-    p.row_map = epi == kEpiSwiGLU ? nullptr : d->mat.d_row_map;
+    p.row_map = epi == kEpiSwiGLU || epi == kEpiPairSum ? nullptr : d->mat.d_row_map;
     p.part = part;
     p.counters = flags;
     p.err = c.d_err;
@@ -1582,7 +1696,10 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
     p.xstride = lay.xstride;
     p.ctab_off = lay.ctab_off;
     p.off_bar = lay.off_bar;
-    ONPU_CUDA(gemv_launch(d->mat.gm.fmt, ntiles, epi, p, lay.smem, s, false), -1);
+    p.wchunks = lay.wchunks;
+    p.kwin = pl.kwin ? 1 : 0;
+    p.yf32 = yf32 ? 1 : 0;
+    ONPU_CUDA(gemv_launch(d->mat.gm.fmt, pl.ntiles, epi, p, lay.smem, s, false), -1);
     ++c.calls;
     return 0;
 }
@@ -1888,29 +2005,36 @@ int onpu_comm_open(void *comm, const void *handles) {
     return 0;
 }
 
-int onpu_dense_mv_allreduce_dev(void *h, void *comm, const void *x, int64_t ldx, int64_t rows, float *y,
-                                void *y_bf16, void *stream) {
-    clear_err();
+}  // extern "C"
+
+namespace {
+// onpu_dense_mv_allreduce(_f32)_dev: x bf16, or fp32 (at most 8 rows) when xf32
+int mv_allreduce_impl(const char *who, void *h, void *comm, const void *x, bool xf32, int64_t ldx, int64_t rows,
+                      float *y, void *y_bf16, void *stream) {
     auto *d = static_cast<DenseH *>(h);
     auto *cm = static_cast<CommH *>(comm);
     if (rows <= 0) return 0;
     if (d->gateup || d->residual || (d->geo.ok && d->geo.K != d->mat.gm.K)) {
-        set_err("onpu_dense_mv_allreduce_dev: needs a plain matrix (no gate/up or residual rows, K %% 32 == 0)");
+        set_err("%s: needs a plain matrix (no gate/up or residual rows, K %% 32 == 0)", who);
         return -1;
     }
-    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & 7) || ldx < d->mat.gm.K) {
-        set_err("onpu_dense_mv_allreduce_dev: x rows must be 16-byte aligned with ldx %% 8 == 0 and ldx >= K");
+    if ((reinterpret_cast<uintptr_t>(x) & 15) || (ldx & (xf32 ? 3 : 7)) || ldx < d->mat.gm.K) {
+        set_err("%s: x rows must be 16-byte aligned (ldx a multiple of 16 bytes) with ldx >= K", who);
+        return -1;
+    }
+    if (xf32 && rows > 8) {
+        set_err("%s: fp32 activations take at most 8 rows per call", who);
         return -1;
     }
     const int64_t n = rows * d->mat.gm.N;
     if (n > cm->cap || (!y && !y_bf16) || (y_bf16 && (reinterpret_cast<uintptr_t>(y_bf16) & 1))) {
-        set_err("onpu_dense_mv_allreduce_dev: rows x N = %lld exceeds the all-reduce buffer (%lld) or no output",
+        set_err("%s: rows x N = %lld exceeds the all-reduce buffer (%lld) or no output", who,
                 static_cast<long long>(n), static_cast<long long>(cm->cap));
         return -1;
     }
     for (int r = 0; r < cm->world; ++r)
         if (!cm->bufs[r]) {
-            set_err("onpu_dense_mv_allreduce_dev: rank %d's buffer is not mapped (onpu_comm_open)", r);
+            set_err("%s: rank %d's buffer is not mapped (onpu_comm_open)", who, r);
             return -1;
         }
     Ctx &c = ctx();
@@ -1923,12 +2047,30 @@ int onpu_dense_mv_allreduce_dev(void *h, void *comm, const void *x, int64_t ldx,
     po.world = cm->world;
     po.cap = cm->cap;
     auto s = static_cast<cudaStream_t>(stream);
-    if (run_gemv(c, d->mat, js->d, js->n, js->ntiles, js->mmax, kEpiPeer, static_cast<const uint16_t *>(x), ldx,
-                 nullptr, d->mat.gm.N, s, pdl_enabled(), nullptr, &po))
+    GemvOpts o;
+    if (xf32) o.xf = static_cast<const float *>(x);
+    if (run_gemv(c, d->mat, js->d, js->n, js->mmax, kEpiPeer, xf32 ? nullptr : static_cast<const uint16_t *>(x), ldx,
+                 nullptr, d->mat.gm.N, s, pdl_enabled(), nullptr, &po, o))
         return -1;
     ONPU_CUDA(comm_reduce_launch(cm->bufs, cm->rank, cm->world, cm->cap, y, y_bf16, n, c.d_err, s), -1);
     return 0;
 }
+}  // namespace
+
+extern "C" {
+
+int onpu_dense_mv_allreduce_dev(void *h, void *comm, const void *x, int64_t ldx, int64_t rows, float *y,
+                                void *y_bf16, void *stream) {
+    clear_err();
+    return mv_allreduce_impl("onpu_dense_mv_allreduce_dev", h, comm, x, false, ldx, rows, y, y_bf16, stream);
+}
+
+int onpu_dense_mv_allreduce_f32_dev(void *h, void *comm, const float *x, int64_t ldx, int64_t rows, float *y,
+                                    void *y_bf16, void *stream) {
+    clear_err();
+    return mv_allreduce_impl("onpu_dense_mv_allreduce_f32_dev", h, comm, x, true, ldx, rows, y, y_bf16, stream);
+}
+
 
 int onpu_comm_allreduce(void *comm, const float *src, float *dst, void *dst_bf16, int64_t n, void *stream) {
     clear_err();

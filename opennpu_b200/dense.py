@@ -10,7 +10,7 @@ import torch
 
 from . import libonpu as L
 
-EPI_F32, EPI_BF16, EPI_SWIGLU, EPI_PAIRSUM = 0, 1, 2, 3
+EPI_F32, EPI_BF16, EPI_SWIGLU, EPI_PAIRSUM, EPI_SWIGLU_F32 = 0, 1, 2, 3, 5
 FMT_Q4NX, FMT_Q4S, FMT_Q4F16 = 0, 1, 2
 
 
@@ -126,24 +126,31 @@ class DenseMatrix:
     def nbytes(self):
         return self.info()[3]
 
+    def max_f32_rows(self):
+        """The most activation rows (0..8) an fp32-input call takes for this matrix."""
+        return int(L.load().onpu_dense_max_f32_rows(self.h))
+
     def prepare(self, rows):
         L.check(L.load().onpu_dense_prepare(self.h, rows), "onpu_dense_prepare")
 
     def mv(self, x, out=None, epi=None, stream=None):
-        """x: bf16 CUDA [M, K] (row stride % 8 == 0) -> [M, N] fp32 (EPI_F32), bf16 (EPI_BF16),
-        [M, N/2] bf16 silu(gate) * up (EPI_SWIGLU) or [M, N/2] fp32 row + residual (EPI_PAIRSUM,
-        the default of a two-pass matrix; EPI_F32 otherwise)."""
-        assert x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.stride(1) == 1
+        """x: bf16 CUDA [M, K] (row stride % 8 == 0), or fp32 [M <= 8, K] (row stride % 4 == 0; each
+        value staged as two fp16 halves, so it is not rounded to 16 bits) -> [M, N] fp32 (EPI_F32),
+        bf16 (EPI_BF16), [M, N/2] silu(gate) * up in bf16 (EPI_SWIGLU) or fp32 (EPI_SWIGLU_F32), or
+        [M, N/2] fp32 row + residual (EPI_PAIRSUM, the default of a two-pass matrix; EPI_F32
+        otherwise)."""
+        assert x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and x.dim() == 2 and x.stride(1) == 1
         if epi is None:
             epi = EPI_PAIRSUM if self.residual else EPI_F32
         M = x.shape[0]
         if out is None:
-            ncol = self.N // 2 if epi in (EPI_SWIGLU, EPI_PAIRSUM) else self.N
-            fp32 = epi in (EPI_F32, EPI_PAIRSUM)
+            ncol = self.N // 2 if epi in (EPI_SWIGLU, EPI_SWIGLU_F32, EPI_PAIRSUM) else self.N
+            fp32 = epi in (EPI_F32, EPI_PAIRSUM, EPI_SWIGLU_F32)
             out = torch.empty(M, ncol, device=x.device, dtype=torch.float32 if fp32 else torch.bfloat16)
-        rc = L.load().onpu_dense_mv_dev(self.h, x.data_ptr(), x.stride(0), M, out.data_ptr(), out.stride(0), epi,
-                                        _stream_ptr(stream))
-        L.check(rc, "onpu_dense_mv_dev")
+        fn = "onpu_dense_mv_f32_dev" if x.dtype == torch.float32 else "onpu_dense_mv_dev"
+        rc = getattr(L.load(), fn)(self.h, x.data_ptr(), x.stride(0), M, out.data_ptr(), out.stride(0), epi,
+                                   _stream_ptr(stream))
+        L.check(rc, fn)
         return out
 
     def mm(self, x, out=None, epi=EPI_F32, stream=None):

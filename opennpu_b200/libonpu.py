@@ -64,6 +64,8 @@ SIGNATURES = {
     "onpu_dense_new_residual_f32_dev": (P, [P, I64, I64, I64, I32, P]),
     "onpu_dense_prepare": (I32, [P, I64]),
     "onpu_dense_mv_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
+    "onpu_dense_mv_f32_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
+    "onpu_dense_max_f32_rows": (I32, [P]),
     "onpu_dense_mv_dev_noalloc": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mm_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_unpack_dev": (I32, [P, P, P, P, P]),
@@ -88,6 +90,7 @@ SIGNATURES = {
     "onpu_comm_allreduce": (I32, [P, P, P, P, I64, P]),
     "onpu_comm_free": (None, [P]),
     "onpu_dense_mv_allreduce_dev": (I32, [P, P, P, I64, I64, P, P, P]),
+    "onpu_dense_mv_allreduce_f32_dev": (I32, [P, P, P, I64, I64, P, P, P]),
     "onpu_chain_new": (P, []),
     "onpu_chain_add": (I32, [P, P, P, I64, I64, P, I64, I32, I32]),
     "onpu_chain_info": (I32, [P, I64P]),

@@ -11,7 +11,7 @@ scales [N, K/32], the layout `DenseMatrix.from_int4` takes.
 """
 import torch
 
-from .dense import DenseMatrix, EPI_BF16, EPI_F32, EPI_SWIGLU
+from .dense import DenseMatrix, EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_SWIGLU_F32
 
 GROUP = 32
 
@@ -77,9 +77,15 @@ class TPLinear:
 class TPDecoderLayer:
     """One decoder layer's projections on one rank: q/k/v (column), o (row), gate/up with the
     SwiGLU epilogue (column), down (row). Attention is not part of the path: o takes this rank's
-    q-projection output (its heads, bf16) as the stand-in for the attention output of those heads.
-    The layer's input x (bf16 [M, hidden]) is the same on every rank; its output (fp32 [M, hidden],
-    all-reduced) too."""
+    q-projection output (its heads) as the stand-in for the attention output of those heads.
+    The layer's input x ([M, hidden], the same on every rank) and output (fp32 [M, hidden],
+    all-reduced) likewise.
+
+    Decode (M up to f32_rows, the most fp32 rows every projection's GEMV keeps in shared memory):
+    every activation between the projections stays fp32, as in the reference's
+    dequantise-then-matmul path (opennpu/native/reference.py:55-57, :84); each GEMV stages its fp32
+    input as two fp16 halves per value. Longer batches carry bf16 activations between the
+    projections (the rounding the reference's device path applies to every NPU input)."""
 
     def __init__(self, qkv, o, gu, dn, nq, group=None, allreduce=None):
         """qkv / gu: this rank's stacked row blocks (q|k|v, gate|up); o / dn: its K blocks; each an
@@ -91,6 +97,7 @@ class TPDecoderLayer:
         self.dn = TPLinear(*dn, "row", group=group, allreduce=allreduce)
         self.nq = nq
         assert self.o.K == nq
+        self.f32_rows = min(p.m.max_f32_rows() for p in (self.qkv, self.o, self.gu, self.dn))
 
     @classmethod
     def from_full(cls, w, rank, world, group=None, allreduce=None):
@@ -101,18 +108,25 @@ class TPDecoderLayer:
                    nq[1] - nq[0], group, allreduce)
 
     def buffers(self, M, device="cuda"):
-        return {"qkv": torch.empty(M, self.qkv.N, device=device, dtype=torch.bfloat16),
+        dt = torch.float32 if M <= self.f32_rows else torch.bfloat16
+        return {"qkv": torch.empty(M, self.qkv.N, device=device, dtype=dt),
                 "h": torch.empty(M, self.o.N, device=device),
                 "x2": torch.empty(M, self.o.N, device=device, dtype=torch.bfloat16),
-                "a": torch.empty(M, self.gu.N // 2, device=device, dtype=torch.bfloat16),
+                "a": torch.empty(M, self.gu.N // 2, device=device, dtype=dt),
                 "y": torch.empty(M, self.dn.N, device=device)}
 
     def __call__(self, x, b, stream=None, y_bf16=None):
-        """x: bf16 [M, hidden]; b: buffers(); returns b["y"] (fp32, summed over ranks). y_bf16: also
-        receive the output as bf16 (the next layer's input)."""
-        self.qkv(x, b["qkv"], epi=EPI_BF16, stream=stream)
-        self.o(b["qkv"][:, :self.nq], b["h"], stream=stream, out_bf16=b["x2"])
-        self.gu(b["x2"], b["a"], epi=EPI_SWIGLU, stream=stream)
+        """x: [M, hidden] (fp32 or bf16 for M <= 8, else bf16); b: buffers(); returns b["y"] (fp32,
+        summed over ranks). y_bf16: also receive the output as bf16 (the next layer's input when
+        the activations are bf16)."""
+        if b["qkv"].dtype == torch.float32:
+            self.qkv(x, b["qkv"], epi=EPI_F32, stream=stream)
+            self.o(b["qkv"][:, :self.nq], b["h"], stream=stream)
+            self.gu(b["h"], b["a"], epi=EPI_SWIGLU_F32, stream=stream)
+        else:
+            self.qkv(x, b["qkv"], epi=EPI_BF16, stream=stream)
+            self.o(b["qkv"][:, :self.nq], b["h"], stream=stream, out_bf16=b["x2"])
+            self.gu(b["x2"], b["a"], epi=EPI_SWIGLU, stream=stream)
         self.dn(b["a"], b["y"], stream=stream, out_bf16=y_bf16)
         return b["y"]
 

@@ -181,8 +181,8 @@ def silu(a):
 def moe_ffn(h, ids, w, Wg, Wu, Wd):
     """reference.py:77-84: for each token t and slot j (expert e = ids[t, j]),
     y_t += w[t, j] * (silu(h_t Wg_e^T) * (h_t Wu_e^T)) Wd_e^T. Wg/Wu/Wd: callables e -> fp32
-    matrices (gate [I][H], up [I][H], down [H][I]). Accumulates in float64, and rounds the
-    activation to bf16 before the down projection when ``act_bf16`` is set on the caller side."""
+    matrices (gate [I][H], up [I][H], down [H][I]). Accumulates in float64; the activation between
+    the projections is not rounded (the reference computes it in fp32)."""
     T = h.shape[0]
     out = np.zeros((T, Wd(int(ids[0, 0])).shape[0]), np.float64)
     for e in np.unique(ids):

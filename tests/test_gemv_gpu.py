@@ -160,3 +160,93 @@ def test_bad_inputs_are_rejected_not_run():
         m.mv(torch.zeros(1, 64, dtype=torch.bfloat16, device="cuda"), epi=dense.EPI_SWIGLU)
     assert L.load().onpu_dense_new_int4(64, 48, 0) is None
     assert L.load().onpu_dense_new2(5120, 17408, 1) is None   # no 8-column geometry (reference: NULL)
+
+
+# ------------------------------------------------------------------ fp32 activations (split staging)
+@pytest.mark.parametrize("N,K", [(64, 64), (130, 160), (1024, 4096), (4096, 12288), (2048, 768), (33, 2080)])
+@pytest.mark.parametrize("M", [1, 2, 5, 8])
+def test_f32_activations_match_oracle(N, K, M):
+    """onpu_dense_mv_f32_dev: fp32 activations that are not bf16 values (each staged as two fp16
+    halves), against the oracle's fp32 dequantise-then-matmul (reference.py:55-57). The tensor
+    cores add the fp16 products with truncation, ~1e-6 relative for 11-bit inputs, so the tight
+    bound is 1e-5 here (the bf16 path: exact 8-bit inputs)."""
+    dense = _dev()
+    v, s, qk, sc = make_int4(N, K, seed=N + 5 * K)
+    m = dense.DenseMatrix.from_int4(qk.cuda(), sc.cuda())
+    if m.max_f32_rows() < M:
+        pytest.skip(f"{M} fp32 rows of K = {K} do not fit in shared memory")
+    x = np.random.default_rng(M + K).normal(0, 1, size=(M, K)).astype(np.float32)
+    x[0, :4] = [1e-6, -3e-8, 0.0, 7.25][:min(4, K)]                    # fp16-subnormal halves, zero
+    y = m.mv(torch.from_numpy(x).cuda())
+    dense.check_device()
+    ref = O.matmul_xwT(x, O.dequant_baseline(v, s))
+    assert_close(y.cpu().numpy(), ref)
+
+
+def test_f32_activations_beyond_fp16_range():
+    """Tokens with values beyond fp16's range are staged scaled by a power of two; every token is
+    still within 1e-5 of the oracle, relative to its own output scale."""
+    dense = _dev()
+    N, K = 512, 4096
+    v, s, qk, sc = make_int4(N, K, seed=3)
+    m = dense.DenseMatrix.from_int4(qk.cuda(), sc.cuda())
+    x = np.random.default_rng(4).normal(0, 1, size=(3, K)).astype(np.float32)
+    x[0, :3] = [3e4, -5e4, 1e5]
+    x[1] *= 1e6
+    y = m.mv(torch.from_numpy(x).cuda()).cpu().numpy().astype(np.float64)
+    dense.check_device()
+    ref = O.matmul_xwT(x, O.dequant_baseline(v, s)).astype(np.float64)
+    for t in range(3):
+        assert np.linalg.norm(y[t] - ref[t]) <= 1e-5 * np.linalg.norm(ref[t]), t
+
+
+def test_f32_activations_rejects_more_than_eight_rows():
+    dense = _dev()
+    from opennpu_b200 import libonpu as L
+    v, s, qk, sc = make_int4(256, 512, seed=1)
+    m = dense.DenseMatrix.from_int4(qk.cuda(), sc.cuda())
+    with pytest.raises(L.OnpuError, match="at most 8 rows"):
+        m.mv(torch.zeros(9, 512, device="cuda"))
+
+
+# ------------------------------------------------------------------ BASELINE configs[1] at full size
+def _qwen3_8b(name, seed):
+    N, K = {"qkv": (6144, 4096), "gate_up": (24576, 4096), "down": (4096, 12288)}[name]
+    return (N, K) + make_int4(N, K, seed)
+
+
+@pytest.mark.parametrize("M", [1, 4, 8])
+def test_qwen3_8b_mlp_full_size(M):
+    """Config 2's MLP as the bench runs it: gate/up 24576 x 4096 with the SwiGLU fused (fp32
+    activation), then down 4096 x 12288 on that activation, against the oracle's fp32 chain
+    (reference.py:55-57, :84) on the same weights; the bf16-out SwiGLU against the oracle's
+    activation rounded once to bf16, and q/k/v 6144 x 4096."""
+    dense = _dev()
+    Ng, K, vg, sg, qg, scg = _qwen3_8b("gate_up", 81)
+    Nd, Kd, vd, sd, qd, scd = _qwen3_8b("down", 82)
+    Nq, Kq, vq, sq, qq, scq = _qwen3_8b("qkv", 83)
+    gu = dense.DenseMatrix.from_int4(qg.cuda(), scg.cuda(), gateup=True)
+    dn = dense.DenseMatrix.from_int4(qd.cuda(), scd.cuda())
+    qkv = dense.DenseMatrix.from_int4(qq.cuda(), scq.cuda())
+    x = O.gen_x(M, K, seed=84 + M)
+    xt = torch.from_numpy(x).to(torch.bfloat16).cuda()
+    a32 = gu.mv(xt, epi=dense.EPI_SWIGLU_F32)
+    a16 = gu.mv(xt, epi=dense.EPI_SWIGLU)
+    # the fp32 activation where its rows fit in shared memory, else the bf16 one (the reference's
+    # device rounding), checked against the oracle on the activation it was given
+    f32 = dn.max_f32_rows() >= M
+    y = dn.mv(a32 if f32 else a16)
+    yq = qkv.mv(xt)
+    dense.check_device()
+    h = O.matmul_xwT(x, O.dequant_baseline(vg, sg)).astype(np.float64)
+    I = Ng // 2
+    a = O.silu(h[:, :I]) * h[:, I:]
+    assert_close(a32.cpu().numpy(), a)
+    got16 = a16.float().cpu().numpy()
+    ref16 = O.round_bf16(a.astype(np.float32))
+    assert np.abs(got16 - ref16).max() <= np.abs(ref16).max() * 2.0 ** -8      # one bf16 rounding apart at most
+    ref = O.matmul_xwT(a if f32 else got16, O.dequant_baseline(vd, sd))
+    # fp32 activations with 11-bit halves: the tensor cores' truncating adds leave ~1e-5 over
+    # K = 12288 (still 100x inside the bound)
+    assert_close(y.cpu().numpy(), ref, tight=1e-4)
+    assert_close(yq.cpu().numpy(), O.matmul_xwT(x, O.dequant_baseline(vq, sq)))

@@ -35,24 +35,40 @@ def ckpt(tmp_path):
     return d
 
 
-def test_key_follows_checkpoint_files(ckpt, tmp_path):
+def test_entries_follow_checkpoint_files(ckpt, tmp_path):
+    """An entry counts only while the checkpoint's *.safetensors / *.json files are unchanged
+    (names, sizes, mtimes); other files do not matter; the first store after a change empties the
+    directory."""
     root = tmp_path / "cache"
-    a = PackCache(ckpt, root=root).root
-    assert PackCache(ckpt, root=root).root == a
-    (ckpt / "model.safetensors").write_bytes(b"x" * 101)               # size
-    b = PackCache(ckpt, root=root).root
-    assert b != a
-    t = time.time() + 100
-    os.utime(ckpt / "model.safetensors", (t, t))                       # mtime
-    c = PackCache(ckpt, root=root).root
-    assert c not in (a, b)
-    (ckpt / "generation_config.json").write_text("{}")                 # a new file
-    assert PackCache(ckpt, root=root).root not in (a, b, c)
+    blob = _blob()
+    c = PackCache(ckpt, root=root, keep_free=0)
+    assert c.save_blob("w", blob)
+    assert np.array_equal(PackCache(ckpt, root=root).load_blob("w"), blob)
     (ckpt / "notes.txt").write_text("ignored")                         # not a checkpoint file
-    d = PackCache(ckpt, root=root).root
-    (ckpt / "notes.txt").write_text("still ignored")
-    assert PackCache(ckpt, root=root).root == d
-    assert a.parent == root / "npu4" and a.name.startswith("ckpt-")
+    assert PackCache(ckpt, root=root).load_blob("w") is not None
+    manifests = []
+    for change in (lambda: (ckpt / "model.safetensors").write_bytes(b"x" * 101),          # size
+                   lambda: os.utime(ckpt / "model.safetensors", (time.time() + 100,) * 2),  # mtime
+                   lambda: (ckpt / "generation_config.json").write_text("{}")):           # a new file
+        change()
+        c2 = PackCache(ckpt, root=root, keep_free=0)
+        assert c2.root == c.root and not c2.current()
+        assert c2.load_blob("w") is None and c2.misses == 1
+        assert c2.save_blob("v", blob) and c2.current()
+        assert not c2._path("w").exists() and c2._path("v").exists()   # the stale entry was dropped
+        assert c2.save_blob("w", blob)
+        manifests.append(c2.manifest)
+    assert manifests[0] != manifests[1] != manifests[2]
+    assert c.root.parent == root / f"gpu-layout-v{L.load().onpu_layout_version()}"
+    assert c.root.name.startswith("ckpt-")
+
+
+def test_checkpoints_with_one_name_do_not_share_entries(tmp_path):
+    a, b = tmp_path / "a" / "ckpt", tmp_path / "b" / "ckpt"
+    for d in (a, b):
+        d.mkdir(parents=True)
+        (d / "model.safetensors").write_bytes(b"y")
+    assert PackCache(a, root=tmp_path / "cache").root != PackCache(b, root=tmp_path / "cache").root
 
 
 def test_save_then_load_is_atomic_and_exact(ckpt, tmp_path):
@@ -62,8 +78,9 @@ def test_save_then_load_is_atomic_and_exact(ckpt, tmp_path):
     assert c.save_blob("layer.0.mlp", blob)
     got = c.load_blob("layer.0.mlp")
     assert np.array_equal(got, blob)
-    assert not list(c.root.glob("*.part"))
+    assert not list(c.root.glob("*.tmp"))
     assert c.load_blob("layer.1.mlp") is None                          # names do not collide
+    assert c._path("a/b") != c._path("a_b")
     c2 = PackCache(ckpt, root=tmp_path / "cache", keep_free=0)         # a second load finds it
     assert np.array_equal(c2.load_blob("layer.0.mlp"), blob)
 

@@ -1,8 +1,9 @@
 """Tensor-parallel decoder-layer projections on the GPU: the ranks' shards (column-parallel q/k/v
 and gate/up, row-parallel o and down) run through the int4 GEMV, their row-parallel partials are
 summed, and the layer output matches the oracle's dequantise-then-matmul of the full matrices
-(bf16 intermediates at the same points). One GPU emulates the ranks (the partial sums are added
-by the test, in rank order); with two or more GPUs, two NCCL ranks run the same layer."""
+(opennpu/native/reference.py:55-57, :84: fp32 activations between the projections, never
+rounded). One GPU emulates the ranks (the partial sums are added by the test, in rank order); with
+two or more GPUs, two NCCL ranks run the same layer."""
 import os
 import socket
 
@@ -17,11 +18,12 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 HIDDEN, INTER, QH, KVH = 1024, 2048, 8, 2
+REL_L2, MAX_ABS = 1e-3, 2e-2
 
 
-def _weights(seed):
+def _weights(seed, hidden=HIDDEN, inter=INTER, qh=QH, kvh=KVH):
     w = {}
-    for i, (name, N, K) in enumerate(tp.dense_layer_shapes(HIDDEN, INTER, QH, KVH)):
+    for i, (name, N, K) in enumerate(tp.dense_layer_shapes(hidden, inter, qh, kvh)):
         v, s = O.gen_weights(N, K, seed=seed + i)
         w[name] = (torch.from_numpy(O.pack_baseline(v)), torch.from_numpy(s.view(np.int16)))
     return w
@@ -29,45 +31,85 @@ def _weights(seed):
 
 def _deq(qk, s):
     qk, s = qk.numpy(), s.numpy().view(np.float16)
-    return O.dequant_baseline(O.unpack_baseline(qk, qk.shape[1] * 2), s).astype(np.float64)
+    return O.dequant_baseline(O.unpack_baseline(qk, qk.shape[1] * 2), s)
+
+
+def _mm(x, wq):
+    """x @ W.T in float64 for a (codes, scales) matrix, dequantised a block of rows at a time."""
+    qk, s = wq
+    rows = max(1, (1 << 22) // (qk.shape[1] * 2))
+    out = []
+    for r0 in range(0, qk.shape[0], rows):
+        out.append(x @ _deq(qk[r0:r0 + rows], s[r0:r0 + rows]).astype(np.float64).T)
+    return np.concatenate(out, axis=1)
 
 
 def _oracle_layer(w, x):
-    """The layer's data flow on the full matrices, float64 sums, bf16 where the GPU path rounds."""
-    q = O.round_bf16((x @ _deq(*w["q"]).T).astype(np.float32)).astype(np.float64)
-    h = q @ _deq(*w["o"]).T
-    x2 = O.round_bf16(h.astype(np.float32)).astype(np.float64)
-    g, u = x2 @ _deq(*w["gate"]).T, x2 @ _deq(*w["up"]).T
-    a = O.round_bf16((O.silu(g) * u).astype(np.float32)).astype(np.float64)
-    return a @ _deq(*w["down"]).T
+    """The layer's data flow on the full matrices (o reads the q projection's output as the
+    attention stand-in), float64 sums, no rounding between the projections."""
+    q = _mm(x, w["q"])
+    h = _mm(q, w["o"])
+    g, u = _mm(h, w["gate"]), _mm(h, w["up"])
+    return _mm(O.silu(g) * u, w["down"])
 
 
 def _close(y, ref):
+    """rel-L2 <= 1e-3, and max-abs <= 2e-2 at the scale of one projection's output on N(0, 1)
+    inputs (rms ~10): this synthetic chain has no normalisation between the projections, so its
+    values grow ~10x per projection (to ~1e6 at the Qwen2.5-32B sizes) and the absolute bound is
+    scaled by the output's rms / 10."""
     y = np.asarray(y, np.float64)
+    assert np.isfinite(y).all()
     err = np.linalg.norm(y - ref) / np.linalg.norm(ref)
-    assert err <= 1e-3, err
-    # bf16 intermediates may round one ulp apart between the paths
-    assert np.abs(y - ref).max() <= 2e-2 + np.abs(ref).max() * 2.0 ** -7
+    rms = float(np.sqrt(np.mean(ref ** 2)))
+    mx = float(np.abs(y - ref).max())
+    assert err <= REL_L2, (err, mx, rms)
+    assert mx <= MAX_ABS * max(1.0, rms / 10.0), (err, mx, rms)
+
+
+def _run_emulated(w, x, world, hidden):
+    M = x.shape[0]
+    layers = [tp.TPDecoderLayer.from_full(w, r, world) for r in range(world)]
+    bufs = [lay.buffers(M) for lay in layers]
+    h = torch.zeros(M, hidden, device="cuda")
+    for lay, b in zip(layers, bufs):                     # o partials, summed in rank order
+        lay.qkv(x, b["qkv"], epi=tp.EPI_F32)
+        h += lay.o(b["qkv"][:, :lay.nq], b["h"])
+    y = torch.zeros(M, hidden, device="cuda")
+    for lay, b in zip(layers, bufs):
+        lay.gu(h, b["a"], epi=tp.EPI_SWIGLU_F32)
+        y += lay.dn(b["a"], b["y"])
+    torch.cuda.synchronize()
+    return y.cpu().numpy()
 
 
 @pytest.mark.parametrize("world", [1, 2, 4])
-def test_tp_layer_emulated_ranks_match_oracle(world):
+@pytest.mark.parametrize("M", [1, 3, 8])
+def test_tp_layer_emulated_ranks_match_oracle(world, M):
     w = _weights(seed=10)
-    M = 3
-    x = torch.from_numpy(O.gen_x(M, HIDDEN, seed=11)).to(torch.bfloat16).cuda()
-    layers = [tp.TPDecoderLayer.from_full(w, r, world) for r in range(world)]
-    bufs = [lay.buffers(M) for lay in layers]
-    h = torch.zeros(M, HIDDEN, device="cuda")
-    for lay, b in zip(layers, bufs):                     # o partials, summed in rank order
-        lay.qkv(x, b["qkv"], epi=tp.EPI_BF16)
-        h += lay.o(b["qkv"][:, :lay.nq], b["h"])
-    x2 = h.to(torch.bfloat16)
-    y = torch.zeros(M, HIDDEN, device="cuda")
-    for lay, b in zip(layers, bufs):
-        lay.gu(x2, b["a"], epi=tp.EPI_SWIGLU)
-        y += lay.dn(b["a"], b["y"])
+    x = torch.from_numpy(O.gen_x(M, HIDDEN, seed=11 + M)).cuda()        # fp32 activations (bf16 values)
+    y = _run_emulated(w, x, world, HIDDEN)
+    _close(y, _oracle_layer(w, x.cpu().numpy().astype(np.float64)))
+
+
+def test_tp_layer_whole_call_matches_oracle():
+    """TPDecoderLayer.__call__ itself at one rank (no communicator): fp32 input, fp32 output."""
+    w = _weights(seed=30)
+    x = torch.from_numpy(O.gen_x(2, HIDDEN, seed=31)).cuda()
+    lay = tp.TPDecoderLayer.from_full(w, 0, 1)
+    y = lay(x, lay.buffers(2))
     torch.cuda.synchronize()
-    _close(y.cpu().numpy(), _oracle_layer(w, x.float().cpu().numpy().astype(np.float64)))
+    _close(y.cpu().numpy(), _oracle_layer(w, x.cpu().numpy().astype(np.float64)))
+
+
+@pytest.mark.parametrize("world", [1, 8])
+def test_tp_layer_qwen25_32b_shapes(world):
+    """BASELINE configs[4] at full size: hidden 5120, intermediate 27648, 40 / 8 heads x 128, one
+    decode token, the ranks' shards of TP = 1 and TP = 8 (K blocks of 640 and 3456)."""
+    w = _weights(seed=40, hidden=5120, inter=27648, qh=40, kvh=8)
+    x = torch.from_numpy(O.gen_x(1, 5120, seed=41)).cuda()
+    y = _run_emulated(w, x, world, 5120)
+    _close(y, _oracle_layer(w, x.cpu().numpy().astype(np.float64)))
 
 
 def _free_port():
@@ -86,7 +128,7 @@ def _rank_main(rank, world, port, q):
     try:
         w = _weights(seed=20)
         M = 2
-        x = torch.from_numpy(O.gen_x(M, HIDDEN, seed=21)).to(torch.bfloat16).cuda()
+        x = torch.from_numpy(O.gen_x(M, HIDDEN, seed=21)).cuda()
         lay = tp.TPDecoderLayer.from_full(w, rank, world, group=torch.distributed.group.WORLD)
         y = lay(x, lay.buffers(M))
         torch.cuda.synchronize()
@@ -111,4 +153,4 @@ def test_tp_layer_two_ranks_nccl():
     assert all(p.exitcode == 0 for p in procs)
     w = _weights(seed=20)
     x = O.gen_x(2, HIDDEN, seed=21)
-    _close(y, _oracle_layer(w, O.round_bf16(x).astype(np.float64)))
+    _close(y, _oracle_layer(w, x.astype(np.float64)))

@@ -1,5 +1,7 @@
 """onpu_dense_mv_dev_noalloc (static device scratch, no allocation in the call) against
-onpu_dense_mv_dev on the same matrix and inputs, two calls in a row.
+onpu_dense_mv_dev on the same matrix and inputs, two calls in a row. Both entries launch the same
+grid, so the split rows are added in the same order and the outputs agree bit for bit; the
+regular path itself is checked against the oracle by the GEMV parity tests.
 
 Collected last on purpose: it must pass in a fresh process (the first call sets up the static
 scratch) and after every other test (the shared scratch and status word have seen other launches).
@@ -8,7 +10,7 @@ import pytest
 import torch
 
 from opennpu_b200 import libonpu as L
-from opennpu_b200.dense import DenseMatrix, EPI_F32, EPI_BF16, EPI_SWIGLU
+from opennpu_b200.dense import DenseMatrix, EPI_F32, EPI_BF16, EPI_SWIGLU, EPI_SWIGLU_F32, EPI_PAIRSUM
 
 pytestmark = pytest.mark.gpu
 
@@ -29,8 +31,9 @@ def _x(rows, K, seed):
 
 
 def _call(fn, m, x, rows, epi):
-    n_out = m.N // 2 if epi == EPI_SWIGLU else m.N
-    y = torch.empty(rows, n_out, device="cuda", dtype=torch.float32 if epi == EPI_F32 else torch.bfloat16)
+    n_out = m.N // 2 if epi in (EPI_SWIGLU, EPI_SWIGLU_F32, EPI_PAIRSUM) else m.N
+    bf16 = epi in (EPI_BF16, EPI_SWIGLU)
+    y = torch.empty(rows, n_out, device="cuda", dtype=torch.bfloat16 if bf16 else torch.float32)
     s = torch.cuda.current_stream().cuda_stream
     rc = fn(m.h, x.data_ptr(), x.stride(0), rows, y.data_ptr(), y.stride(0), epi, s)
     L.check(rc, fn.__name__)
@@ -38,12 +41,9 @@ def _call(fn, m, x, rows, epi):
 
 
 def _close(a, b):
-    # two bf16 outputs may round one bf16 ulp apart (2^-8 relative) on top of the fp32 tolerance
-    ulp = b.float().abs().max().item() * 2.0 ** -8 if b.dtype == torch.bfloat16 else 0.0
-    a, b = a.float(), b.float()
-    err = (a - b).norm() / b.norm().clamp_min(1e-30)
-    assert err.item() <= REL_L2, err.item()
-    assert (a - b).abs().max().item() <= MAX_ABS + ulp
+    """Bit-identical (same grid and summation order), hence also within the output tolerance."""
+    assert a.dtype == b.dtype and a.shape == b.shape
+    assert torch.equal(a, b), (a.float() - b.float()).abs().max().item()
 
 
 # (N, K, gateup, epilogue, (rows of call 1, rows of call 2))
@@ -52,6 +52,8 @@ CASES = [
     (4096, 4096, False, EPI_F32, (17, 3)),          # two MMA tiles, then one
     (1024, 2048, False, EPI_BF16, (16, 16)),
     (2048, 1024, True, EPI_SWIGLU, (1, 40)),        # fused SwiGLU, several descriptors
+    (6144, 4096, True, EPI_SWIGLU_F32, (1, 8)),     # fused SwiGLU with fp32 outputs
+    (4096, 12288, False, EPI_F32, (1, 2)),          # a Qwen3-8B down projection: each CTA stages its part of K
 ]
 
 
@@ -64,6 +66,21 @@ def test_noalloc_matches_dev_two_calls(N, K, gateup, epi, rows):
         x = _x(r, K, seed=100 * i + r)
         y_ref = _call(lib.onpu_dense_mv_dev, m, x, r, epi)
         y_new = _call(lib.onpu_dense_mv_dev_noalloc, m, x, r, epi)
+        torch.cuda.synchronize()
+        _close(y_new, y_ref)
+    assert lib.onpu_check_device() == 0, L.last_error()
+
+
+def test_noalloc_two_pass_pairsum():
+    """The two-pass (residual) matrix and its pair-sum epilogue through both entries."""
+    lib = L.require_device()
+    g = torch.Generator(device="cuda").manual_seed(11)
+    W = torch.randn(512, 2048, device="cuda", generator=g) * 0.05
+    m = DenseMatrix.from_float_residual(W)
+    for i, r in enumerate((1, 6)):
+        x = _x(r, 2048, seed=50 + i)
+        y_ref = _call(lib.onpu_dense_mv_dev, m, x, r, EPI_PAIRSUM)
+        y_new = _call(lib.onpu_dense_mv_dev_noalloc, m, x, r, EPI_PAIRSUM)
         torch.cuda.synchronize()
         _close(y_new, y_ref)
     assert lib.onpu_check_device() == 0, L.last_error()
