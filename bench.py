@@ -1,21 +1,27 @@
 """Benchmark of the int4 group-32 weight-only matmul path on B200 (one JSON line on rank 0).
 
-Default workload: the Qwen3-8B decode projections, 36 layers of
-random int4 weights (q/k/v fused 6144x4096, gate/up fused 24576x4096 with the SwiGLU fused into
-its epilogue, down 4096x12288), M tokens (default 1) of bf16 N(0,1) activations. One step = one
-decode pass over the 36 layers' projections = 108 GEMV launches, replayed from a CUDA graph.
-3.57 GB of weights per step (> the 126 MB L2), so every step streams HBM; no flush is needed.
+Default workload: the Qwen2.5-32B dense decode stack, 64 layers of
+random int4 group-32 weights (hidden 5120, intermediate 27648, 40 query / 8 KV heads x 128),
+tensor-parallel over the ranks: q/k/v and gate/up column-parallel, o and down row-parallel with
+an all-reduce after each (a peer-memory kernel fused with the row-parallel GEMV, or NCCL). M = 1
+token per step by default (--rows 8 for the batched decode); the activations between the
+projections stay fp32. One step = one decode pass over the 64 layers' projections from a CUDA
+graph; 17.6 GB of weights per step at TP 1 (> L2, no flush needed).
 
-Metric: achieved HBM GB/s = algorithmic bytes (int4 codes + fp16 scales + activations in +
-outputs) per step / step time. Also reported: tokens/s = M / step time.
+Metric: decode tokens/s (strong scaling: the same model over N GPUs). Also in the line: the
+dominant kernel (the gate/up GEMV + SwiGLU) timed alone against the measured HBM bandwidth, the
+reference's CPU path timed on the host cores, the step through pinned host copies (e2e), a
+parity check of one layer against the oracle, and at N = 1 the Qwen3-8B decode projections
+(configs[1]) in GB/s.
 
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config qwen3-8b|gemv] [--m M]
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--config qwen2.5-32b|qwen3-8b|gemv|prefill|moe|attn] [--rows M]
 
---gpus N > 1 runs under torchrun, one rank per GPU, each rank an independent replica of the
-decode stack on its own tokens (the dense projections of one replica need no exchange: replicas
-only, weak scaling). Time = max over ranks of the device-timed region.
---impl reference times the reference's CPU dequantise-then-matmul path (restated in oracle/) on
-this host's cores, on a bounded sample of the same workload.
+Other configs: qwen3-8b (configs[1], GB/s; at --gpus N independent replicas), gemv,
+prefill (configs[2], TFLOP/s), moe (configs[3], tokens/s; expert-parallel at N > 1), attn (the
+decode attention row). --gpus N > 1 runs under torchrun, one rank per GPU; time = max over ranks
+of the device-timed region. --impl reference times the reference's CPU dequantise-then-matmul
+path (restated in oracle/) on this host's cores, on a bounded sample of the same workload.
 """
 import argparse
 import json
@@ -622,7 +628,7 @@ def run_moe(args):
     rank, world, local = dist_setup(args.gpus)
     hbm, _, peak_kind = peaks()
     T = args.m if args.m > 0 else 1
-    layers = args.layers if args.layers != LAYERS else M_LAYERS
+    layers = args.layers
     group = torch.distributed.group.WORLD if world > 1 else None
     work = MoEStack(T, seed=3000, layers=layers, rank=rank, world=world, group=group)
     s = torch.cuda.Stream()
@@ -725,6 +731,56 @@ def run_moe(args):
 T_HIDDEN, T_INTER, T_QH, T_KVH, T_LAYERS = 5120, 27648, 40, 8, 64
 
 
+def tp_layer0_parity(work, rank):
+    """One layer of the timed stack against the oracle: layer 0's weights drawn again from the
+    stack's seed, dequantised per 32 on the host and multiplied in float64 (reference.py:24-28,
+    :55-57, :84 semantics; o takes q's output as the attention stand-in). At one rank the whole
+    layer (all-reduced output) is checked; with more ranks, this rank's q/k/v shard."""
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(work.seed)
+    mats = [gen_int4_cuda(N, K, gen) for N, K in work.shapes]
+    lay, M = work.layers[0], work.M
+    x = torch.randn(M, T_HIDDEN, device="cuda", generator=torch.Generator(device="cuda").manual_seed(99))
+    x = x.to(torch.bfloat16).to(work.x.dtype)
+    b = lay.buffers(M)
+
+    def mm(xx, qk, sc):                     # float64 x @ W.T, W dequantised a block of rows at a time
+        qk, sc = qk.cpu(), sc.cpu().float()
+        out = []
+        for r0 in range(0, qk.shape[0], 2048):
+            q = qk[r0:r0 + 2048]
+            v = torch.stack([(q & 15).to(torch.int16), (q >> 4).to(torch.int16)], -1).view(q.shape[0], -1)
+            v = torch.where(v >= 8, v - 16, v).double()
+            w = (v.view(v.shape[0], -1, 32) * sc[r0:r0 + 2048].double()[..., None]).view(v.shape[0], -1)
+            out.append(xx @ w.T)
+        return torch.cat(out, 1)
+
+    xd = x.double().cpu()
+    if work.world == 1:
+        y = lay(x, b).double().cpu()
+        torch.cuda.synchronize()
+        q = mm(xd, *mats[0])[:, :lay.nq]
+        h = mm(q, *mats[1])
+        gu = mm(h, *mats[2])
+        I = gu.shape[1] // 2
+        a = gu[:, :I] / (1 + torch.exp(-gu[:, :I])) * gu[:, I:]
+        ref = mm(a, *mats[3])
+        what = "layer 0 (q/k/v, o, gate/up + SwiGLU, down)"
+    else:
+        y = lay.qkv(x, b["qkv"], epi=work.tp.EPI_F32 if work.f32 else work.tp.EPI_BF16).double().cpu()
+        torch.cuda.synchronize()
+        ref = mm(xd, *mats[0])
+        if not work.f32:
+            ref = ref.float().bfloat16().double()
+        what = f"layer 0, rank {rank}'s q/k/v shard"
+    err = float((y - ref).norm() / ref.norm())
+    mx = float((y - ref).abs().max())
+    rms = float(ref.pow(2).mean().sqrt())
+    return {"what": what, "rel_l2": err, "max_abs": mx, "ref_rms": rms,
+            "ok": bool(err <= 1e-3 and mx <= 2e-2 * max(1.0, rms / 10.0)),
+            "bound": "rel-L2 <= 1e-3; max-abs <= 2e-2 at a projection's output scale (rms 10), scaled by rms / 10"}
+
+
 class TPStack:
     """Qwen2.5-32B decode projections, 64 layers of random int4 weights, tensor-parallel
     over the ranks: q/k/v and gate/up column-parallel (row blocks), o and down row-parallel (K
@@ -758,7 +814,22 @@ class TPStack:
         shards = [(q + 2 * kv, T_HIDDEN), (T_HIDDEN, h_r), (2 * i_r, T_HIDDEN), (T_HIDDEN, i_r)]
         xb = 4 if self.f32 else 2
         self.bytes_per_layer = sum(int4_param_bytes(N, K) + M * K * xb + M * N * 4 for N, K in shards)
-        self.launches_per_step = 4 * layers                   # our GEMVs (plus NCCL all-reduces, casts)
+        # our kernels per layer: 4 GEMVs (o and down carry the peer all-reduce in the same launch)
+        self.launches_per_step = 4 * layers
+        self.seed, self.shapes = seed, shards
+
+    def dominant(self, s):
+        """The gate/up GEMV with its fused SwiGLU (the largest launch of the step) over every layer:
+        (callable, algorithmic bytes per launch, launches per call, kernel name)."""
+        tp, b = self.tp, self.bufs
+        x, epi = (b["h"], tp.EPI_SWIGLU_F32) if self.f32 else (b["x2"], tp.EPI_SWIGLU)
+        N, K = self.layers[0].gu.N, self.layers[0].gu.K
+        nbytes = int4_param_bytes(N, K) + self.M * K * x.element_size() + self.M * (N // 2) * b["a"].element_size()
+
+        def run():
+            for lay in self.layers:
+                lay.gu(x, b["a"], epi=epi, stream=s)
+        return run, nbytes, len(self.layers), f"gemv_int4_kernel gate_up {N}x{K} + SwiGLU"
 
     def step(self):
         x = self.x
@@ -800,17 +871,67 @@ def cpu_tp_sample(M, seconds=10.0, seed=0):
     return n * layer_bytes / dt / 1e9, torch.get_num_threads(), f"{n} x one Qwen2.5-32B layer's 7 projections (dequant + fp32 matmul, M={M})"
 
 
+def qwen3_8b_extra(args, hbm):
+    """configs[1] at one GPU, kept beside the default line: the Qwen3-8B decode projections (36
+    layers, M = 1, fp32 MLP activation) in GB/s and its gate/up launch against the HBM roofline."""
+    work = DecodeStack(1, seed=1000, layers=LAYERS, act="f32")
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            work.step()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        work.step()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(10, args.steps)
+    e0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(steps):
+            g.replay()
+    e1.record(s)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    run_dom, dom_bytes, dom_n, dom_name = work.dominant()
+    gd = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gd, stream=s):
+        run_dom()
+    with torch.cuda.stream(s):
+        gd.replay()
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(20):
+            gd.replay()
+    d1.record(s)
+    d1.synchronize()
+    us = d0.elapsed_time(d1) * 1e3 / (20 * dom_n)
+    del g, gd
+    gbs = work.bytes_per_step / (ms * 1e-3) / 1e9
+    out = {"workload": "qwen3-8b-decode-projections (configs[1]), M = 1, 36 layers", "value": round(gbs, 2),
+           "unit": "GB/s", "ms_per_step": round(ms, 4), "tokens_per_s": round(1e3 / ms, 1),
+           "roofline": {"kernel": dom_name, "achieved": round(dom_bytes / (us * 1e-6) / 1e9, 1), "peak": hbm,
+                        "frac": round(dom_bytes / (us * 1e-6) / 1e9 / hbm, 4), "us_per_launch": round(us, 3)}}
+    del work
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_tp(args):
     rank, world, local = dist_setup(args.gpus)
     hbm, _, peak_kind = peaks()
     M = args.m
-    layers = args.layers if args.layers != LAYERS else T_LAYERS
+    layers = args.layers
     group = torch.distributed.group.WORLD if world > 1 else None
     allreduce = None
     if world > 1 and args.allreduce == "peer":
         from opennpu_b200.comm import PeerAllReduce
-        allreduce = PeerAllReduce(group, cap_floats=M * T_HIDDEN)
+        # one communicator per call site (o, down): the fused GEMV's CTAs sum rows fixed by the shape
+        allreduce = (PeerAllReduce(group, cap_floats=M * T_HIDDEN), PeerAllReduce(group, cap_floats=M * T_HIDDEN))
     work = TPStack(M, rank, world, group, seed=4000 + rank, layers=layers, allreduce=allreduce)
+    f32 = work.f32
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(max(args.warmup, 1)):
@@ -850,6 +971,29 @@ def run_tp(args):
     rank_bytes = work.bytes_per_layer * layers
     gbs_rank = rank_bytes / (ms_step * 1e-3) / 1e9
 
+    # the dominant kernel alone: a graph of its launches over all layers, CUDA events on its stream
+    run_dom, dom_bytes, dom_n, dom_name = work.dominant(s)
+    gdom = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gdom, stream=s):
+        run_dom()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            gdom.replay()
+    reps = 20
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0.record(s)
+    with torch.cuda.stream(s):
+        for _ in range(reps):
+            gdom.replay()
+    d1.record(s)
+    d1.synchronize()
+    dom_us = d0.elapsed_time(d1) * 1e3 / (reps * dom_n)
+    del gdom
+    if world > 1:
+        t = torch.tensor([dom_us], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        dom_us = float(t.item())
+
     e2e = None
     if not args.no_e2e:
         hx = torch.empty(work.x.shape, dtype=work.x.dtype, pin_memory=True)
@@ -872,40 +1016,65 @@ def run_tp(args):
             dt = float(t.item())
         e2e = {"value": round(M / dt, 2), "unit": "tokens/s", "h2d_bytes_per_step": hx.numel() * hx.element_size(),
                "d2h_bytes_per_step": hy.numel() * 4, "ms_per_step": round(dt * 1e3, 3),
-               "path": "TPDecoderLayer stack (onpu_dense_mv_dev; row-parallel o/down fused with the peer all-reduce, or NCCL) from a CUDA graph, pinned host "
-                       "input/output copies and a host synchronisation per step"}
-    cpu = None
+               "path": "TPDecoderLayer stack (onpu_dense_mv_f32_dev / onpu_dense_mv_dev; row-parallel o and down "
+                       "fused with the peer all-reduce at N > 1) from a CUDA graph, pinned host input/output "
+                       "copies and a host synchronisation per step (wall clock)"}
+    del graph
+    parity = tp_layer0_parity(work, rank)
+    cpu = extra = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, sample = cpu_tp_sample(M, seconds=args.cpu_seconds)
-        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": sample}
+        step_bytes = layers * sum(int4_param_bytes(N, K) for N, K in work.shapes)
+        cpu = {"value": round(v * 1e9 / step_bytes * M, 4), "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": sample, "weight_gb_per_s": round(v, 3)}
+    if rank == 0 and world == 1 and not args.no_extra:
+        del work
+        torch.cuda.empty_cache()
+        extra = qwen3_8b_extra(args, hbm)
     if rank == 0:
+        achieved = dom_bytes / (dom_us * 1e-6) / 1e9
+        traffic = None
+        tpf = ROOT / "profiles" / "traffic.json"
+        if tpf.exists():
+            traffic = json.loads(tpf.read_text()).get(f"qwen2.5-32b/tp{world}/M{M}")
         line = {
             "metric": "int4 dense decode stack tokens/s (Qwen2.5-32B, tensor-parallel)", "value": round(tok_s, 2),
             "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "int4 weights, " + ("fp32 activations (two fp16 halves)" if work.f32 else "bf16 activations")
+            "dtype": "int4 weights, " + ("fp32 activations (two fp16 halves)" if f32 else "bf16 activations")
                      + ", fp32 accumulate",
-            "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1))",
-            "config": {"workload": "qwen2.5-32b-decode-projections-tp", "M": M, "layers": layers,
-                       "parallelism": f"tp{world}", "gb_per_s_all_ranks": round(gbs_rank * world, 1),
-                       "bytes_per_step_per_gpu": rank_bytes,
-                       "l2": "inputs larger than L2 (no flush needed)", "cuda_graph": True,
-                       "collective": (("one-shot all-reduce over NVLink peer memory (libonpu comm kernel)"
-                                       if allreduce is not None else "NCCL all-reduce") + " (fp32) after o and down")
-                       if world > 1 else None},
-            "roofline": {"bound": "hbm", "achieved": round(gbs_rank, 1), "peak": hbm, "unit": "GB/s",
-                         "frac": round(gbs_rank / hbm, 4), "peak_kind": peak_kind + " (copy bandwidth)",
-                         "traffic": None, "kernel": "whole decode step per GPU (GEMVs, all-reduces, casts)"},
-            "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": work.launches_per_step * args.steps,
+            "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1) input)",
+            "config": tp_config(M, layers, world),
+            "details": {"gb_per_s_all_ranks": round(gbs_rank * world, 1), "gb_per_s_per_gpu": round(gbs_rank, 1),
+                        "bytes_per_step_per_gpu": rank_bytes, "l2": "inputs larger than L2 (no flush needed)",
+                        "cuda_graph": True,
+                        "collective": (("the row-parallel GEMV fused with a one-shot all-reduce over NVLink peer "
+                                        "memory (libonpu comm kernel)" if allreduce is not None else "NCCL all-reduce")
+                                       + " (fp32) after o and down") if world > 1 else None},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(achieved / hbm, 4), "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": dom_name, "algorithmic_bytes_per_launch": dom_bytes,
+                         "us_per_launch": round(dom_us, 3),
+                         "step_gb_per_s_per_gpu": round(gbs_rank, 1), "step_frac": round(gbs_rank / hbm, 4)},
+            "parity": parity, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
+            "gpu_launches": 4 * layers * args.steps,
         }
+        if extra is not None:
+            line["qwen3_8b_decode"] = extra
         print(json.dumps(line), flush=True)
-    del graph
     if world > 1:
         torch.distributed.barrier()
         if allreduce is not None:
-            allreduce.close()
+            for ar in allreduce:
+                ar.close()
             torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def tp_config(M, layers, world):
+    """The config dict of the qwen2.5-32b lines, the same in both arms."""
+    return {"workload": "qwen2.5-32b-decode-projections-tp", "M": M, "layers": layers, "parallelism": f"tp{world}"}
+
 
 
 class GemvRotation:
@@ -938,17 +1107,36 @@ class GemvRotation:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    """SM clock, power and clock-event (throttle) reasons sampled every 10 ms through NVML while
+    the timed region runs (short timed regions still get samples); nvidia-smi every 200 ms when
+    NVML is not importable."""
     Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
          "clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
         self.proc = None
+        self.nvml = None
+        self.samples = []           # (sm MHz, reason bits)
         self.lines = []
+        self.max_mhz = None
+        self.stop_flag = threading.Event()
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self.idx)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM))
+            self.t = threading.Thread(target=self._poll, daemon=True)
+            self.t.start()
+            return
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-i", str(self.idx), "-lms", "200"], stdout=subprocess.PIPE,
@@ -962,11 +1150,31 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
+    def _poll(self):
+        nv = self.nvml
+        get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop_flag.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)),
+                                     int(get_reasons(self.h))))
+            except Exception:
+                pass
+            time.sleep(0.01)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.nvml is not None:
+            self.stop_flag.set()
+            self.t.join(timeout=2)
+            if not self.samples:
+                return None
+            reasons = sorted(n for n, bit in self.REASONS.items() if any(r & bit for _, r in self.samples))
+            return {"sm_mhz": float(np.median([c for c, _ in self.samples])), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml, 10 ms"}
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -991,7 +1199,8 @@ class ClockSampler:
                     reasons.add(n)
         if not sm:
             return None
-        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvidia-smi, 200 ms"}
 
 
 # ------------------------------------------------------------------ CPU baseline (oracle port)
@@ -1236,8 +1445,8 @@ def run_reference(args):
         else:
             gbs, cores, sample = cpu_tp_sample(M, seconds=per)
             from opennpu_b200 import tp
-            step_bytes = T_LAYERS * sum(int4_param_bytes(N, K)
-                                        for _, N, K in tp.dense_layer_shapes(T_HIDDEN, T_INTER, T_QH, T_KVH))
+            step_bytes = args.layers * sum(int4_param_bytes(N, K)
+                                           for _, N, K in tp.dense_layer_shapes(T_HIDDEN, T_INTER, T_QH, T_KVH))
             v = gbs * 1e9 / step_bytes * M
         if i >= args.warmup:
             vals.append(v)
@@ -1257,10 +1466,12 @@ def run_reference(args):
     }[cfg]
     line = {"impl": "reference", "metric": metric, "value": round(v, 4), "unit": unit,
             "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if cfg == "qwen2.5-32b" else "weak", "vs_baseline": None,
             "dtype": "bf16 cache, fp32 arithmetic" if cfg == "attn" else "int4 dequantised to fp32",
             "data": "synthetic",
-            "config": {"workload": workload, "M": M, **({"context": args.context} if cfg == "attn" else {})},
+            "config": (tp_config(M, args.layers, int(os.environ.get("WORLD_SIZE", "1"))) if cfg == "qwen2.5-32b"
+                       else {"workload": workload, "M": M, "layers": args.layers,
+                             **({"context": args.context} if cfg == "attn" else {})}),
             "cpu_baseline": {"value": round(v, 4), "unit": unit, "cores": cores, "kind": kind,
                              "sample": f"per step ({per:.2f} s): {sample}"},
             "e2e": {"value": round(v, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -1273,7 +1484,8 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="qwen3-8b", choices=["qwen3-8b", "gemv", "prefill", "moe", "qwen2.5-32b", "attn"])
+    ap.add_argument("--config", default="qwen2.5-32b",
+                    choices=["qwen2.5-32b", "qwen3-8b", "gemv", "prefill", "moe", "attn"])
     ap.add_argument("--context", type=int, default=4096, help="attn: KV-cache length (tokens)")
     ap.add_argument("--m", "--rows", dest="m", type=int, default=1,
                     help="tokens (M / T); spell it --rows under torchrun, which claims --m")
@@ -1281,14 +1493,18 @@ def main():
                     help="qwen2.5-32b at N>1: the row-parallel all-reduce (peer-memory kernel or NCCL)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true", help="qwen2.5-32b: skip the Qwen3-8B figures at N = 1")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--act", default="f32", choices=["f32", "bf16"],
                     help="qwen3-8b: the MLP activation between gate/up and down (fp32, or rounded to bf16)")
     ap.add_argument("--mode", default="launches", choices=["chain", "launches"],
                     help="chain: the step as one persistent GEMV-chain launch; launches: one launch per matrix")
-    ap.add_argument("--layers", type=int, default=LAYERS,
-                    help="decoder layers in the stack (profiling captures use fewer; the metric is quoted at 36)")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers in the stack (profiling captures use fewer; the metric is quoted at the "
+                         "config's own count: qwen2.5-32b 64, qwen3-8b 36, moe 48)")
     args = ap.parse_args()
+    if args.layers is None:
+        args.layers = {"qwen2.5-32b": T_LAYERS, "qwen3-8b": LAYERS, "moe": M_LAYERS, "attn": A_LAYERS}.get(args.config, 1)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

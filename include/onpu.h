@@ -241,13 +241,22 @@ int onpu_comm_ipc_handle(void *comm, void *out64);
 int onpu_comm_open(void *comm, const void *handles);
 int onpu_comm_allreduce(void *comm, const float *src, float *dst, void *dst_bf16, int64_t n, void *stream);
 void onpu_comm_free(void *comm);
-/* The row-parallel projection and its all-reduce fused (no reference counterpart): y / y_bf16
- * (either may be NULL) = the sum over ranks of x . W_rank^T, rows x N fp32 / bf16, where W_rank is
- * this rank's K block (dense handle h, no gate/up or residual rows) and comm an opened
- * onpu_comm handle with cap >= rows x N. The GEMV's epilogue stores every finished output, paired
- * with the call number in one 8-byte word, straight into every rank's buffer over NVLink while the
- * rest of the matrix is still streaming; a second small launch waits for all ranks' words and adds
- * them in rank order. Same call-sequence rule as onpu_comm_allreduce. 0 ok, < 0 error. */
+/* How long a kernel waits for another rank's words (the fused all-reduce GEMV and
+ * onpu_comm_allreduce) before it gives up, sets the device status (onpu_check_device reports
+ * an all-reduce timeout) and returns with the values as found: 2 s unless set; later launches use
+ * the new limit. 0 ok, < 0 error. */
+int onpu_comm_set_wait(double seconds);
+/* The row-parallel projection and its all-reduce fused in one launch (no reference counterpart):
+ * y / y_bf16 (either may be NULL) = the sum over ranks of x . W_rank^T, rows x N fp32 / bf16,
+ * where W_rank is this rank's K block (dense handle h, no gate/up or residual rows) and comm an
+ * opened onpu_comm handle with cap >= rows x N. The GEMV's epilogue stores every finished output,
+ * paired with the call number in one 8-byte word, straight into every rank's buffer over NVLink
+ * while the rest of the matrix is still streaming; after its range each CTA waits (bounded) for
+ * every rank's words of the rows it finished, adds them in rank order (the same sums on every
+ * rank) and writes them. The rows each CTA sums follow from the shape, so every call on one
+ * communicator must have the same matrix shape, row count and activation type (use one
+ * communicator per call site, e.g. one for o and one for down), and no onpu_comm_allreduce on it;
+ * every rank makes the same sequence of calls. 0 ok, < 0 error. */
 int onpu_dense_mv_allreduce_dev(void *h, void *comm, const void *x, int64_t ldx, int64_t rows, float *y,
                                 void *y_bf16, void *stream);
 /* The same with fp32 activations (rows <= 8, staged as in onpu_dense_mv_f32_dev). */

@@ -53,17 +53,25 @@ class PeerAllReduce:
         except Exception:   # interpreter shutdown
             pass
 
+    site = None                  # (N, K, rows, dtype) of the fused calls on this communicator
+
     def linear(self, m, x, out=None, out_bf16=None, stream=None):
-        """The row-parallel projection fused with this all-reduce: the sum over ranks of
-        x . W_rank^T for this rank's DenseMatrix shard m, its outputs sent to the peers from the
-        GEMV's epilogue. x: bf16 [M, K_rank], or fp32 [M <= 8, K_rank] (staged as two fp16 halves
-        per value); out fp32 and / or out_bf16 bf16 [M, N]."""
+        """The row-parallel projection fused with this all-reduce, one launch: the sum over ranks of
+        x . W_rank^T for this rank's DenseMatrix shard m; the GEMV's epilogue sends its outputs to
+        the peers and each CTA then sums every rank's words of its own rows. x: bf16 [M, K_rank], or
+        fp32 [M <= 8, K_rank] (staged as two fp16 halves per value); out fp32 and / or out_bf16
+        bf16 [M, N]. Every call on one communicator has the same shape (one per call site)."""
         assert x.is_cuda and x.dtype in (torch.bfloat16, torch.float32) and x.dim() == 2 and x.stride(1) == 1
         M = x.shape[0]
         if out is None and out_bf16 is None:
             out = torch.empty(M, m.N, device=x.device)
         for o, dt in ((out, torch.float32), (out_bf16, torch.bfloat16)):
             assert o is None or (o.dtype == dt and o.is_contiguous() and o.shape == (M, m.N))
+        site = (m.N, m.K, M, x.dtype)
+        if self.site is None:
+            self.site = site
+        elif self.site != site:                 # each CTA sums rows fixed by the shape: one site per handle
+            raise ValueError(f"this communicator serves {self.site}; use another one for {site}")
         fn = "onpu_dense_mv_allreduce_f32_dev" if x.dtype == torch.float32 else "onpu_dense_mv_allreduce_dev"
         rc = getattr(L.load(), fn)(m.h, self.h, x.data_ptr(), x.stride(0), M, 0 if out is None else out.data_ptr(),
                                    0 if out_bf16 is None else out_bf16.data_ptr(), _stream_ptr(stream))

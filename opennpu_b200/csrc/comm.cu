@@ -7,6 +7,7 @@
 //
 // Every rank owns one buffer (cudaMalloc, shared with the peers through CUDA IPC handles):
 //   slots[2][world][cap] of 8-byte words {fp32 value, call number} | calls[kCommCtas] u32
+//   | the call counters of the row-parallel GEMV's CTAs (kEpiPeer, gemv.cu) [kPeerCtaCounters] u32
 // A call is one launch of kCommCtas CTAs; CTA b owns elements [b * per, (b + 1) * per):
 //  1. every thread stores its elements of the local partial, each paired with the call number in
 //     one 8-byte store, into slot [parity][rank] of every rank's buffer (peer stores over NVLink);
@@ -30,7 +31,6 @@ namespace onpu_b200 {
 namespace {
 
 constexpr int kCommThreads = 256;
-constexpr uint64_t kCommWaitNs = 2000000000ull;
 
 struct CommParams {
     uint2 *bufs[kCommMaxRanks];      // every rank's buffer (this rank's own at [rank])
@@ -42,6 +42,7 @@ struct CommParams {
     int64_t n;
     int *err;
     int send;                        // 0: the values were sent by a GEMV epilogue; only receive
+    uint64_t wait_ns;                // how long a thread waits for a peer's word
 };
 
 __device__ __forceinline__ void st_word(uint2 *p, uint32_t v, uint32_t tag) {
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(kCommThreads) comm_allreduce_kernel(const Comm
             if (r.y != c) {
                 const uint64_t t0 = global_timer_ns();
                 for (int it = 0; r.y != c; ++it) {
-                    if ((it & 255) == 255 && global_timer_ns() - t0 > kCommWaitNs) {
+                    if ((it & 255) == 255 && global_timer_ns() - t0 > p.wait_ns) {
                         atomicOr(p.err, 16);
                         break;
                     }
@@ -97,11 +98,11 @@ __global__ void __launch_bounds__(kCommThreads) comm_allreduce_kernel(const Comm
 }  // namespace
 
 int64_t comm_buffer_bytes(int world, int64_t cap) {
-    return 2 * static_cast<int64_t>(world) * cap * 8 + kCommCtas * 4;
+    return 2 * static_cast<int64_t>(world) * cap * 8 + (kCommCtas + kPeerCtaCounters) * 4;
 }
 
 cudaError_t comm_allreduce_launch(void *const *bufs, int rank, int world, int64_t cap, const float *src, float *dst,
-                                  void *dst_bf16, int64_t n, int *err, cudaStream_t stream) {
+                                  void *dst_bf16, int64_t n, int *err, uint64_t wait_ns, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     if (world < 1 || world > kCommMaxRanks || n > cap) return cudaErrorInvalidValue;
     CommParams p{};
@@ -115,12 +116,13 @@ cudaError_t comm_allreduce_launch(void *const *bufs, int rank, int world, int64_
     p.n = n;
     p.err = err;
     p.send = 1;
+    p.wait_ns = wait_ns;
     comm_allreduce_kernel<<<kCommCtas, kCommThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }
 
 cudaError_t comm_reduce_launch(void *const *bufs, int rank, int world, int64_t cap, float *dst, void *dst_bf16,
-                               int64_t n, int *err, cudaStream_t stream) {
+                               int64_t n, int *err, uint64_t wait_ns, cudaStream_t stream) {
     if (n <= 0) return cudaSuccess;
     if (world < 1 || world > kCommMaxRanks || n > cap) return cudaErrorInvalidValue;
     CommParams p{};
@@ -133,6 +135,7 @@ cudaError_t comm_reduce_launch(void *const *bufs, int rank, int world, int64_t c
     p.n = n;
     p.err = err;
     p.send = 0;
+    p.wait_ns = wait_ns;
     comm_allreduce_kernel<<<kCommCtas, kCommThreads, 0, stream>>>(p);
     return cudaGetLastError();
 }

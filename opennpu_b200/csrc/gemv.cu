@@ -49,8 +49,10 @@ using namespace gemv_core;
 
 
 // Store the finished sums of strip rows r (v_lo) and r+8 (v_hi) of one token (output row yr).
+// call: kEpiPeer's all-reduce call number of this CTA.
 template <int EPI>
-__device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, int r, int yr, float v_lo, float v_hi) {
+__device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, int r, int yr, float v_lo, float v_hi,
+                                           uint32_t call) {
     if (yr < 0) return;
     if constexpr (EPI == kEpiSwiGLU || EPI == kEpiPairSum) {
         const int i = g * (kRowGroup / 2) + s * 8 + r;       // row r and row r+8 of the strip pair up
@@ -67,7 +69,6 @@ __device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, in
     } else if constexpr (EPI == kEpiPeer) {
         // row-parallel projection: each finished value goes straight to every rank's all-reduce
         // buffer as one 8-byte {value, call number} word (the receive side waits on the number)
-        const uint32_t call = __ldcg(p.peer_calls) + 1u;
         const int64_t set = static_cast<int64_t>(call & 1u) * p.peer_world;
         const int row = g * kRowGroup + s * kStripRows + r;
 #pragma unroll
@@ -95,6 +96,47 @@ __device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, in
                 else reinterpret_cast<__nv_bfloat16 *>(p.y)[o] = __float2bfloat16_rn(v);
             }
         }
+    }
+}
+
+// kEpiPeer, after the CTA's range: the rows this CTA finished (row groups whose first chunk lies in
+// [lo, hi): it summed their split parts) were sent to every rank; the same CTA index of every rank
+// finished the same rows (same shape, same grid), so wait for each rank's word of each of them
+// carrying this call's number, add the ranks' values in rank order (the same float sum on every
+// rank) and write the sum. Waits are bounded (peer_wait_ns, 2 s by default; then the error word and
+// the value as found).
+__device__ void peer_receive(const GemvParams &p, int lo, int hi, uint32_t call, int tid, int nthr) {
+    const int rg0 = (lo + p.chunks - 1) / p.chunks, rg1 = (hi + p.chunks - 1) / p.chunks;   // one job
+    const int mt = p.jobs[0].m;
+    const int64_t n_el = static_cast<int64_t>(rg1 - rg0) * kRowGroup * mt;
+    const int64_t set = static_cast<int64_t>(call & 1u) * p.peer_world;
+    const uint2 *own = static_cast<const uint2 *>(p.peer[p.peer_rank]);
+    for (int64_t i = tid; i < n_el; i += nthr) {
+        const int tok = static_cast<int>(i % mt);
+        const int64_t rr = static_cast<int64_t>(rg0) * kRowGroup + i / mt;
+        if (rr >= p.N) continue;
+        const int yr = p.jobs[0].yrow[tok];
+        const int64_t e = static_cast<int64_t>(yr) * p.ldy + rr;
+        float acc = 0.f;
+        for (int d = 0; d < p.peer_world; ++d) {
+            const uint2 *w = own + (set + d) * p.peer_cap + e;
+            uint2 v;
+            asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(w) : "memory");
+            if (v.y != call) {
+                const uint64_t t0 = global_timer_ns();
+                for (int it = 0; v.y != call; ++it) {
+                    if ((it & 255) == 255 && global_timer_ns() - t0 > p.peer_wait_ns) {
+                        atomicOr(p.err, 16);
+                        break;
+                    }
+                    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(w) : "memory");
+                }
+            }
+            const float x = __uint_as_float(v.x);
+            acc = d == 0 ? x : acc + x;
+        }
+        if (p.y) reinterpret_cast<float *>(p.y)[e] = acc;
+        if (p.y_bf16) reinterpret_cast<__nv_bfloat16 *>(p.y_bf16)[e] = __float2bfloat16_rn(acc);
     }
 }
 
@@ -224,6 +266,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     pdl_wait_prerequisites();                         // x / outputs / scratch may belong to the previous kernel
     const bool tr = trace && threadIdx.x == 0;
     if (tr) trace[2] = global_timer_ns();
+    uint32_t call = 0;                                // kEpiPeer: this CTA's all-reduce call number
+    if constexpr (EPI == kEpiPeer) call = *reinterpret_cast<volatile uint32_t *>(p.peer_calls + cta) + 1u;
 
     int j = lo / per_job;
     int g = (lo - j * per_job) / p.chunks;
@@ -299,10 +343,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             if (split) {
-                store_pair<EPI>(p, g, s, r, yr[nt][0], acc[nt][0] + acc[nt][1], acc[nt][2] + acc[nt][3]);
+                store_pair<EPI>(p, g, s, r, yr[nt][0], acc[nt][0] + acc[nt][1], acc[nt][2] + acc[nt][3], call);
             } else {
 #pragma unroll
-                for (int h = 0; h < 2; ++h) store_pair<EPI>(p, g, s, r, yr[nt][h], acc[nt][h], acc[nt][2 + h]);
+                for (int h = 0; h < 2; ++h) store_pair<EPI>(p, g, s, r, yr[nt][h], acc[nt][h], acc[nt][2 + h], call);
             }
         }
     };
@@ -449,6 +493,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     }
     if (tr) trace[5] = global_timer_ns();
     if (seg < hi) flush(seg, hi);
+    if constexpr (EPI == kEpiPeer) {
+        __threadfence();                               // this CTA's own words, before other threads read them
+        named_bar_sync(1, kConsumers * 32);
+        peer_receive(p, lo, hi, call, threadIdx.x, kConsumers * 32);
+        named_bar_sync(1, kConsumers * 32);
+        if (threadIdx.x == 0) *reinterpret_cast<volatile uint32_t *>(p.peer_calls + cta) = call;
+    }
     if (tr) {
         trace[6] = global_timer_ns();
         trace[7] = waited;

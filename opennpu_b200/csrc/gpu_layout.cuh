@@ -82,7 +82,9 @@ enum GemvEpilogue : int {
     kEpiBF16 = 1,     // y[yrow][n] = bf16(acc)
     kEpiSwiGLU = 2,   // strip rows 0-7 gate, 8-15 up: y[yrow][i] = bf16(silu(gate_i) * up_i) (fp32 with yf32)
     kEpiPairSum = 3,  // strip rows 0-7 a row, 8-15 its residual: y[yrow][i] = row_i + residual_i (fp32)
-    kEpiPeer = 4,     // fp32 y[yrow][n] sent to every rank's all-reduce buffer (8-byte {value, call} words)
+    kEpiPeer = 4,     // row-parallel projection + all-reduce: each finished output goes to every rank's
+                      // buffer as an 8-byte {value, call} word; after its range, a CTA waits for every
+                      // rank's words of the rows it finished and writes their sum (fp32 y, bf16 y_bf16)
 };
 
 // GEMV tracing: per CTA, ns stamps of kernel entry, producer's first copy issued, consumers past
@@ -91,6 +93,7 @@ enum GemvEpilogue : int {
 constexpr int kGemvTrace = 8;
 
 constexpr int kPeerMaxRanks = 8;       // ranks of the peer-memory all-reduce (comm.cu)
+constexpr int kPeerCtaCounters = 1024; // call counters of the GEMV CTAs that sum rows (kEpiPeer)
 
 struct GemvParams {
     const GemvJob *jobs;
@@ -127,11 +130,14 @@ struct GemvParams {
     const float *xf;                   // xsplit: fp32 activations, row stride ldx (elements)
     int yf32;                          // kEpiSwiGLU: fp32 outputs instead of bf16
     // kEpiPeer: every output value goes, with the all-reduce call number, into slot [parity][rank]
-    // of each rank's buffer (comm.cu layout); the call number is the buffer's counter + 1
+    // of each rank's buffer (comm.cu layout); CTA i's call number is peer_calls[i] + 1 (one counter
+    // per CTA in this rank's buffer, advanced by the CTA when its rows are summed)
     void *peer[kPeerMaxRanks];
     int peer_rank, peer_world;
     int64_t peer_cap;
-    const uint32_t *peer_calls;
+    uint32_t *peer_calls;
+    void *y_bf16;                      // kEpiPeer: the summed rows also as bf16 (may be null)
+    uint64_t peer_wait_ns;             // kEpiPeer: how long a CTA waits for a peer rank's words
 };
 
 // One link of a GEMV chain: y = x . W^T for m consecutive activation rows, run inside one

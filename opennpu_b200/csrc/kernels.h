@@ -76,17 +76,19 @@ struct PeerOut {
     void *bufs[kCommMaxRanks];
     int rank, world;
     int64_t cap;
+    void *y_bf16 = nullptr;    // the summed rows also as bf16
 };
 // the receive half of comm_allreduce_launch: wait for every rank's words of this call (the senders
 // were the GEMV's kEpiPeer epilogues) and add them in rank order into dst / dst_bf16
 cudaError_t comm_reduce_launch(void *const *bufs, int rank, int world, int64_t cap, float *dst, void *dst_bf16,
-                               int64_t n, int *err, cudaStream_t stream);
+                               int64_t n, int *err, uint64_t wait_ns, cudaStream_t stream);
 // bytes of one rank's buffer: two slot sets of world x cap 8-byte words, per-CTA call counters
+// (the comm kernel's kCommCtas, then kPeerCtaCounters of the GEMV CTAs that sum rows)
 int64_t comm_buffer_bytes(int world, int64_t cap);
 // bufs[r]: rank r's buffer as mapped in this process (own at [rank]); dst (fp32) and / or dst_bf16
 // = the sum over ranks of src, added in rank order
 cudaError_t comm_allreduce_launch(void *const *bufs, int rank, int world, int64_t cap, const float *src, float *dst,
-                                  void *dst_bf16, int64_t n, int *err, cudaStream_t stream);
+                                  void *dst_bf16, int64_t n, int *err, uint64_t wait_ns, cudaStream_t stream);
 
 // ---- MoE router (router.cu): softmax(h . Wr^T) -> top-k -> renormalise, one CTA per token
 constexpr int kMaxRouteExperts = 256;

@@ -127,6 +127,7 @@ struct Ctx {
     int64_t ts_cap = 0;
     int64_t calls = 0;
     double wait_s = 0;
+    uint64_t peer_wait_ns = 2000000000ull;   // bounded waits on other ranks' words (onpu_comm_set_wait)
     unsigned long long *gemv_trace = nullptr;   // onpu_gemv_trace: stamps of later GEMV launches
     int64_t gemv_trace_ctas = 0;
 };
@@ -323,8 +324,15 @@ int run_gemv(Ctx &c, const GpuMat &m, const GemvJob *d_jobs, int njobs, int mmax
         p.peer_rank = peer->rank;
         p.peer_world = peer->world;
         p.peer_cap = peer->cap;
-        p.peer_calls = reinterpret_cast<const uint32_t *>(static_cast<const uint2 *>(peer->bufs[peer->rank]) +
-                                                          2 * static_cast<int64_t>(peer->world) * peer->cap);
+        p.peer_calls = reinterpret_cast<uint32_t *>(static_cast<uint2 *>(peer->bufs[peer->rank]) +
+                                                    2 * static_cast<int64_t>(peer->world) * peer->cap) +
+                       kCommCtas;
+        p.y_bf16 = peer->y_bf16;
+        p.peer_wait_ns = c.peer_wait_ns;
+        if (W > kPeerCtaCounters) {
+            set_err("the all-reduce GEMV's %d CTAs exceed the communicator's %d call counters", W, kPeerCtaCounters);
+            return -1;
+        }
     }
     p.mul[0] = 1u << 28;
     p.mul[1] = 1u << 24;
@@ -2047,13 +2055,13 @@ int mv_allreduce_impl(const char *who, void *h, void *comm, const void *x, bool 
     po.world = cm->world;
     po.cap = cm->cap;
     auto s = static_cast<cudaStream_t>(stream);
+    po.y_bf16 = y_bf16;
     GemvOpts o;
     if (xf32) o.xf = static_cast<const float *>(x);
-    if (run_gemv(c, d->mat, js->d, js->n, js->mmax, kEpiPeer, xf32 ? nullptr : static_cast<const uint16_t *>(x), ldx,
-                 nullptr, d->mat.gm.N, s, pdl_enabled(), nullptr, &po, o))
-        return -1;
-    ONPU_CUDA(comm_reduce_launch(cm->bufs, cm->rank, cm->world, cm->cap, y, y_bf16, n, c.d_err, s), -1);
-    return 0;
+    // one launch: the epilogue sends each finished row to every rank, and each CTA then sums every
+    // rank's words of the rows it finished into y / y_bf16
+    return run_gemv(c, d->mat, js->d, js->n, js->mmax, kEpiPeer, xf32 ? nullptr : static_cast<const uint16_t *>(x),
+                    ldx, y, d->mat.gm.N, s, pdl_enabled(), nullptr, &po, o);
 }
 }  // namespace
 
@@ -2090,9 +2098,21 @@ int onpu_comm_allreduce(void *comm, const float *src, float *dst, void *dst_bf16
             return -1;
         }
     Ctx &c = ctx();
-    ONPU_CUDA(comm_allreduce_launch(h->bufs, h->rank, h->world, h->cap, src, dst, dst_bf16, n, c.d_err,
+    ONPU_CUDA(comm_allreduce_launch(h->bufs, h->rank, h->world, h->cap, src, dst, dst_bf16, n, c.d_err, c.peer_wait_ns,
                                     static_cast<cudaStream_t>(stream)),
               -1);
+    return 0;
+}
+
+int onpu_comm_set_wait(double seconds) {
+    clear_err();
+    if (!(seconds > 0.0) || seconds > 60.0) {
+        set_err("onpu_comm_set_wait: the limit must be in (0, 60] seconds");
+        return -1;
+    }
+    Ctx &c = ctx();
+    std::lock_guard<std::mutex> lk(g_mu);
+    c.peer_wait_ns = static_cast<uint64_t>(seconds * 1e9);
     return 0;
 }
 

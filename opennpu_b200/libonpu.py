@@ -89,6 +89,7 @@ SIGNATURES = {
     "onpu_comm_open": (I32, [P, P]),
     "onpu_comm_allreduce": (I32, [P, P, P, P, I64, P]),
     "onpu_comm_free": (None, [P]),
+    "onpu_comm_set_wait": (I32, [C.c_double]),
     "onpu_dense_mv_allreduce_dev": (I32, [P, P, P, I64, I64, P, P, P]),
     "onpu_dense_mv_allreduce_f32_dev": (I32, [P, P, P, I64, I64, P, P, P]),
     "onpu_chain_new": (P, []),

@@ -89,12 +89,14 @@ class TPDecoderLayer:
 
     def __init__(self, qkv, o, gu, dn, nq, group=None, allreduce=None):
         """qkv / gu: this rank's stacked row blocks (q|k|v, gate|up); o / dn: its K blocks; each an
-        (int4 codes, fp16 scales) pair. nq: this rank's q rows (= o's K block). allreduce: see
-        TPLinear."""
+        (int4 codes, fp16 scales) pair. nq: this rank's q rows (= o's K block). allreduce: None
+        (NCCL), or a pair of comm.PeerAllReduce, one for o and one for down (a communicator serves
+        one call site: the fused GEMV's CTAs sum rows fixed by the shape)."""
+        ar_o, ar_dn = allreduce if allreduce is not None else (None, None)
         self.qkv = TPLinear(*qkv, "column", group=group)
-        self.o = TPLinear(*o, "row", group=group, allreduce=allreduce)
+        self.o = TPLinear(*o, "row", group=group, allreduce=ar_o)
         self.gu = TPLinear(*gu, "column", gateup=True, group=group)
-        self.dn = TPLinear(*dn, "row", group=group, allreduce=allreduce)
+        self.dn = TPLinear(*dn, "row", group=group, allreduce=ar_dn)
         self.nq = nq
         assert self.o.K == nq
         self.f32_rows = min(p.m.max_f32_rows() for p in (self.qkv, self.o, self.gu, self.dn))

@@ -20,7 +20,7 @@ def _reference_line(config):
     return json.loads(r.stdout.strip().splitlines()[-1])
 
 
-@pytest.mark.parametrize("config,unit", [("attn", "GB/s"), ("gemv", "GB/s")])
+@pytest.mark.parametrize("config,unit", [("attn", "GB/s"), ("gemv", "GB/s"), ("qwen2.5-32b", "tokens/s")])
 def test_reference_arm_prints_one_contract_line(config, unit):
     d = _reference_line(config)
     assert d["impl"] == "reference" and d["unit"] == unit and d["value"] > 0
@@ -28,6 +28,11 @@ def test_reference_arm_prints_one_contract_line(config, unit):
         assert key in d, key
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["cpu_baseline"]["value"] == d["value"] and d["cpu_baseline"]["cores"] >= 1
+    if config == "qwen2.5-32b":            # the default config: the same config dict as our arm's line
+        sys.path.insert(0, str(ROOT))
+        import bench
+        assert d["config"] == bench.tp_config(1, 64, 1) and d["scaling"] == "strong"
     if config == "attn":
         assert d["config"]["context"] == 4096
         assert d["cpu_baseline"]["kind"] == ("reference" if O.ref_lib() is not None else "port")
+

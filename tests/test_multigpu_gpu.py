@@ -1,7 +1,8 @@
 """Two ranks on two GPUs (skipped with fewer): the peer-memory all-reduce against the exact sums
 (direct calls, calls alternating buffers, a CUDA-graph replay), the tensor-parallel decoder layer
-with that all-reduce, and the expert-parallel MoE layer (NCCL all-gather + reduce-scatter)
-against the single-GPU layer. NVLS is off in NCCL; the peer kernel uses plain peer stores."""
+with the row-parallel GEMVs fused with that all-reduce (one communicator per call site), and the
+expert-parallel MoE layer (NCCL all-gather + reduce-scatter) against the single-GPU layer. NVLS is
+off in NCCL; the peer kernels use plain peer stores."""
 import os
 import socket
 
@@ -102,14 +103,18 @@ def _tp_main(rank, world, port, q):
         from opennpu_b200.comm import PeerAllReduce
         from tests.test_tp_gpu import HIDDEN, _weights
         from oracle import oracle as O
-        ar = PeerAllReduce(cap_floats=4 * HIDDEN)
+        ars = (PeerAllReduce(cap_floats=4 * HIDDEN), PeerAllReduce(cap_floats=4 * HIDDEN))   # o, down
         w = _weights(seed=30)
-        x = torch.from_numpy(O.gen_x(3, HIDDEN, seed=31)).to(torch.bfloat16).cuda()
-        lay = tp.TPDecoderLayer.from_full(w, rank, world, allreduce=ar)
-        y = lay(x, lay.buffers(3)).cpu().numpy()
+        x = torch.from_numpy(O.gen_x(3, HIDDEN, seed=31)).cuda()
+        lay = tp.TPDecoderLayer.from_full(w, rank, world, allreduce=ars)
+        b = lay.buffers(3)
+        ys = [lay(x, b).cpu().numpy() for _ in range(3)]          # both slot sets, then the first again
         torch.distributed.barrier()
-        ar.close()
+        for ar in ars:
+            ar.close()
         torch.distributed.barrier()
+        assert all(np.array_equal(ys[0], yy) for yy in ys)
+        y = ys[0]
         q.put((rank, y))
     finally:
         torch.distributed.destroy_process_group()
