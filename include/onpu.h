@@ -138,6 +138,30 @@ int onpu_check_device(void);
 void *onpu_dense_new_int4(int64_t N, int64_t K, int gateup);
 /* Fill from host (on_device = 0) or device (on_device = 1) arrays; 0 ok, < 0 error. */
 int onpu_dense_load_int4(void *h, const uint8_t *qk, const uint16_t *scales, int on_device, void *stream);
+/* GGUF weights as they lie in a llama.cpp checkpoint (ggml type ids): rows of blocks, row stride
+ * K/32 * 18 bytes (Q4_0) or K/256 * 144 bytes (Q4_K).
+ * Q4_0: blocks of 32 = fp16 d + 16 bytes (element j in the low nibble of byte j, j + 16 in the
+ *   high one), w = (q - 8) d: the BASELINE int4 + fp16 format, ingested exactly (ONPU_FMT_Q4F16),
+ *   no requantisation (the reference dequantises and requantises every non-Q4_K type,
+ *   llama/ggml-opennpu/ggml-opennpu.cpp:183-207).
+ * Q4_K: super-blocks of 256 = fp16 d, fp16 dmin, 12 bytes of 6-bit scales / mins, 128 bytes of
+ *   codes; transcoded into q4nx (ONPU_FMT_Q4NX) as the reference's q4k_codes does
+ *   (ggml-opennpu.cpp:100-143): the codes exactly, each 32-group's scale d * sc and min -dmin * m
+ *   as the bf16 pair among their 3 x 3 bf16 neighbours closest (least squares) to the exact
+ *   weights. The transcode runs on the GPU. */
+#define ONPU_GGML_Q4_0 2
+#define ONPU_GGML_Q4_K 12
+/* GGUF rows (device) -> codes q [rows][K] (0..15), 16-bit scales [rows][K/32] (fp16 bits for Q4_0,
+ * bf16 for Q4_K) and, for Q4_K, bf16 mins [rows][K/32] (device). Asynchronous. 0 ok, < 0 error. */
+int onpu_gguf_codes_dev(int type, const void *src, int64_t rows, int64_t K, uint8_t *q, uint16_t *scales,
+                        uint16_t *mins, void *stream);
+/* A dense [N, K] handle from N GGUF rows on the host (on_device = 0) or device (1); gateup as in
+ * onpu_dense_new_int4. Synchronous; NULL on error. */
+void *onpu_dense_new_gguf(int64_t N, int64_t K, int type, const void *data, int on_device, int gateup, void *stream);
+/* An expert bank [E][N, K] from E x N GGUF rows (a ggml [K, N, E] expert tensor), as
+ * onpu_bank_new_int4 for int4. Synchronous; NULL on error. */
+void *onpu_bank_new_gguf(int64_t N, int64_t K, int64_t E, int type, const void *data, int on_device, int gateup,
+                         void *stream);
 /* The load-time search quantisers on the GPU: W fp32 [N][ldw] (device, 16-byte
  * aligned, ldw % 4 == 0, K % 32 == 0) -> codes q [N][K] (0..15), 16-bit (bf16) scales [N][K/32] and,
  * for q4nx (sym = 0), mins [N][K/32]; bit-exact with onpu_pack's quantisers
@@ -310,6 +334,42 @@ int onpu_dense_mv_dev_noalloc(void *h, const void *x, int64_t ldx, int64_t rows,
 /* GPU layout -> plain codes q[N][K] (0..15), scales[N][K/32] (and mins for q4nx), device pointers;
  * for bit-exact verification. */
 int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins, void *stream);
+
+/* ---- the ggml-opennpu backend's operator layer (llama/ggml-opennpu/ggml-opennpu.cpp:270-539,
+ * 703-753) over this library: which MUL_MAT / MUL_MAT_ID nodes it takes, their tensor layouts,
+ * and the learned sibling fusion. Tensors are described by the ggml_tensor fields the layer
+ * reads; the ggml_backend_* registration around it needs llama.cpp's headers. */
+typedef struct onpu_ggml_tensor {
+    int32_t type;            /* ggml type id: F32 0, F16 1, Q4_0 2, Q4_K 12, I32 26, BF16 30 */
+    int32_t weights;         /* non-zero: the tensor lives in a weights buffer */
+    int64_t ne[4];           /* elements per dimension, innermost first (ggml ne) */
+    int64_t nb[4];           /* byte strides per dimension (ggml nb) */
+    void *data;              /* host memory */
+    const char *name;        /* "blk.<i>.<what>.weight" for weights (sibling fusion groups by block) */
+} onpu_ggml_tensor;
+#define ONPU_GGML_OP_VIEW 0        /* NONE / RESHAPE / VIEW / PERMUTE / TRANSPOSE: no work */
+#define ONPU_GGML_OP_MUL_MAT 1     /* dst[N, M...] = w[K, N] x[K, M...]                      */
+#define ONPU_GGML_OP_MUL_MAT_ID 2  /* dst[N, n_used, T] = w[K, N, E] experts ids[n_used, T] of x[K, n_used|1, T] */
+/* 1 when the node runs here (opennpu_supports): MUL_MAT of a contiguous weight (F32, F16, BF16,
+ * Q4_0, Q4_K; K % 32 == 0, Q4_K K % 256 == 0) with ne2 == ne3 == 1 over F32 rows, not a Hadamard
+ * hint, N x K >= OPENNPU_MIN_PARAMS (default 2^20); MUL_MAT_ID of Q4_0 / Q4_K experts with I32 ids
+ * and N x K >= 2^17; view ops; never a weight named by an OPENNPU_CPU_TENSORS prefix. */
+int onpu_ggml_supports(int op, const onpu_ggml_tensor *dst, const onpu_ggml_tensor *w, const onpu_ggml_tensor *x,
+                       const onpu_ggml_tensor *ids, int hadamard_hint);
+void *onpu_ggml_new(void);
+/* Record a node before any runs (the backend's supports_op sees every node while llama.cpp
+ * reserves its graphs): weights reading the same input, in the same block and with the same K,
+ * become one fused group (at most 4) on the first compute; OPENNPU_FUSE=0 turns fusion off. */
+void onpu_ggml_note(void *ctx, int op, const onpu_ggml_tensor *w, const onpu_ggml_tensor *x,
+                    const onpu_ggml_tensor *ids);
+/* Run a node, writing dst (host). A fused group's first member computes every member; the others
+ * copy their waiting slice when their input (pointer and contents) and ids are unchanged. Weights
+ * become GPU handles on first use. 0 ok, < 0 error (onpu_last_error). */
+int onpu_ggml_compute(void *ctx, int op, const onpu_ggml_tensor *dst, const onpu_ggml_tensor *w,
+                      const onpu_ggml_tensor *x, const onpu_ggml_tensor *ids);
+/* fused slices used, fused slices discarded, groups, weight handles */
+void onpu_ggml_stats(void *ctx, int64_t *out4);
+void onpu_ggml_free(void *ctx);
 
 /* onpu_attn_step on device pointers (a KV cache resident in HBM), asynchronous on `stream`:
  * kv_bf16 selects a bf16 cache. K, V 16-byte aligned with hs and rs multiples of 16 bytes.

@@ -123,6 +123,14 @@ cudaError_t route_launch(const uint16_t *h, int64_t ldh, int64_t T, const uint16
                          const ExpertJobsParams *jobs = nullptr);
 int64_t route_counter_slots(int64_t T);
 
+// ---- GGUF block formats (gguf.cu): ggml rows of Q4_0 / Q4_K blocks -> plain codes q [rows][K]
+// (0..15), 16-bit scales [rows][K/32] (fp16 for Q4_0, bf16 for Q4_K) and bf16 mins (Q4_K)
+constexpr int kGgmlQ4_0 = 2;
+constexpr int kGgmlQ4_K = 12;
+int64_t gguf_row_bytes(int type, int64_t K);                // -1: type or K not supported
+cudaError_t gguf_codes_launch(int type, const uint8_t *src, int64_t rows, int64_t K, uint8_t *q, uint16_t *scales,
+                              uint16_t *mins, cudaStream_t stream);
+
 // ---- layout conversion (repack.cu)
 // Where the codes of the matrix come from.
 enum RepackSource : int {

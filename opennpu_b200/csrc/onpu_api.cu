@@ -741,8 +741,22 @@ void onpu_dense_mv(void *h, const float *x, int64_t rows, float *y) {
     const int64_t K = d->mat.gm.K, N = d->mat.gm.N;
     const int64_t Kin = d->geo.ok ? d->geo.K : K;
     JobSet *js = dense_jobs(d, rows);
-    if (!js || !stage_x(c, x, rows, Kin, K) || !grow(c.d_y, c.y_cap, rows * N)) return;
-    if (run_gemv(c, d->mat, js->d, js->n, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
+    if (!js || !grow(c.d_y, c.y_cap, rows * N)) return;
+    // up to 8 rows whose fp32 values fit in shared memory: staged exactly (two fp16 halves per
+    // value); otherwise rounded to bf16, as the reference's device path rounds its inputs
+    const bool exact = Kin == K && rows <= 8 && plan_gemv(c, d->mat.gm, 1, 2 * static_cast<int>(rows), false).lay.xres;
+    if (exact) {
+        if (!grow(c.d_in, c.in_cap, rows * K)) return;
+        ONPU_CUDA(cudaMemcpyAsync(c.d_in, x, sizeof(float) * rows * K, cudaMemcpyHostToDevice, c.stream), );
+        GemvOpts o;
+        o.xf = c.d_in;
+        if (run_gemv(c, d->mat, js->d, js->n, js->mmax, kEpiF32, nullptr, K, c.d_y, N, c.stream, false, nullptr,
+                     nullptr, o))
+            return;
+    } else {
+        if (!stage_x(c, x, rows, Kin, K)) return;
+        if (run_gemv(c, d->mat, js->d, js->n, js->mmax, kEpiF32, c.d_x, K, c.d_y, N, c.stream, false)) return;
+    }
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * rows * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
 }
@@ -784,12 +798,23 @@ void onpu_bank_run(void *h, const float *x, int x_per_slot, int64_t T, const int
     std::lock_guard<std::mutex> lk(g_mu);
     const int64_t N = b->geo.N, Kp = b->mat.gm.K;
     const int64_t xrows = x_per_slot ? T * k : T;
-    if (!stage_x(c, x, xrows, b->geo.K, Kp)) return;
     std::vector<GemvJob> jobs;
     int mm = 1;
-    build_expert_jobs(b->mat, ids, T, k, x_per_slot != 0, false, jobs, mm);
+    // fp32 inputs staged exactly (two fp16 halves, jobs of 8) when those rows fit in shared
+    // memory; otherwise rounded to bf16 (the reference's device rounding)
+    const bool exact = b->geo.K == Kp && gemv_resident(16, Kp);
+    if (exact) {
+        if (!grow(c.d_in, c.in_cap, xrows * Kp)) return;
+        ONPU_CUDA(cudaMemcpyAsync(c.d_in, x, sizeof(float) * xrows * Kp, cudaMemcpyHostToDevice, c.stream), );
+    } else if (!stage_x(c, x, xrows, b->geo.K, Kp)) {
+        return;
+    }
+    build_expert_jobs(b->mat, ids, T, k, x_per_slot != 0, false, jobs, mm, exact ? 8 : kMaxTokensPerJob);
     if (!upload_jobs(c, jobs) || !grow(c.d_y, c.y_cap, T * k * N)) return;
-    if (run_gemv(c, b->mat, c.d_jobs, static_cast<int>(jobs.size()), mm, kEpiF32, c.d_x, Kp, c.d_y, N, c.stream, false))
+    GemvOpts o;
+    if (exact) o.xf = c.d_in;
+    if (run_gemv(c, b->mat, c.d_jobs, static_cast<int>(jobs.size()), mm, kEpiF32, exact ? nullptr : c.d_x, Kp, c.d_y, N,
+                 c.stream, false, nullptr, nullptr, o))
         return;
     ONPU_CUDA(cudaMemcpyAsync(y, c.d_y, sizeof(float) * T * k * N, cudaMemcpyDeviceToHost, c.stream), );
     finish(c);
@@ -941,6 +966,150 @@ void *onpu_dense_new_int4(int64_t N, int64_t K, int gateup) {
         return nullptr;
     }
     return d;
+}
+
+}  // extern "C"
+
+namespace {
+// E matrices of GGUF rows (device bytes, E * N rows of row_bytes) -> the GPU layout of m (one
+// matrix after the other): codes, scales and mins on the device, then the codes repack. Caller
+// holds g_mu.
+bool gguf_to_mat(GpuMat &m, int type, const uint8_t *d_src, int64_t N, int64_t K, int64_t E, cudaStream_t s,
+                 const char *who) {
+    const int64_t rb = gguf_row_bytes(type, K);
+    uint8_t *q = nullptr;
+    uint16_t *sc = nullptr, *mn = nullptr;
+    const size_t nq = static_cast<size_t>(N * K), ns = static_cast<size_t>(N * (K / 32));
+    cudaError_t e = cudaMalloc(&q, nq);
+    if (e == cudaSuccess) e = cudaMalloc(&sc, ns * 2);
+    if (e == cudaSuccess) e = cudaMalloc(&mn, ns * 2);
+    for (int64_t x = 0; x < E && e == cudaSuccess; ++x) {
+        e = gguf_codes_launch(type, d_src + x * N * rb, N, K, q, sc, mn, s);
+        RepackParams p{};
+        p.src_kind = kSrcCodes;
+        p.src = q;
+        p.scales = sc;
+        p.mins = type == kGgmlQ4_K ? mn : nullptr;
+        p.src_row = m.d_row_map;
+        p.N = N;
+        p.K = K;
+        p.fmt = m.gm.fmt;
+        p.dst = m.d_w + x * m.gm.bytes;
+        if (e == cudaSuccess) e = repack_launch(p, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);     // q / sc / mn are reused
+    }
+    cudaFree(q);
+    cudaFree(sc);
+    cudaFree(mn);
+    if (e != cudaSuccess) {
+        set_err("%s: %s", who, cudaGetErrorString(e));
+        return false;
+    }
+    return true;
+}
+
+// GGUF bytes of E matrices on the device (a copy when they are on the host); nullptr on error
+const uint8_t *gguf_device_bytes(const void *data, int on_device, int64_t bytes, uint8_t *&owned, cudaStream_t s,
+                                 const char *who) {
+    owned = nullptr;
+    if (on_device) return static_cast<const uint8_t *>(data);
+    cudaError_t e = cudaMalloc(&owned, static_cast<size_t>(bytes));
+    if (e == cudaSuccess) e = cudaMemcpyAsync(owned, data, static_cast<size_t>(bytes), cudaMemcpyHostToDevice, s);
+    if (e != cudaSuccess) {
+        set_err("%s: %s", who, cudaGetErrorString(e));
+        cudaFree(owned);
+        owned = nullptr;
+        return nullptr;
+    }
+    return owned;
+}
+}  // namespace
+
+extern "C" {
+
+int onpu_gguf_codes_dev(int type, const void *src, int64_t rows, int64_t K, uint8_t *q, uint16_t *scales,
+                        uint16_t *mins, void *stream) {
+    clear_err();
+    if (gguf_row_bytes(type, K) < 0 || rows <= 0 || (type == kGgmlQ4_K && !mins)) {
+        set_err("onpu_gguf_codes_dev: type %d with K = %lld is not a supported GGUF layout (Q4_0: K %% 32 == 0, "
+                "Q4_K: K %% 256 == 0 and a mins output)", type, static_cast<long long>(K));
+        return -1;
+    }
+    ONPU_CUDA(gguf_codes_launch(type, static_cast<const uint8_t *>(src), rows, K, q, scales, mins,
+                                static_cast<cudaStream_t>(stream)),
+              -1);
+    return 0;
+}
+
+void *onpu_dense_new_gguf(int64_t N, int64_t K, int type, const void *data, int on_device, int gateup, void *stream) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    const int64_t rb = gguf_row_bytes(type, K);
+    if (N <= 0 || rb < 0 || !data) {
+        set_err("onpu_dense_new_gguf: type %d with K = %lld is not a supported GGUF layout (Q4_0: K %% 32 == 0, "
+                "Q4_K: K %% 256 == 0)", type, static_cast<long long>(K));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    auto *d = new DenseH;
+    d->fmt = type == kGgmlQ4_K ? kFmtQ4NX : kFmtQ4F16;
+    d->gateup = gateup != 0;
+    uint8_t *owned = nullptr;
+    bool ok = alloc_mat(d->mat, N, K, d->fmt, 1);
+    if (ok && d->gateup && !set_gateup_interleave(d->mat)) {
+        set_err("onpu_dense_new_gguf: gate/up matrix needs N/2 %% 8 == 0");
+        ok = false;
+    }
+    const uint8_t *src = ok ? gguf_device_bytes(data, on_device, N * rb, owned, s, "onpu_dense_new_gguf") : nullptr;
+    ok = ok && src && gguf_to_mat(d->mat, type, src, N, K, 1, s, "onpu_dense_new_gguf");
+    cudaFree(owned);
+    if (!ok) {
+        delete d;
+        return nullptr;
+    }
+    return d;
+}
+
+void *onpu_bank_new_gguf(int64_t N, int64_t K, int64_t E, int type, const void *data, int on_device, int gateup,
+                         void *stream) {
+    clear_err();
+    Ctx &c = ctx();
+    if (!c.ok) {
+        set_err("no usable CUDA device");
+        return nullptr;
+    }
+    const int64_t rb = gguf_row_bytes(type, K);
+    if (N <= 0 || E <= 0 || rb < 0 || !data) {
+        set_err("onpu_bank_new_gguf: type %d with K = %lld is not a supported GGUF layout (Q4_0: K %% 32 == 0, "
+                "Q4_K: K %% 256 == 0)", type, static_cast<long long>(K));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lk(g_mu);
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : c.stream;
+    auto *b = new BankH;
+    b->fmt = type == kGgmlQ4_K ? kFmtQ4NX : kFmtQ4F16;
+    b->owns_buf = false;
+    b->geo.N = N;                 // no stream-order geometry: the weights arrive as GGUF blocks
+    b->geo.K = K;
+    uint8_t *owned = nullptr;
+    bool ok = alloc_mat(b->mat, N, K, b->fmt, E);
+    if (ok && gateup && !set_gateup_interleave(b->mat)) {
+        set_err("onpu_bank_new_gguf: gate/up rows need N %% 2 == 0 and N/2 %% 8 == 0");
+        ok = false;
+    }
+    const uint8_t *src = ok ? gguf_device_bytes(data, on_device, E * N * rb, owned, s, "onpu_bank_new_gguf") : nullptr;
+    ok = ok && src && gguf_to_mat(b->mat, type, src, N, K, E, s, "onpu_bank_new_gguf");
+    cudaFree(owned);
+    if (!ok) {
+        delete b;
+        return nullptr;
+    }
+    return b;
 }
 
 int onpu_quantize_dev(const float *W, int64_t ldw, int64_t N, int64_t K, int sym, uint8_t *q, uint16_t *scales,

@@ -63,6 +63,15 @@ SIGNATURES = {
     "onpu_dense_new_f32_dev": (P, [P, I64, I64, I64, I32, I32, P]),
     "onpu_dense_new_residual_f32_dev": (P, [P, I64, I64, I64, I32, P]),
     "onpu_dense_prepare": (I32, [P, I64]),
+    "onpu_ggml_supports": (I32, [I32, P, P, P, P, I32]),
+    "onpu_ggml_new": (P, []),
+    "onpu_ggml_note": (None, [P, I32, P, P, P]),
+    "onpu_ggml_compute": (I32, [P, I32, P, P, P, P]),
+    "onpu_ggml_stats": (None, [P, I64P]),
+    "onpu_ggml_free": (None, [P]),
+    "onpu_gguf_codes_dev": (I32, [I32, P, I64, I64, P, P, P, P]),
+    "onpu_dense_new_gguf": (P, [I64, I64, I32, P, I32, I32, P]),
+    "onpu_bank_new_gguf": (P, [I64, I64, I64, I32, P, I32, I32, P]),
     "onpu_dense_mv_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_mv_f32_dev": (I32, [P, P, I64, I64, P, I64, I32, P]),
     "onpu_dense_max_f32_rows": (I32, [P]),
@@ -191,3 +200,13 @@ def fp(a):
 
 def i32p(a):
     return a.ctypes.data_as(I32P)
+
+
+class GgmlTensor(C.Structure):
+    """onpu_ggml_tensor: the ggml_tensor fields the ggml op layer reads (include/onpu.h)."""
+    _fields_ = [("type", C.c_int32), ("weights", C.c_int32), ("ne", C.c_int64 * 4), ("nb", C.c_int64 * 4),
+                ("data", C.c_void_p), ("name", C.c_char_p)]
+
+
+GGML_OP_VIEW, GGML_OP_MUL_MAT, GGML_OP_MUL_MAT_ID = 0, 1, 2
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q4_K, GGML_I32, GGML_BF16 = 0, 1, 2, 12, 26, 30

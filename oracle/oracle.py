@@ -16,6 +16,9 @@ packer). Reference lines followed (paths relative to the reference project root)
 - ``moe_ffn``          opennpu/native/reference.py:77-84 (per-expert SwiGLU, weighted sum)
 - ``moe_act/moe_sum``  llama/ggml-opennpu/onpu_cpu.cpp:233-274
 - ``attn_step``        llama/ggml-opennpu/onpu_cpu.cpp:173-218 (decode attention, GQA, mask, sinks)
+- ``q4k_transcode``    llama/ggml-opennpu/ggml-opennpu.cpp:100-143 (GGUF Q4_K -> q4nx codes, bf16 s / m)
+- ``q4_0_codes``       the GGUF Q4_0 block (the ggml format the reference reads through to_float,
+                       ggml-opennpu.cpp:77-86) unpacked: codes and fp16 scale
 
 Parity pin: tests/test_oracle.py checks these against the reference's own code — its Python
 imported in the container that generated tests/golden/*.npz (tests/golden/make_golden.py) and its
@@ -215,6 +218,91 @@ def moe_sum(o, ids, w, bias=None):
     if bias is not None:
         o = o + np.asarray(bias, np.float32)[ids.reshape(-1)].reshape(o.shape)
     return (o.reshape(T, k, -1) * w[:, :, None]).sum(1).astype(np.float32)
+
+
+# ------------------------------------------------------------------ GGUF blocks
+def q4_0_codes(blocks):
+    """GGUF Q4_0 blocks uint8 [nb, 18] -> codes uint8 [nb, 32] (w = (q - 8) * d) and the fp16 d bits
+    uint16 [nb]: byte j holds element j (low nibble) and element j + 16 (high nibble)."""
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 18)
+    d = b[:, :2].copy().view(np.uint16)[:, 0]
+    qs = b[:, 2:]
+    return np.concatenate([qs & 15, qs >> 4], axis=1).astype(np.uint8), d
+
+
+def q4k_scale_min(sc, sub):
+    """6-bit scale and min of sub-block `sub` (0..7) from the 12 packed bytes sc [..., 12]."""
+    sc = sc.astype(np.int32)
+    if sub < 4:
+        return sc[..., sub] & 63, sc[..., sub + 4] & 63
+    return ((sc[..., sub + 4] & 0xF) | ((sc[..., sub - 4] >> 6) << 4),
+            (sc[..., sub + 4] >> 4) | ((sc[..., sub] >> 6) << 4))
+
+
+def _bf_step(h, direction):
+    """The bf16 value next to h (bits, uint16 array) upwards (+1) or downwards (-1) in value; from
+    zero, the smallest subnormal of that sign (ggml-opennpu.cpp:106-110)."""
+    f = bf16_bits_to_f32(h)
+    step = np.where((f > 0) == (direction > 0), h.astype(np.int32) + 1, h.astype(np.int32) - 1)
+    zero = np.uint16(0x0001 if direction > 0 else 0x8001)
+    return np.where(f == 0, zero, step.astype(np.uint16)).astype(np.uint16)
+
+
+def q4k_transcode(blocks):
+    """GGUF Q4_K super-blocks uint8 [nb, 144] -> q4nx: codes uint8 [nb, 8, 32], bf16 scale and min
+    bits uint16 [nb, 8], as ggml-opennpu.cpp:114-143 (q4k_codes): the codes of sub-block b, exact
+    weights q * S + M with S = d * sc_b and M = -dmin * m_b (fp32), then among the 3 x 3 bf16 pairs
+    next to (bf16(S), bf16(M)) the first (in ds-major order) with the least fp32 sum of squared
+    errors, every float operation rounded separately in the reference's order."""
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 144)
+    nb = b.shape[0]
+    d = b[:, 0:2].copy().view(np.float16)[:, 0].astype(np.float32)
+    dmin = b[:, 2:4].copy().view(np.float16)[:, 0].astype(np.float32)
+    sc, qs = b[:, 4:16], b[:, 16:144]
+    q = np.empty((nb, 8, 32), np.uint8)
+    s_out = np.empty((nb, 8), np.uint16)
+    m_out = np.empty((nb, 8), np.uint16)
+    for sub in range(8):
+        sv, mv = q4k_scale_min(sc, sub)
+        qq = qs[:, (sub // 2) * 32:(sub // 2) * 32 + 32]
+        q[:, sub] = (qq >> 4) if sub & 1 else (qq & 15)
+        qf = q[:, sub].astype(np.float32)
+        S = (d * sv.astype(np.float32)).astype(np.float32)
+        M = ((-dmin) * mv.astype(np.float32)).astype(np.float32)
+        s0, m0 = f32_to_bf16_bits(S), f32_to_bf16_bits(M)
+        best = np.full(nb, np.inf, np.float32)
+        bs, bm = s0.copy(), m0.copy()
+        for ds in (-1, 0, 1):
+            for dm in (-1, 0, 1):
+                sc_ = _bf_step(s0, ds) if ds else s0
+                mn_ = _bf_step(m0, dm) if dm else m0
+                sf, mf = bf16_bits_to_f32(sc_), bf16_bits_to_f32(mn_)
+                e = np.zeros(nb, np.float32)
+                for l in range(32):
+                    x = ((qf[:, l] * sf) + mf) - ((qf[:, l] * S) + M)
+                    e = e + x * x
+                take = e < best
+                best = np.where(take, e, best)
+                bs = np.where(take, sc_, bs)
+                bm = np.where(take, mn_, bm)
+        s_out[:, sub], m_out[:, sub] = bs, bm
+    return q, s_out, m_out
+
+
+def q4k_exact(blocks):
+    """The exact fp32 weights of Q4_K super-blocks [nb, 144] -> [nb, 256]: q * (d * sc) - dmin * m."""
+    b = np.ascontiguousarray(blocks, np.uint8).reshape(-1, 144)
+    d = b[:, 0:2].copy().view(np.float16)[:, 0].astype(np.float32)
+    dmin = b[:, 2:4].copy().view(np.float16)[:, 0].astype(np.float32)
+    out = np.empty((b.shape[0], 8, 32), np.float32)
+    for sub in range(8):
+        sv, mv = q4k_scale_min(b[:, 4:16], sub)
+        qq = b[:, 16 + (sub // 2) * 32:16 + (sub // 2) * 32 + 32]
+        qf = ((qq >> 4) if sub & 1 else (qq & 15)).astype(np.float32)
+        S = (d * sv.astype(np.float32)).astype(np.float32)
+        dm = (dmin * mv.astype(np.float32)).astype(np.float32)
+        out[:, sub] = qf * S[:, None] - dm[:, None]
+    return out.reshape(-1, 256)
 
 
 # ------------------------------------------------------------------ the C restatement
