@@ -175,42 +175,43 @@ class PrefillStack:
     """Qwen3-14B MLP projections for M prefill tokens on the tensor cores (gate_up with
     the SwiGLU epilogue, then down), `layers` layers of synthetic int4 weights."""
 
-    def __init__(self, M, seed, layers=2):
-        from opennpu_b200 import dense
+    def __init__(self, M, seed, layers=2, rank=0, world=1, group=None):
+        """world > 1: tensor parallelism (tp.TPMLP): this rank's gate/up rows (column-parallel)
+        and down K block (row-parallel, NCCL all-reduce of the [M, hidden] output); every rank
+        generates only its own shards."""
+        from opennpu_b200 import dense, tp
         self.dense = dense
         gen = torch.Generator(device="cuda")
         gen.manual_seed(seed)
         self.layers = []
+        ir = P_INTER // world
         for _ in range(layers):
-            qk, s = gen_int4_cuda(2 * P_INTER, P_HIDDEN, gen)
-            gu = dense.DenseMatrix.from_int4(qk, s, gateup=True)
-            del qk, s
-            qk, s = gen_int4_cuda(P_HIDDEN, P_INTER, gen)
-            dn = dense.DenseMatrix.from_int4(qk, s)
-            del qk, s
-            self.layers.append((gu, dn))
+            gu = gen_int4_cuda(2 * ir, P_HIDDEN, gen)
+            dn = gen_int4_cuda(P_HIDDEN, ir, gen)
+            self.layers.append(tp.TPMLP(gu, dn, group=group))
+            del gu, dn
         torch.cuda.synchronize()
-        self.M = M
+        self.M, self.world = M, world
         self.x = torch.randn(M, P_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
-        self.a = torch.empty(M, P_INTER, device="cuda", dtype=torch.bfloat16)
+        self.a = torch.empty(M, ir, device="cuda", dtype=torch.bfloat16)
         self.y = torch.empty(M, P_HIDDEN, device="cuda")
+        # whole-model FLOPs (the same at every rank count: strong scaling)
         self.flops_gu = 2 * M * (2 * P_INTER) * P_HIDDEN
         self.flops_per_step = layers * (self.flops_gu + 2 * M * P_HIDDEN * P_INTER)
+        self.flops_gu_rank = self.flops_gu // world
         self.launches_per_step = 4 * layers            # activation copy + GEMM, per matrix
 
     def step(self):
-        d = self.dense
-        for gu, dn in self.layers:
-            gu.mm(self.x, out=self.a, epi=d.EPI_SWIGLU)
-            dn.mm(self.a, out=self.y)
+        for mlp in self.layers:
+            mlp(self.x, self.a, self.y)
 
     def dominant(self):
         d = self.dense
 
         def run():
-            for gu, _ in self.layers:
-                gu.mm(self.x, out=self.a, epi=d.EPI_SWIGLU)
-        return run, self.flops_gu, len(self.layers)
+            for mlp in self.layers:
+                mlp.gu.mm(self.x, self.a, epi=d.EPI_SWIGLU)
+        return run, self.flops_gu_rank, len(self.layers)
 
 
 _CPU_CACHE = {}
@@ -259,7 +260,8 @@ def run_prefill(args):
     rank, world, local = dist_setup(args.gpus)
     _, tflops_peak, peak_kind = peaks()
     M = args.m if args.m > 1 else 2048
-    work = PrefillStack(M, seed=2000 + rank, layers=2)
+    group = torch.distributed.group.WORLD if world > 1 else None
+    work = PrefillStack(M, seed=2000 + rank, layers=2, rank=rank, world=world, group=group)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(max(args.warmup, 1)):
@@ -295,7 +297,7 @@ def run_prefill(args):
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms = float(t.item())
     ms_step = ms / args.steps
-    tflops = work.flops_per_step * world / (ms_step * 1e-3) / 1e12
+    tflops = work.flops_per_step / (ms_step * 1e-3) / 1e12          # the whole model, over all ranks
 
     run_dom, dom_flops, dom_n = work.dominant()
     gdom = torch.cuda.CUDAGraph()
@@ -342,12 +344,13 @@ def run_prefill(args):
         line = {
             "metric": "int4 prefill dequant-GEMM TFLOP/s (Qwen3-14B MLP, tcgen05)", "value": round(tflops, 2),
             "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int4 weights dequantised to fp16, fp16 x fp16 -> fp32",
             "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1))",
             "config": {"workload": "qwen3-14b-prefill-mlp", "M": M, "layers": len(work.layers),
                        "matrices": "gate_up 34816x5120 + SwiGLU, down 5120x17408",
-                       "parallelism": f"replicas{world}", "l2": "weights larger than L2 (no flush needed)",
+                       "parallelism": f"tp{world}", "l2": "weights larger than L2 (no flush needed)",
+                       "collective": "NCCL all-reduce of the [M, 5120] fp32 output after down" if world > 1 else None,
                        "cuda_graph": True},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": tflops_peak, "unit": "TFLOP/s",
                          "frac": round(achieved / tflops_peak, 4), "peak_kind": peak_kind + " (bf16 dense, burst)",
@@ -519,7 +522,7 @@ class MoEStack:
     routed-expert FFN of every layer; each layer has its own weights and its own bf16 N(0,1)
     input rows, so the routing (and the experts read) differs per layer."""
 
-    def __init__(self, T, seed, layers=M_LAYERS, rank=0, world=1, group=None):
+    def __init__(self, T, seed, layers=M_LAYERS, rank=0, world=1, group=None, ep="gather"):
         """world > 1: expert parallelism, this rank holds experts [rank * E / world, ...) of every
         layer and its own T tokens (moe.EPMoELayer: all-gather of tokens and routing, reduce-scatter
         of the outputs). Router weights are the same on every rank."""
@@ -542,14 +545,17 @@ class MoEStack:
                   + 1e-4).half()
             ffn = moe.ExpertFFN(gq, gs, dq, ds)
             del gq, gs, dq, ds
-            ep = moe.EPMoELayer(wr, ffn, rank, world, M_E, group=group, k=M_K) if world > 1 else None
-            self.layers.append((wr, ffn, ep))
+            kind = moe.EPMoELayerA2A if ep == "a2a" else moe.EPMoELayer
+            ep_layer = kind(wr, ffn, rank, world, M_E, group=group, k=M_K) if world > 1 else None
+            self.layers.append((wr, ffn, ep_layer))
         torch.cuda.synchronize()
         self.x = torch.randn(layers, T, M_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
         self.ids = torch.empty(layers, T, M_K, dtype=torch.int32, device="cuda")
         self.w = torch.empty(layers, T, M_K, device="cuda")
         self.y = torch.empty(layers, T, M_HIDDEN, device="cuda")
-        self.bufs = [ep.buffers(T, M_HIDDEN) for _, _, ep in self.layers] if world > 1 else None
+        self.ep = ep
+        self.bufs = ([e.buffers(T, M_HIDDEN) for _, _, e in self.layers] if world > 1 and ep == "gather"
+                     else None)
         # router (+ job lists), gate_up, down, combine; with expert parallelism the job builder runs
         # separately (the ids are all-gathered first)
         self.launches_per_step = (4 if world == 1 else 5) * layers
@@ -560,7 +566,10 @@ class MoEStack:
         for l, (wr, ffn, ep) in enumerate(self.layers):
             x = self.x[l]
             if ep is not None:
-                self.y[l].copy_(ep(x, self.bufs[l], stream=stream))
+                if self.ep == "a2a":
+                    self.y[l].copy_(ep(x, stream=stream))
+                else:
+                    self.y[l].copy_(ep(x, self.bufs[l], stream=stream))
                 continue
             ffn.layer(x, wr, M_K, out=self.y[l], ids=self.ids[l], w=self.w[l], stream=stream)
 
@@ -630,7 +639,7 @@ def run_moe(args):
     T = args.m if args.m > 0 else 1
     layers = args.layers
     group = torch.distributed.group.WORLD if world > 1 else None
-    work = MoEStack(T, seed=3000, layers=layers, rank=rank, world=world, group=group)
+    work = MoEStack(T, seed=3000, layers=layers, rank=rank, world=world, group=group, ep=args.ep)
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(max(args.warmup, 1)):
@@ -638,13 +647,22 @@ def run_moe(args):
     s.synchronize()
     from opennpu_b200 import dense
     dense.check_device()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=s):
-        work.step(s)
-    torch.cuda.synchronize()
+    # the all-to-all form reads its split sizes on the host: it runs eagerly, not from a graph
+    graph = None
+    if not (world > 1 and args.ep == "a2a"):
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s):
+            work.step(s)
+        torch.cuda.synchronize()
+
+    def replay():
+        if graph is not None:
+            graph.replay()
+        else:
+            work.step(s)
     with torch.cuda.stream(s):
         for _ in range(args.warmup):
-            graph.replay()
+            replay()
     s.synchronize()
     if world > 1:
         torch.distributed.barrier()
@@ -655,7 +673,7 @@ def run_moe(args):
     e0.record(s)
     with torch.cuda.stream(s):
         for _ in range(args.steps):
-            graph.replay()
+            replay()
     e1.record(s)
     e1.synchronize()
     ms = e0.elapsed_time(e1)
@@ -705,15 +723,18 @@ def run_moe(args):
             "metric": "MoE layer tokens/s (Qwen3-30B-A3B: router + 128-expert top-8 int4 FFN)",
             "value": round(tok_s, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int4 weights, bf16 activations, fp32 accumulate",
+            "vs_baseline": None, "dtype": "int4 weights, bf16 inputs, fp32 activation between the projections, "
+                                          "fp32 accumulate",
             "data": "synthetic (seeded random int4 experts, fp16 scales, bf16 N(0,1) tokens, N(0,0.02) router)",
             "config": {"workload": "qwen3-30b-a3b-moe-layer", "T": T, "T_per_gpu": T, "layers": layers,
                        "experts": M_E, "top_k": M_K, "hidden": M_HIDDEN, "expert_inter": M_INTER,
                        "parallelism": f"ep{world}" if world > 1 else "single", "us_per_layer": round(layer_us, 3),
-                       "collective": "NCCL all-gather (tokens, ids, weights) + reduce-scatter (outputs)"
-                       if world > 1 else None,
+                       "collective": (("NCCL all-to-all dispatch of routed token rows (+ counts) and combine"
+                                       if args.ep == "a2a" else
+                                       "NCCL all-gather (tokens, ids, weights) + reduce-scatter (outputs)")
+                                      if world > 1 else None),
                        "l2": "selected experts of all layers per step exceed L2 (no flush needed)",
-                       "cuda_graph": True},
+                       "cuda_graph": graph is not None},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gbs / hbm, 4), "peak_kind": peak_kind + " (copy bandwidth)",
                          "traffic": None, "kernel": "whole MoE layer (router + job lists, gate_up + SwiGLU GEMV, "
@@ -1491,6 +1512,8 @@ def main():
                     help="tokens (M / T); spell it --rows under torchrun, which claims --m")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="qwen2.5-32b at N>1: the row-parallel all-reduce (peer-memory kernel or NCCL)")
+    ap.add_argument("--ep", default="gather", choices=["gather", "a2a"],
+                    help="moe at N>1: all-gather + reduce-scatter (graph-captured) or all-to-all dispatch/combine")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extra", action="store_true", help="qwen2.5-32b: skip the Qwen3-8B figures at N = 1")

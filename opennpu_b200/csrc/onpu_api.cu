@@ -243,6 +243,9 @@ struct GemvOpts {
     bool yf32 = false;            // kEpiSwiGLU: fp32 outputs
 };
 
+constexpr int kMaxCtasPerRowGroup = 4;
+constexpr int kCapBelowChunks = 16;     // ... when the CTAs would get fewer chunks than this
+
 // The resident activation layout of a launch of T chunks, and its CTA count: one resident wave,
 // trimmed to whole CTAs per row group (host-known job count). A one-job launch whose CTAs each
 // cover less than a row group stages only its own part of K (kwin) when that layout keeps the wave
@@ -259,6 +262,12 @@ GemvPlan plan_gemv(const Ctx &c, const GpuMatrix &gm, int njobs, int mrows, bool
     pl.lay = gemv_layout(gm.fmt, mrows, gm.K);
     int W = choose_workers(c, gm.fmt, pl.ntiles, T, pl.lay.smem);
     if (!device_count) W = align_workers(W, njobs, gm.row_groups);
+    // a small matrix with few row groups (a tensor-parallel shard) would otherwise split each row
+    // group over many CTAs of a few chunks each, and its first CTA waits for and adds every
+    // partner's partial sums: then at most kMaxCtasPerRowGroup CTAs per row group (such a matrix
+    // is latency-, not bandwidth-bound)
+    if (!device_count && njobs == 1 && (T + W - 1) / W < kCapBelowChunks && W > gm.row_groups * kMaxCtasPerRowGroup)
+        W = gm.row_groups * kMaxCtasPerRowGroup;
     pl.workers = W;
     if (njobs == 1 && !device_count && W > 0) {
         const int len = (T + W - 1) / W;

@@ -152,3 +152,61 @@ class EPMoELayer:
         self.ffn(b["x_all"], b["ids_all"], b["w_all"], out=b["y_all"], stream=stream, e0=self.e0)
         dist.reduce_scatter_tensor(b["y"], b["y_all"], group=self.group)
         return b["y"]
+
+
+def plan_dispatch(ids, E, world):
+    """Which of a rank's tokens go to which rank: rank d holds experts [d * E / world, (d + 1) * E /
+    world); a token goes to every rank holding one of its k experts, once. Returns (order, counts):
+    order int64 [S] lists token indices grouped by destination rank (ascending token order within
+    each), counts int64 [world] the tokens per destination (S = counts.sum())."""
+    T = ids.shape[0]
+    dest = (ids.long() // (E // world))                                   # [T, k]
+    hit = torch.zeros(T, world, dtype=torch.bool, device=ids.device)
+    hit.scatter_(1, dest, True)
+    counts = hit.sum(0)
+    order = hit.t().nonzero()[:, 1]                                       # rank-major, then token
+    return order, counts
+
+
+class EPMoELayerA2A:
+    """Expert-parallel MoE layer with an all-to-all dispatch and combine (NCCL): each rank routes
+    its own T tokens and sends every token only to the ranks that hold one of its experts (with its
+    ids and weights); each rank runs its experts over the tokens it received (the slots routed to
+    other ranks are skipped) and sends each token's share back; the owner adds the shares in rank
+    order. Against EPMoELayer's all-gather / reduce-scatter this moves only the rows a rank needs,
+    but the counts are exchanged first and read on the host (split sizes), so a call is not
+    capturable in a CUDA graph."""
+
+    def __init__(self, wr, ffn, rank, world, E, group=None, k=8, norm_topk_prob=True):
+        self.wr, self.ffn, self.rank, self.world, self.group = wr, ffn, rank, world, group
+        self.E, self.k, self.norm = E, k, norm_topk_prob
+        assert E % world == 0 and ffn.E == E // world
+        self.e0 = rank * (E // world)
+
+    def __call__(self, x, stream=None):
+        """x: bf16 [T, H] (this rank's tokens) -> fp32 [T, H]."""
+        dist = torch.distributed
+        T, H = x.shape
+        ids, w = route(x, self.wr, self.k, self.norm, stream=stream)
+        order, counts = plan_dispatch(ids, self.E, self.world)
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        send_sizes, recv_sizes = counts.tolist(), recv_counts.tolist()    # host: the split sizes
+        R = sum(recv_sizes)
+        xs, ids_s, w_s = x[order].contiguous(), ids[order].contiguous(), w[order].contiguous()
+        xr = torch.empty(R, H, dtype=x.dtype, device=x.device)
+        ids_r = torch.empty(R, self.k, dtype=ids.dtype, device=x.device)
+        w_r = torch.empty(R, self.k, dtype=w.dtype, device=x.device)
+        dist.all_to_all_single(xr, xs, recv_sizes, send_sizes, group=self.group)
+        dist.all_to_all_single(ids_r, ids_s, recv_sizes, send_sizes, group=self.group)
+        dist.all_to_all_single(w_r, w_s, recv_sizes, send_sizes, group=self.group)
+        yr = self.ffn(xr, ids_r, w_r, stream=stream, e0=self.e0) if R else torch.empty(0, H, device=x.device)
+        yb = torch.empty(order.numel(), yr.shape[1], dtype=yr.dtype, device=x.device)
+        dist.all_to_all_single(yb, yr, send_sizes, recv_sizes, group=self.group)
+        y = torch.zeros(T, yr.shape[1], dtype=yr.dtype, device=x.device)
+        o = 0
+        for n in send_sizes:                      # rank order: the same float sums on every run
+            if n:
+                y.index_add_(0, order[o:o + n], yb[o:o + n])
+            o += n
+        return y

@@ -74,6 +74,39 @@ class TPLinear:
         return out
 
 
+    def mm(self, x, out, epi=EPI_F32, stream=None, reduce=True):
+        """Prefill (many rows) on the tensor cores (DenseMatrix.mm, fp16 operands, fp32
+        accumulation); a row-parallel shard's partial output is then all-reduced over the group
+        (NCCL), as for decode. x: bf16 [M, K_shard or K]."""
+        self.m.mm(x, out=out, epi=epi, stream=stream)
+        if self.kind == "row" and reduce and self.group is not None:
+            if stream is not None:
+                with torch.cuda.stream(stream):
+                    torch.distributed.all_reduce(out, group=self.group)
+            else:
+                torch.distributed.all_reduce(out, group=self.group)
+        return out
+
+
+class TPMLP:
+    """One rank's shard of a SwiGLU MLP for prefill: gate/up column-parallel (this rank's block of
+    gate rows stacked on its block of up rows, so the GEMM's SwiGLU epilogue stays fused), down
+    row-parallel (this rank's K block) followed by an all-reduce of the [M, hidden] fp32 output."""
+
+    def __init__(self, gu, dn, group=None):
+        self.gu = TPLinear(*gu, "column", gateup=True, group=group)
+        self.dn = TPLinear(*dn, "row", group=group)
+
+    @classmethod
+    def from_full(cls, gate, up, down, rank, world, group=None):
+        return cls(fused_rows_shard([gate, up], rank, world), row_shard(*down, rank, world), group)
+
+    def __call__(self, x, a, y, stream=None, reduce=True):
+        """x bf16 [M, hidden]; a bf16 [M, inter / world] (the activation); y fp32 [M, hidden]."""
+        self.gu.mm(x, a, epi=EPI_SWIGLU, stream=stream)
+        return self.dn.mm(a, y, stream=stream, reduce=reduce)
+
+
 class TPDecoderLayer:
     """One decoder layer's projections on one rank: q/k/v (column), o (row), gate/up with the
     SwiGLU epilogue (column), down (row). Attention is not part of the path: o takes this rank's
@@ -126,6 +159,8 @@ class TPDecoderLayer:
             self.o(b["qkv"][:, :self.nq], b["h"], stream=stream)
             self.gu(b["h"], b["a"], epi=EPI_SWIGLU_F32, stream=stream)
         else:
+            if x.dtype != torch.bfloat16:           # these rows take the bf16 path (too many for fp32)
+                x = x.to(torch.bfloat16)
             self.qkv(x, b["qkv"], epi=EPI_BF16, stream=stream)
             self.o(b["qkv"][:, :self.nq], b["h"], stream=stream, out_bf16=b["x2"])
             self.gu(b["x2"], b["a"], epi=EPI_SWIGLU, stream=stream)

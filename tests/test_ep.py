@@ -77,3 +77,19 @@ def test_expert_parallel_layer_gloo_world2():
     assert all(p.exitcode == 0 for p in procs)
     res = dict(q.get(timeout=5) for _ in range(2))
     assert max(res.values()) <= 1e-9
+
+
+def test_plan_dispatch_sends_each_token_once_to_each_expert_rank():
+    import torch
+    from opennpu_b200.moe import plan_dispatch
+    g = torch.Generator().manual_seed(0)
+    E, k, T, world = 32, 8, 50, 4
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    order, counts = plan_dispatch(ids, E, world)
+    assert int(counts.sum()) == order.numel()
+    o = 0
+    for d in range(world):
+        toks = order[o:o + int(counts[d])].tolist()
+        o += int(counts[d])
+        want = [t for t in range(T) if any(int(e) // (E // world) == d for e in ids[t])]
+        assert toks == want

@@ -108,3 +108,28 @@ def test_prefill_rejects_bad_arguments():
     assert lib.onpu_dense_mm_dev(m.h, x.data_ptr(), 500, 4, y.data_ptr(), 256, EPI_F32, st) < 0
     assert lib.onpu_dense_mm_dev(m.h, x.data_ptr(), 512, 4, y.data_ptr(), 128, EPI_F32, st) < 0
     assert lib.onpu_dense_mm_dev(m.h, x.data_ptr(), 512, 4, y.data_ptr(), 256, EPI_SWIGLU, st) < 0
+
+
+@pytest.fixture(scope="module")
+def qwen3_14b_mlp():
+    """BASELINE configs[2] at full size: gate/up 17408 x 5120 (one of the pair) and down
+    5120 x 17408, int4 group-32 weights."""
+    vg, sg, mg = _int4(17408, 5120, seed=141)
+    vd, sd, md = _int4(5120, 17408, seed=142)
+    return (vg, sg, mg), (vd, sd, md)
+
+
+@pytest.mark.parametrize("M", [512, 2048])
+@pytest.mark.parametrize("which", ["gate", "down"])
+def test_prefill_qwen3_14b_full_size(qwen3_14b_mlp, M, which):
+    """The tensor-core GEMM at config 3's shapes against the oracle's fp32 dequantise-then-matmul
+    (the weights rounded to fp16 once on the GPU: ~2^-12 of each weight, within the bound). The
+    oracle's product runs in fp32 BLAS here (float64 would take minutes at this size)."""
+    v, s, m = qwen3_14b_mlp[0] if which == "gate" else qwen3_14b_mlp[1]
+    K = v.shape[1]
+    x = O.gen_x(M, K, seed=M + K)
+    y = m.mm(torch.from_numpy(x).to(torch.bfloat16).cuda())
+    torch.cuda.synchronize()
+    L.check(L.load().onpu_check_device(), "device status")
+    ref = O.matmul_xwT(x, O.dequant_baseline(v, s), acc=np.float32)
+    _assert_close(y.cpu().numpy(), ref)

@@ -154,3 +154,32 @@ def test_tp_layer_two_ranks_nccl():
     w = _weights(seed=20)
     x = O.gen_x(2, HIDDEN, seed=21)
     _close(y, _oracle_layer(w, x.astype(np.float64)))
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_tp_prefill_mlp_emulated_ranks(world):
+    """Prefill under tensor parallelism on one GPU: each rank's gate/up rows and down K block on
+    the tensor cores, the row-parallel partials summed in rank order, against the oracle's
+    dequantise-then-matmul with the same roundings as the GPU path (fp16 weights and activations
+    into the GEMMs, the SwiGLU activation rounded to bf16 between them)."""
+    H, I, M = 1024, 2048, 96
+    w = {}
+    for i, (name, N, K) in enumerate([("gate", I, H), ("up", I, H), ("down", H, I)]):
+        v, s = O.gen_weights(N, K, seed=60 + i)
+        w[name] = (torch.from_numpy(O.pack_baseline(v)), torch.from_numpy(s.view(np.int16)))
+    x = torch.from_numpy(O.gen_x(M, H, seed=63)).to(torch.bfloat16).cuda()
+    y = torch.zeros(M, H, device="cuda")
+    for r in range(world):
+        mlp = tp.TPMLP.from_full(w["gate"], w["up"], w["down"], r, world)
+        a = torch.empty(M, I // world, device="cuda", dtype=torch.bfloat16)
+        yr = torch.empty(M, H, device="cuda")
+        y += mlp(x, a, yr)
+    torch.cuda.synchronize()
+    f16 = lambda W: W.astype(np.float16).astype(np.float64)
+    xd = x.float().cpu().numpy().astype(np.float64)
+    g, u = xd @ f16(_deq(*w["gate"])).T, xd @ f16(_deq(*w["up"])).T
+    a = O.round_bf16((O.silu(g) * u).astype(np.float32)).astype(np.float64)
+    ref = a @ f16(_deq(*w["down"])).T
+    yy = y.cpu().numpy().astype(np.float64)
+    err = np.linalg.norm(yy - ref) / np.linalg.norm(ref)
+    assert err <= 1e-3, err
