@@ -314,10 +314,14 @@ int onpu_chain_run(void *chain, void *stream);
 int onpu_chain_trace(void *chain, uint64_t *stamps);
 void onpu_chain_free(void *chain);
 /* Tracing of the GEMV kernels (dense and expert launches through this library): later launches
- * with at most `ctas` CTAs write 8 %globaltimer values per CTA to the device buffer `stamps`
- * [ctas][8]: entry, producer's first copy issued, consumers past griddepcontrol.wait, activations
- * staged, first weights arrived, last stage consumed, range flushed, then the nanoseconds the
- * consumers waited for weights. Each launch overwrites the same slots. NULL turns it off. */
+ * with at most `ctas` CTAs write 12 values per CTA to the device buffer `stamps` [ctas][12]:
+ * %globaltimer stamps (ns) of entry, producer's first copy issued, consumers past
+ * griddepcontrol.wait, activations staged, first weights arrived, last stage consumed, range
+ * flushed; the nanoseconds the consumers waited for weights; then for a split row group the stamp
+ * of this CTA's partial sums published (as a later contributor), the stamp of its partners' flags
+ * seen and their count (as the first contributor), and the stamp of their partial sums read. Slots
+ * a launch does not reach keep their value; each launch overwrites the same slots. NULL turns it
+ * off. */
 int onpu_gemv_trace(uint64_t *stamps, int64_t ctas);
 
 /* onpu_dense_mv_dev with no allocation in the call: no reference counterpart (the NPU library

@@ -11,10 +11,11 @@
 // A call is one launch of kCommCtas CTAs; CTA b owns elements [b * per, (b + 1) * per):
 //  1. every thread stores its elements of the local partial, each paired with the call number in
 //     one 8-byte store, into slot [parity][rank] of every rank's buffer (peer stores over NVLink);
-//  2. it then reads slot [parity][s][i] of its own buffer for every rank s, until the word carries
-//     this call's number (an 8-byte store lands whole, so value and number arrive together: no
-//     fence, no separate flag), and adds the values in rank order (the same float sum on every
-//     rank). Waits are bounded (2 s, then the error word is set and the word's value is used).
+//  2. it then reads slot [parity][s][i] of its own buffer for every rank s (all ranks' loads in
+//     flight at once), until the word carries this call's number (an 8-byte store lands whole, so
+//     value and number arrive together: no fence, no separate flag), and adds the values in rank
+//     order (the same float sum on every rank). Waits are bounded (2 s by default, then the error
+//     word is set and the word's value is used).
 // The call number is kept per CTA in the owner's buffer, so CUDA-graph replays need no host
 // state. Two slot sets by call parity: a rank can be at most one call ahead of a peer that is
 // still reading (it cannot finish call c+1 without that peer's words of call c+1).
@@ -45,15 +46,6 @@ struct CommParams {
     uint64_t wait_ns;                // how long a thread waits for a peer's word
 };
 
-__device__ __forceinline__ void st_word(uint2 *p, uint32_t v, uint32_t tag) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v), "r"(tag) : "memory");
-}
-__device__ __forceinline__ uint2 ld_word(const uint2 *p) {
-    uint2 r;
-    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
-    return r;
-}
-
 __global__ void __launch_bounds__(kCommThreads) comm_allreduce_kernel(const CommParams p) {
     const int b = blockIdx.x;
     const int64_t per = (p.n + kCommCtas - 1) / kCommCtas;
@@ -71,23 +63,7 @@ __global__ void __launch_bounds__(kCommThreads) comm_allreduce_kernel(const Comm
             for (int d = 0; d < p.world; ++d) st_word(p.bufs[d] + (set + p.rank) * p.cap + i, v, c);
         }
     for (int64_t i = lo + threadIdx.x; i < hi; i += kCommThreads) {
-        float acc = 0.f;
-        for (int s = 0; s < p.world; ++s) {
-            const uint2 *w = own + (set + s) * p.cap + i;
-            uint2 r = ld_word(w);
-            if (r.y != c) {
-                const uint64_t t0 = global_timer_ns();
-                for (int it = 0; r.y != c; ++it) {
-                    if ((it & 255) == 255 && global_timer_ns() - t0 > p.wait_ns) {
-                        atomicOr(p.err, 16);
-                        break;
-                    }
-                    r = ld_word(w);
-                }
-            }
-            const float x = __uint_as_float(r.x);
-            acc = s == 0 ? x : acc + x;
-        }
+        const float acc = recv_words_sum<kCommMaxRanks>(own + set * p.cap + i, p.cap, p.world, c, p.wait_ns, p.err);
         if (p.dst) p.dst[i] = acc;
         if (p.dst_bf16) p.dst_bf16[i] = __float2bfloat16_rn(acc);
     }

@@ -77,10 +77,8 @@ __device__ __forceinline__ void store_pair(const GemvParams &p, int g, int s, in
             if (rr < p.N) {
                 const int64_t e = static_cast<int64_t>(yr) * p.ldy + rr;
                 const uint32_t v = __float_as_uint(h ? v_hi : v_lo);
-                for (int d = 0; d < p.peer_world; ++d) {
-                    uint2 *w = static_cast<uint2 *>(p.peer[d]) + (set + p.peer_rank) * p.peer_cap + e;
-                    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(w), "r"(v), "r"(call) : "memory");
-                }
+                for (int d = 0; d < p.peer_world; ++d)
+                    st_word(static_cast<uint2 *>(p.peer[d]) + (set + p.peer_rank) * p.peer_cap + e, v, call);
             }
         }
     } else {
@@ -117,24 +115,8 @@ __device__ void peer_receive(const GemvParams &p, int lo, int hi, uint32_t call,
         if (rr >= p.N) continue;
         const int yr = p.jobs[0].yrow[tok];
         const int64_t e = static_cast<int64_t>(yr) * p.ldy + rr;
-        float acc = 0.f;
-        for (int d = 0; d < p.peer_world; ++d) {
-            const uint2 *w = own + (set + d) * p.peer_cap + e;
-            uint2 v;
-            asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(w) : "memory");
-            if (v.y != call) {
-                const uint64_t t0 = global_timer_ns();
-                for (int it = 0; v.y != call; ++it) {
-                    if ((it & 255) == 255 && global_timer_ns() - t0 > p.peer_wait_ns) {
-                        atomicOr(p.err, 16);
-                        break;
-                    }
-                    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(w) : "memory");
-                }
-            }
-            const float x = __uint_as_float(v.x);
-            acc = d == 0 ? x : acc + x;
-        }
+        const float acc = recv_words_sum<kPeerMaxRanks>(own + set * p.peer_cap + e, p.peer_cap, p.peer_world, call,
+                                                         p.peer_wait_ns, p.err);
         if (p.y) reinterpret_cast<float *>(p.y)[e] = acc;
         if (p.y_bf16) reinterpret_cast<__nv_bfloat16 *>(p.y_bf16)[e] = __float2bfloat16_rn(acc);
     }
@@ -373,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
                 }
             named_bar_sync(1, kConsumers * 32);
             if (threadIdx.x == 0) st_release_gpu(p.counters + cta, 1u);
+            if (tr) trace[8] = global_timer_ns();
             return;
         }
         // tail segment of the first contributor: collect cf+1 .. cl (bounded wait on their flags)
@@ -381,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
                 if (range_empty(w2, W, T)) continue;          // fewer chunks than CTAs: no partials
                 const uint64_t t0 = global_timer_ns();
                 while (ld_acquire_gpu(p.counters + w2) == 0u) {
-                    __nanosleep(256);
+                    __nanosleep(32);
                     if (global_timer_ns() - t0 > kWaitLimitNs) {
                         atomicOr(p.err, 4);
                         break;
@@ -391,20 +374,37 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
             }
         }
         named_bar_sync(1, kConsumers * 32);
+        if (tr) {
+            trace[9] = global_timer_ns();
+            trace[10] = static_cast<unsigned long long>(cl - cf);
+        }
+        // the partners' partial sums, kPartBatch partners' loads in flight before the first add
+        // (one L2 round trip per batch, not per partner), added in partner order (deterministic)
+        for (int w0 = cf + 1; w0 <= cl; w0 += kPartBatch) {
+            float pv[kPartBatch][NT][4];
+            bool has[kPartBatch];
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt)
+            for (int q = 0; q < kPartBatch; ++q) {
+                has[q] = w0 + q <= cl && !range_empty(w0 + q, W, T);
+                const float *src = p.part + static_cast<int64_t>(w0 + q) * kSlotFloats;
 #pragma unroll
-            for (int f = 0; f < 4; ++f) {
-                const int tok = nt * 8 + 2 * t + (f & 1);
-                if (tok < m) {
-                    float v = acc[nt][f];
-                    const int e = ((s * 8 + r) * 2 + (f >> 1)) * 16 + tok;
-#pragma unroll 4
-                    for (int w2 = cf + 1; w2 <= cl; ++w2)
-                        if (!range_empty(w2, W, T)) v += __ldcg(p.part + static_cast<int64_t>(w2) * kSlotFloats + e);
-                    acc[nt][f] = v;
-                }
+                for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                    for (int f = 0; f < 4; ++f) {
+                        const int tok = nt * 8 + 2 * t + (f & 1);
+                        pv[q][nt][f] = has[q] && tok < m ? __ldcg(src + ((s * 8 + r) * 2 + (f >> 1)) * 16 + tok) : 0.f;
+                    }
             }
+#pragma unroll
+            for (int q = 0; q < kPartBatch; ++q)
+                if (has[q])
+#pragma unroll
+                    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+                        for (int f = 0; f < 4; ++f)
+                            if (nt * 8 + 2 * t + (f & 1) < m) acc[nt][f] += pv[q][nt][f];
+        }
+        if (tr) trace[11] = global_timer_ns();
         store_rows();
     };
     (void)flag;

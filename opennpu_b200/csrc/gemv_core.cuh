@@ -17,6 +17,7 @@ constexpr int kThreads = (kConsumers + 1) * 32;    // + the producer warp
 constexpr int kCPS = 4, kNS = 8;                   // chunks per stage, stages
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // a copy that has not landed in 2 s is a fault
 constexpr int kSlotFloats = 4 * 8 * 2 * 16;        // [strip][r][h][token] head partial sums of a CTA
+constexpr int kPartBatch = 4;                       // partners whose partial sums are loaded at once
 constexpr int kXSlot = 192;                        // per-stage activation slot: 128 B + 64 B pad
 
 __host__ __device__ constexpr int stage_w_bytes(int fmt) { return kCPS * chunk_bytes(fmt); }

@@ -90,7 +90,7 @@ enum GemvEpilogue : int {
 // GEMV tracing: per CTA, ns stamps of kernel entry, producer's first copy issued, consumers past
 // griddepcontrol.wait, activations staged, first weight stage arrived, last stage consumed, range
 // flushed (split row groups closed), and the ns the consumers waited for weights in total
-constexpr int kGemvTrace = 8;
+constexpr int kGemvTrace = 12;
 
 constexpr int kPeerMaxRanks = 8;       // ranks of the peer-memory all-reduce (comm.cu)
 constexpr int kPeerCtaCounters = 1024; // call counters of the GEMV CTAs that sum rows (kEpiPeer)

@@ -138,6 +138,49 @@ __device__ __forceinline__ void red_release_add_gpu(unsigned *p, unsigned v) {
     asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// ---------------------------------------------------------------- peer all-reduce words
+// An 8-byte {fp32 value, call number} word (comm.cu, the row-parallel GEMV epilogue): one store
+// lands whole, so value and number arrive together, with no fence and no separate flag.
+__device__ __forceinline__ void st_word(uint2 *p, uint32_t v, uint32_t tag) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(v), "r"(tag) : "memory");
+}
+__device__ __forceinline__ uint2 ld_word(const uint2 *p) {
+    uint2 r;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p) : "memory");
+    return r;
+}
+// The rank-order sum of the `world` (<= MAXW) words at base + d * stride that carry `call`. Every
+// word is loaded before the first is checked, so the ranks cost one memory round trip, not world;
+// a word that has not arrived is polled again, for at most wait_ns (then *err |= 16 and the value
+// it holds is used).
+template <int MAXW>
+__device__ __forceinline__ float recv_words_sum(const uint2 *base, int64_t stride, int world, uint32_t call,
+                                                uint64_t wait_ns, int *err) {
+    uint2 v[MAXW];
+#pragma unroll
+    for (int d = 0; d < MAXW; ++d)
+        if (d < world) v[d] = ld_word(base + d * stride);
+    float acc = 0.f;
+#pragma unroll
+    for (int d = 0; d < MAXW; ++d) {
+        if (d < world) {
+            if (v[d].y != call) {
+                const uint64_t t0 = global_timer_ns();
+                for (int it = 0; v[d].y != call; ++it) {
+                    if ((it & 255) == 255 && global_timer_ns() - t0 > wait_ns) {
+                        atomicOr(err, 16);
+                        break;
+                    }
+                    v[d] = ld_word(base + d * stride);
+                }
+            }
+            const float x = __uint_as_float(v[d].x);
+            acc = d == 0 ? x : acc + x;
+        }
+    }
+    return acc;
+}
+
 // ---------------------------------------------------------------- loads
 __device__ __forceinline__ uint4 ld_cg_v4(const void *p) {   // L2 only: data written in this launch
     uint4 v;
