@@ -25,6 +25,7 @@ path (restated in oracle/) on this host's cores, on a bounded sample of the same
 """
 import argparse
 import json
+import math
 import os
 import subprocess
 import sys
@@ -60,10 +61,25 @@ def int4_param_bytes(N, K):
     return N * K // 2 + N * (K // 32) * 2
 
 
-def gen_int4_cuda(N, K, gen):
-    qk = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=gen)
-    s = ((torch.randn(N, K // 32, device="cuda", generator=gen) * 0.02).abs() + 1e-4).to(torch.float16)
-    return qk, s
+def gen_int4_cuda(N, K, gen, gain=None, k_full=None):
+    """Random int4 weights [N, K] (two's-complement codes packed along K, fp16 group scales).
+    gain None: codes uniform in -8..7, scales |N(0, 0.02)| + 1e-4. gain g: a model-like matrix
+    whose y = W x (summed over k_full inputs, K of them on this rank) has rms g * rms(x): codes
+    uniform in -7..7 (zero mean, as quantised weights are; E[v^2] = 280/15), scales
+    sigma * (|z| + 0.005) with E[(|z| + 0.005)^2] = 1.008. Zero-mean codes matter: with codes of
+    mean -0.5 and positive scales every output shares a common offset that the next projection's
+    32-groups add coherently."""
+    if gain is None:
+        qk = torch.randint(0, 256, (N, K // 2), dtype=torch.uint8, device="cuda", generator=gen)
+        s = ((torch.randn(N, K // 32, device="cuda", generator=gen) * 0.02).abs() + 1e-4).to(torch.float16)
+        return qk, s
+    u = torch.randint(0, 15, (N, K), dtype=torch.uint8, device="cuda", generator=gen)
+    nib = u + (u >= 8).to(torch.uint8)                 # nibbles 0..7, 9..15: v = -7..7, never -8
+    qk = nib[:, 0::2] | (nib[:, 1::2] << 4)
+    del u, nib
+    sigma = gain / math.sqrt(280.0 / 15.0 * (k_full or K) * 1.008)
+    s = ((torch.randn(N, K // 32, device="cuda", generator=gen).abs() + 0.005) * sigma).to(torch.float16)
+    return qk.contiguous(), s
 
 
 class DecodeStack:
@@ -750,6 +766,8 @@ def run_moe(args):
 
 
 T_HIDDEN, T_INTER, T_QH, T_KVH, T_LAYERS = 5120, 27648, 40, 8, 64
+# rms of N(0, 1) gate and up inputs for which silu(g) * u has rms 1 (E[(silu(c g) c u)^2] = 1)
+SWIGLU_UNIT_GAIN = 1.269
 
 
 def tp_layer0_parity(work, rank):
@@ -759,7 +777,7 @@ def tp_layer0_parity(work, rank):
     layer (all-reduced output) is checked; with more ranks, this rank's q/k/v shard."""
     gen = torch.Generator(device="cuda")
     gen.manual_seed(work.seed)
-    mats = [gen_int4_cuda(N, K, gen) for N, K in work.shapes]
+    mats = [gen_int4_cuda(N, K, gen, gain=g, k_full=kf) for N, K, g, kf in work.gen_args]
     lay, M = work.layers[0], work.M
     x = torch.randn(M, T_HIDDEN, device="cuda", generator=torch.Generator(device="cuda").manual_seed(99))
     x = x.to(torch.bfloat16).to(work.x.dtype)
@@ -806,9 +824,13 @@ class TPStack:
     """Qwen2.5-32B decode projections, 64 layers of random int4 weights, tensor-parallel
     over the ranks: q/k/v and gate/up column-parallel (row blocks), o and down row-parallel (K
     blocks on 32-group boundaries) with an all-reduce of the fp32 partial outputs after each. Each
-    rank generates only its own shards. The layer input of layer l+1 is layer l's output: fp32 for
-    decode (M <= 8: every activation stays fp32, each GEMV stages it as two fp16 halves), else
-    rounded to bf16."""
+    rank generates only its own shards. Inside a layer each projection reads the previous one's
+    output (o takes q's output as the stand-in for attention): fp32 for decode (M <= 8: every
+    activation stays fp32, each GEMV stages it as two fp16 halves), else rounded to bf16. Layer
+    l's q/k/v reads its own rms-1 input, the stand-in for the RMSNorm output a model feeds it
+    (the norm is outside the matmul path; without it SwiGLU's quadratic response makes a chain of
+    64 random layers grow or decay without bound); layer 0's input is the one the end-to-end
+    timing copies from the host every step."""
 
     def __init__(self, M, rank, world, group, seed, layers=T_LAYERS, allreduce=None):
         from opennpu_b200 import tp
@@ -818,18 +840,20 @@ class TPStack:
         q, kv = T_QH * 128 // world, T_KVH * 128 // world
         i_r, h_r = T_INTER // world, T_HIDDEN // world
         self.layers = []
+        # model-like scales keep every activation at rms ~1: each projection preserves rms, gate/up
+        # outputs have rms 1.269 so that silu(g) * u has rms 1
+        self.gen_args = [(q + 2 * kv, T_HIDDEN, 1.0, None), (T_HIDDEN, h_r, 1.0, T_HIDDEN),
+                         (2 * i_r, T_HIDDEN, SWIGLU_UNIT_GAIN, None), (T_HIDDEN, i_r, 1.0, T_INTER)]
         for _ in range(layers):
-            qkv = gen_int4_cuda(q + 2 * kv, T_HIDDEN, gen)
-            o = gen_int4_cuda(T_HIDDEN, h_r, gen)
-            gu = gen_int4_cuda(2 * i_r, T_HIDDEN, gen)
-            dn = gen_int4_cuda(T_HIDDEN, i_r, gen)
+            qkv, o, gu, dn = [gen_int4_cuda(N, K, gen, gain=g, k_full=kf) for N, K, g, kf in self.gen_args]
             self.layers.append(tp.TPDecoderLayer(qkv, o, gu, dn, q, group=group, allreduce=allreduce))
             del qkv, o, gu, dn
         torch.cuda.synchronize()
         self.M, self.world = M, world
         self.f32 = M <= min(lay.f32_rows for lay in self.layers)
-        x = torch.randn(M, T_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
-        self.x = x.float() if self.f32 else x
+        xin = torch.randn(layers, M, T_HIDDEN, device="cuda", generator=gen).to(torch.bfloat16)
+        self.xin = xin.float() if self.f32 else xin          # each layer's q/k/v input
+        self.x = self.xin[0]                                 # layer 0's: the host copies this one
         self.xs = [torch.empty(M, T_HIDDEN, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
         self.bufs = self.layers[0].buffers(M)
         shards = [(q + 2 * kv, T_HIDDEN), (T_HIDDEN, h_r), (2 * i_r, T_HIDDEN), (T_HIDDEN, i_r)]
@@ -853,14 +877,11 @@ class TPStack:
         return run, nbytes, len(self.layers), f"gemv_int4_kernel gate_up {N}x{K} + SwiGLU"
 
     def step(self):
-        x = self.x
         for i, lay in enumerate(self.layers):
             if self.f32:
-                x = lay(x, self.bufs)               # fp32 output, the next layer's input
+                lay(self.xin[i], self.bufs)         # fp32 output y
             else:
-                nx = self.xs[i & 1]
-                lay(x, self.bufs, y_bf16=nx)
-                x = nx
+                lay(self.xin[i], self.bufs, y_bf16=self.xs[i & 1])
         return self.bufs["y"]
 
 
@@ -1041,6 +1062,7 @@ def run_tp(args):
                        "fused with the peer all-reduce at N > 1) from a CUDA graph, pinned host input/output "
                        "copies and a host synchronisation per step (wall clock)"}
     del graph
+    y_rms = float(work.bufs["y"].float().pow(2).mean().sqrt())      # the last layer's down output
     parity = tp_layer0_parity(work, rank)
     cpu = extra = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -1064,11 +1086,12 @@ def run_tp(args):
             "ms_per_step": round(ms_step, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "int4 weights, " + ("fp32 activations (two fp16 halves)" if f32 else "bf16 activations")
                      + ", fp32 accumulate",
-            "data": "synthetic (seeded random int4 weights, fp16 scales, bf16 N(0,1) input)",
+            "data": "synthetic (seeded random zero-mean int4 weights, fp16 scales sized so every activation "
+                    "stays at rms ~1; each layer's q/k/v input bf16 N(0,1), the stand-in for its RMSNorm output)",
             "config": tp_config(M, layers, world),
             "details": {"gb_per_s_all_ranks": round(gbs_rank * world, 1), "gb_per_s_per_gpu": round(gbs_rank, 1),
                         "bytes_per_step_per_gpu": rank_bytes, "l2": "inputs larger than L2 (no flush needed)",
-                        "cuda_graph": True,
+                        "cuda_graph": True, "last_layer_output_rms": round(y_rms, 4),
                         "collective": (("the row-parallel GEMV fused with a one-shot all-reduce over NVLink peer "
                                         "memory (libonpu comm kernel)" if allreduce is not None else "NCCL all-reduce")
                                        + " (fp32) after o and down") if world > 1 else None},

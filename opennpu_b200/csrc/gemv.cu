@@ -12,7 +12,8 @@
 //    contiguous range of chunks.
 //  * Per CTA, one producer warp and four consumer warps. The producer streams the range
 //    HBM -> shared memory with 1-D bulk copies (cp.async.bulk, mbarrier transaction counts, no
-//    multicast), NS stages of CPS chunks, recycled through "empty" mbarriers.
+//    multicast, an L2 evict-first policy: weights are read once), NS stages of CPS chunks,
+//    recycled through "empty" mbarriers.
 //  * Activations: a single-job launch whose tokens fit keeps them resident in shared memory
 //    (loaded once by the consumers after griddepcontrol.wait), so the copy engine only carries
 //    weights; otherwise each stage also carries one 128-B copy per token per chunk.
@@ -26,8 +27,9 @@
 //    (release store, no waiting); the first contributor, at the end of its range, waits for those
 //    flags (bounded) and adds the partials to its registers in CTA order - deterministic. Waits
 //    only point at higher-numbered CTAs and the grid is one resident wave, so they terminate.
-//  * Programmatic dependent launch: the weight prefetch (constant data) is issued before
-//    griddepcontrol.wait, so a kernel's weight stream overlaps the previous kernel's tail.
+//  * Programmatic dependent launch: the weight prefetch (constant data) and host-written job
+//    descriptors are read before griddepcontrol.wait, so a kernel's weight stream overlaps the
+//    previous kernel's tail and its activation staging starts with the activation loads.
 //  * Every wait is bounded (2 s of global time); a timed-out wait sets the error word and the
 //    warp keeps draining the pipeline without computing, so no copy is left in flight at exit.
 #include <cuda_bf16.h>
@@ -164,6 +166,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         // ============================================================ producer
         int wj = lo / per_job;                        // weight cursor: job of the next chunk
         const uint8_t *wbase = p.jobs_ready ? p.jobs[wj].w : nullptr;
+        const uint64_t wpol = l2_evict_first_policy();   // weights are read once per launch
         auto issue_weights = [&](int st) {            // lane 0 only
             const int c0 = lo + st * kCPS, c1 = min(hi, c0 + kCPS);
             const uint32_t bar = full + (st % kNS) * 8;
@@ -173,8 +176,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
             while (c < c1) {                          // one copy per run of chunks within a job
                 if (c >= (wj + 1) * per_job) wbase = p.jobs[++wj].w;
                 const int run_end = min(c1, (wj + 1) * per_job);
-                bulk_g2s(dst, wbase + static_cast<int64_t>(c - wj * per_job) * CB,
-                         static_cast<uint32_t>((run_end - c) * CB), bar);
+                bulk_g2s_hint(dst, wbase + static_cast<int64_t>(c - wj * per_job) * CB,
+                              static_cast<uint32_t>((run_end - c) * CB), bar, wpol);
                 dst += (run_end - c) * CB;
                 c = run_end;
             }
@@ -244,18 +247,26 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     // ================================================================ consumers (strip s = warp)
     const int s = warp, r = lane >> 2, t = lane & 3;
     volatile int *flag = reinterpret_cast<volatile int *>(smem + p.off_bar + 2 * kNS * 8);
-    pdl_launch_dependents();
-    pdl_wait_prerequisites();                         // x / outputs / scratch may belong to the previous kernel
-    const bool tr = trace && threadIdx.x == 0;
-    if (tr) trace[2] = global_timer_ns();
-    uint32_t call = 0;                                // kEpiPeer: this CTA's all-reduce call number
-    if constexpr (EPI == kEpiPeer) call = *reinterpret_cast<volatile uint32_t *>(p.peer_calls + cta) + 1u;
-
+    int *s_xrow = reinterpret_cast<int *>(smem + p.off_bar + 2 * kNS * 8 + 16);   // the staged job's rows
     int j = lo / per_job;
     int g = (lo - j * per_job) / p.chunks;
     int kc = lo - j * per_job - g * p.chunks;
     int seg = lo;
-    int m = p.jobs[j].m;
+    int m = 0;
+    // descriptors the host wrote are read before griddepcontrol.wait (they are not the previous
+    // kernel's output), so staging starts with the activation loads themselves
+    auto load_job = [&]() {
+        m = p.jobs[j].m;
+        if (threadIdx.x < kMaxTokensPerJob) s_xrow[threadIdx.x] = p.jobs[j].xrow[threadIdx.x];
+    };
+    if (p.jobs_ready) load_job();
+    pdl_launch_dependents();
+    pdl_wait_prerequisites();                         // x / outputs / scratch may belong to the previous kernel
+    if (!p.jobs_ready) load_job();
+    const bool tr = trace && threadIdx.x == 0;
+    if (tr) trace[2] = global_timer_ns();
+    uint32_t call = 0;                                // kEpiPeer: this CTA's all-reduce call number
+    if constexpr (EPI == kEpiPeer) call = *reinterpret_cast<volatile uint32_t *>(p.peer_calls + cta) + 1u;
 
     const int mslots = p.xslots - 1;                  // rows the activation region is laid out for
     // resident activations: fp16 rows, a zero block, the offset table, token scales; staged
@@ -264,24 +275,27 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     const bool win = xres && p.kwin;
     const int kc0 = win ? lo % p.chunks : 0, nch = win ? hi - lo : p.chunks;
     constexpr bool split = XS;
-    auto row_of = [](const GemvJob *jb) { return [jb](int n) { return jb->xrow[n]; }; };
-    auto stage = [&](int jj, auto su) {
-        const GemvJob *jb = p.jobs + jj;
+    // s_xrow holds job jj's rows and mj its token count; stage_activations' first barrier
+    // publishes s_xrow to every consumer thread before any activation load
+    auto row_of = [s_xrow](int n) { return s_xrow[n]; };
+    auto stage = [&](int mj, auto su) {
         constexpr int SU = decltype(su)::value;
         if constexpr (XS)
-            stage_activations<FMT, NT, false, true, SU>(p.xf, p.ldx, row_of(jb), jb->m, mslots, p.K, kc0, nch,
-                                                        p.wchunks, p.xstride, smem + kNS * STAGE_W, threadIdx.x,
-                                                        kConsumers * 32);
+            stage_activations<FMT, NT, false, true, SU>(p.xf, p.ldx, row_of, mj, mslots, p.K, kc0, nch, p.wchunks,
+                                                        p.xstride, smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
         else
-            stage_activations<FMT, NT, false, false, SU>(p.x, p.ldx, row_of(jb), jb->m, mslots, p.K, kc0, nch,
-                                                         p.wchunks, p.xstride, smem + kNS * STAGE_W, threadIdx.x,
-                                                         kConsumers * 32);
+            stage_activations<FMT, NT, false, false, SU>(p.x, p.ldx, row_of, mj, mslots, p.K, kc0, nch, p.wchunks,
+                                                         p.xstride, smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
     };
-    if (xres) stage(j, std::integral_constant<int, 4>{});
+    if (xres) stage(m, std::integral_constant<int, 4>{});
     if (tr) trace[3] = global_timer_ns();
     uint64_t waited = 0;
-    // inside the chunk loop: fewer loads in flight per thread, so the loop keeps its registers
-    auto restage = [&](int jj) { stage(jj, std::integral_constant<int, 1>{}); };
+    // the next job (every consumer is past the previous one's activations); inside the chunk
+    // loop, so fewer loads in flight per thread and the loop keeps its registers
+    auto restage = [&](int jj) {
+        if (threadIdx.x < kMaxTokensPerJob) s_xrow[threadIdx.x] = p.jobs[jj].xrow[threadIdx.x];
+        stage(p.jobs[jj].m, std::integral_constant<int, 1>{});
+    };
     const float *tscale = reinterpret_cast<const float *>(smem + kNS * STAGE_W + p.ctab_off +
                                                           p.wchunks * tab_chunk_bytes(NT));
 
@@ -598,7 +612,7 @@ GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks) {
     L.xslots = mrows + 1;
     const int64_t xbytes = L.xres ? res_bytes : static_cast<int64_t>(kNS) * kCPS * L.xslots * kXSlot;
     L.off_bar = static_cast<int>(kNS * stage_w_bytes(fmt) + (xbytes + 15) / 16 * 16);
-    L.smem = L.off_bar + 2 * kNS * 8 + 16;
+    L.smem = L.off_bar + 2 * kNS * 8 + 16 + kMaxTokensPerJob * 4;   // mbarriers, flag, staged job's rows
     return L;
 }
 

@@ -83,6 +83,23 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
         : "memory");
 }
 
+// An L2 policy that evicts the lines it tags first: for data read once (streamed weights), so
+// they do not push out what the next kernels read again (activations, partial sums).
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+// bulk_g2s with an L2 cache policy (l2_evict_first_policy)
+__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar,
+                                              uint64_t pol) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+        : "memory");
+}
+
 // Order this thread's earlier generic-proxy shared-memory accesses before later async-proxy
 // (bulk copy) writes to the same buffers.
 __device__ __forceinline__ void fence_proxy_async_smem() {
