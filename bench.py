@@ -598,7 +598,14 @@ class MoEStack:
         el = M_E // self.world
         for l in range(len(self.layers)):
             if self.world > 1:
-                ids = self.bufs[l]["ids_all"].cpu().numpy()
+                if self.ep == "a2a":          # the all-to-all form keeps no gathered ids: route and gather here
+                    from opennpu_b200 import moe
+                    mine, _ = moe.route(self.x[l], self.layers[l][0], M_K)
+                    every = torch.empty(self.world * self.T, M_K, dtype=mine.dtype, device=mine.device)
+                    torch.distributed.all_gather_into_tensor(every, mine.contiguous())
+                    ids = every.cpu().numpy()
+                else:
+                    ids = self.bufs[l]["ids_all"].cpu().numpy()
                 nexp = len({int(e) for e in np.unique(ids) if self.rank * el <= e < (self.rank + 1) * el})
                 toks = self.T * self.world
             else:
