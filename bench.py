@@ -663,6 +663,12 @@ def run_moe(args):
     layers = args.layers
     group = torch.distributed.group.WORLD if world > 1 else None
     work = MoEStack(T, seed=3000, layers=layers, rank=rank, world=world, group=group, ep=args.ep)
+    assert work.lib.onpu_moe_set_fused(args.moe_fused) >= 0
+    fused = args.moe_fused == 1
+    if fused and world == 1:
+        work.launches_per_step = 2 * layers             # router (+ job lists), the persistent expert FFN
+    elif fused:
+        work.launches_per_step = 3 * layers             # router, job lists, the persistent expert FFN
     s = torch.cuda.Stream()
     with torch.cuda.stream(s):
         for _ in range(max(args.warmup, 1)):
@@ -757,11 +763,14 @@ def run_moe(args):
                                        "NCCL all-gather (tokens, ids, weights) + reduce-scatter (outputs)")
                                       if world > 1 else None),
                        "l2": "selected experts of all layers per step exceed L2 (no flush needed)",
-                       "cuda_graph": graph is not None},
+                       "cuda_graph": graph is not None,
+                       "expert_ffn": "one persistent launch (gate_up + SwiGLU, down, combine)" if fused else
+                                     "three launches (gate_up + SwiGLU GEMV, down GEMV, combine)"},
             "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
                          "frac": round(gbs / hbm, 4), "peak_kind": peak_kind + " (copy bandwidth)",
-                         "traffic": None, "kernel": "whole MoE layer (router + job lists, gate_up + SwiGLU GEMV, "
-                                                    "down GEMV, combine)",
+                         "traffic": None, "kernel": "whole MoE layer (router + job lists, then the expert FFN: "
+                                                    + ("moe_ffn_kernel)" if fused else "gate_up + SwiGLU GEMV, down "
+                                                       "GEMV, combine)"),
                          "bytes_per_step": nbytes},
             "cpu_baseline": cpu, "e2e": e2e, "clocks": clk, "gpu_launches": work.launches_per_step * args.steps,
         }
@@ -1542,6 +1551,9 @@ def main():
                     help="tokens (M / T); spell it --rows under torchrun, which claims --m")
     ap.add_argument("--allreduce", default="peer", choices=["peer", "nccl"],
                     help="qwen2.5-32b at N>1: the row-parallel all-reduce (peer-memory kernel or NCCL)")
+    ap.add_argument("--moe-fused", type=int, default=1, choices=[0, 1],
+                    help="moe: the expert FFN as one persistent launch (1, default) or three launches (0); "
+                         "onpu_moe_set_fused")
     ap.add_argument("--ep", default="gather", choices=["gather", "a2a"],
                     help="moe at N>1: all-gather + reduce-scatter (graph-captured) or all-to-all dispatch/combine")
     ap.add_argument("--no-e2e", action="store_true")

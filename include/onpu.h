@@ -236,11 +236,18 @@ void *onpu_ffn_new_int4(int64_t Ng, int64_t Kg, int64_t Nd, int64_t Kd, int64_t 
  * (llama/ggml-opennpu/onpu_api.cpp:261-278). 0 ok, < 0 error. */
 int onpu_moe_ffn_dev(void *ffn, const void *x, int64_t ldx, int64_t T, const int32_t *ids, const float *w, int k,
                      float *y, int64_t ldy, void *stream);
-/* The whole MoE layer in four launches: the router (bf16 wr [E][H], H = the FFN's hidden size;
- * k, norm as in onpu_route_dev) writes ids [T][k] / w [T][k] and, in its last CTA, the expert job
- * lists; then the gate_up and down grouped GEMVs and the combine, as onpu_moe_ffn_dev. Same results
- * as onpu_route_dev followed by onpu_moe_ffn_dev (reference.py:71-84), one launch fewer.
- * 0 ok, < 0 error. */
+/* How onpu_moe_ffn_dev, onpu_moe_ffn_dev_ep and onpu_moe_layer_dev run the expert FFN (no
+ * reference counterpart; the reference's onpu_ffn_run is one NPU dispatch, onpu_api.cpp:423-496):
+ * 1 (default) as ONE persistent launch (gate_up + SwiGLU, down and the combine, grid barriers
+ * between them) whenever both banks share a format; 0 as three launches (gate_up grouped GEMV with
+ * SwiGLU, down grouped GEMV, combine). Both compute the same exact products in fp32; where the
+ * three-launch form splits a row group between CTAs its sums may differ from the persistent
+ * kernel's in the last bits. Returns the previous mode, or -1 for a mode other than 0 or 1. */
+int onpu_moe_set_fused(int mode);
+/* The whole MoE layer: the router (bf16 wr [E][H], H = the FFN's hidden size; k, norm as in
+ * onpu_route_dev) writes ids [T][k] / w [T][k] and, in its last CTA, the expert job lists; then
+ * the expert FFN as onpu_moe_ffn_dev. Same results as onpu_route_dev followed by
+ * onpu_moe_ffn_dev (reference.py:71-84), one launch fewer. 0 ok, < 0 error. */
 int onpu_moe_layer_dev(void *ffn, const void *wr, const void *x, int64_t ldx, int64_t T, int k, int norm, int32_t *ids,
                        float *w, float *y, int64_t ldy, void *stream);
 /* Expert parallelism: the same layer when this FFN holds only experts e0 .. e0 + E - 1 of a larger

@@ -114,6 +114,40 @@ struct ExpertJobsParams {
 };
 cudaError_t expert_jobs_launch(const ExpertJobsParams &p, cudaStream_t stream);
 
+// The routed-expert FFN in one persistent launch (moe_ffn.cu): gate/up + SwiGLU (fp32), down and
+// the weighted combine over the job lists the router kernel built. One resident wave of CTAs.
+struct MoeFfnFused {
+    int fmt;                          // kFmtQ4S / kFmtQ4F16 / kFmtQ4NX (both banks)
+    const GemvJob *jobs_gu, *jobs_dn; // device job lists (expert_jobs_launch / route_launch)
+    const int *njobs;                 // device: jobs in each list
+    int rg_gu, ch_gu, N_gu, K_gu;     // gate/up bank: row groups, 64-K chunks, rows, K
+    int rg_dn, ch_dn, N_dn, K_dn;     // down bank
+    const uint16_t *x;                // bf16 token rows
+    int64_t ldx;
+    float *af;                        // [T*k][K_dn] SwiGLU outputs (scratch)
+    float *o;                         // [T*k][N_dn] expert outputs (scratch)
+    const int32_t *ids;               // [T][k] expert ids
+    const float *w;                   // [T][k] routing weights
+    int64_t T;
+    int k;
+    int id_lo, id_hi;                 // slots whose expert id lies in [id_lo, id_hi) are combined
+    float *y;                         // [T][N_dn] fp32, row stride ldy
+    int64_t ldy;
+    unsigned *bar;                    // 3 counters, zero before the first launch (left zero)
+    int *err;
+    int workers;                      // CTAs: one resident wave
+    int mslots_gu, mslots_dn;         // staged rows: tokens per job, twice that (fp32 halves)
+    int xstride_gu, xstride_dn;       // resident activation row strides
+    int off_bar;                      // shared-memory offset of the mbarriers
+    uint32_t mul[4];                  // 2^28, 2^24, 2^20, 2^16 (as in GemvParams)
+    uint32_t unpk[3];                 // 0x000F000F, 0x00F000F0, 0x64006400
+};
+// dynamic shared memory of the fused FFN kernel, and its layout (mbarrier offset, row strides)
+int moe_ffn_fused_smem(int fmt, int mslots_gu, int K_gu, int mslots_dn, int K_dn, int *off_bar, int *xstride_gu,
+                       int *xstride_dn);
+int moe_ffn_fused_ctas_per_sm(int fmt, int smem);
+cudaError_t moe_ffn_fused_launch(const MoeFfnFused &p, int smem, cudaStream_t stream);
+
 // logits: fp32 [T][E] (output or scratch); counters: route_counter_slots(T) words, zero before the
 // first launch and left zero by every launch
 // jobs (optional): the last token block to finish also builds the expert job lists (as

@@ -93,6 +93,7 @@ SIGNATURES = {
     "onpu_moe_ffn_dev": (I32, [P, P, I64, I64, P, P, I32, P, I64, P]),
     "onpu_moe_ffn_dev_ep": (I32, [P, P, I64, I64, P, P, I32, I64, P, I64, P]),
     "onpu_moe_layer_dev": (I32, [P, P, P, I64, I64, I32, I32, P, P, P, I64, P]),
+    "onpu_moe_set_fused": (I32, [I32]),
     "onpu_comm_new": (P, [I32, I32, I64]),
     "onpu_comm_ipc_handle": (I32, [P, P]),
     "onpu_comm_open": (I32, [P, P]),

@@ -234,6 +234,106 @@ def test_moe_ffn_dev_is_deterministic(config4):
     assert torch.equal(a, b)
 
 
+# ------------------------------------------------------------------ one persistent launch
+@pytest.fixture
+def fused_mode():
+    """Set onpu_moe_set_fused for one test (0: three launches, 1: the persistent kernel)."""
+    lib = L.load()
+    prev = []
+
+    def set_mode(m):
+        old = lib.onpu_moe_set_fused(m)
+        assert old >= 0, L.last_error()
+        if not prev:
+            prev.append(old)
+    yield set_mode
+    if prev:
+        lib.onpu_moe_set_fused(prev[0])
+
+
+@pytest.mark.parametrize("mode", [0, 1])
+@pytest.mark.parametrize("T", [1, 16, 64])
+def test_moe_ffn_both_forms_match_oracle(config4, fused_mode, mode, T):
+    """The expert FFN as three launches (mode 0) and as one persistent launch (mode 1) against the
+    unmodified oracle at config 4's shapes."""
+    fused_mode(mode)
+    ffn, gq, gs, dq, ds = config4
+    g = torch.Generator(device="cuda").manual_seed(300 + T)
+    x = torch.randn(T, ffn.H, device="cuda", generator=g).to(torch.bfloat16)
+    wr = (torch.randn(ffn.E, ffn.H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    ids, w = route(x, wr, 8)
+    y = ffn(x, ids, w)
+    torch.cuda.synchronize()
+    L.check(L.load().onpu_check_device(), "device status")
+    ref = _ffn_oracle(x.float().cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy(), gq, gs, dq, ds)
+    _assert_close(y.cpu().numpy(), ref)
+
+
+def test_moe_fused_agrees_with_three_launches(config4, fused_mode):
+    """The same products in fp32 either way: the outputs agree to the last bits a split row
+    group's summation order can change."""
+    ffn = config4[0]
+    g = torch.Generator(device="cuda").manual_seed(41)
+    x = torch.randn(16, ffn.H, device="cuda", generator=g).to(torch.bfloat16)
+    wr = (torch.randn(ffn.E, ffn.H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    ids, w = route(x, wr, 8)
+    fused_mode(0)
+    a = ffn(x, ids, w)
+    fused_mode(1)
+    b = ffn(x, ids, w)
+    c = ffn(x, ids, w)
+    torch.cuda.synchronize()
+    assert torch.equal(b, c)                                  # deterministic
+    assert ((a - b).norm() / a.norm()).item() <= 1e-6
+
+
+def test_moe_fused_skewed_routing_and_graph_replay(config4, fused_mode):
+    """The persistent kernel with several jobs per expert (every token on the same 8 experts, one
+    expert chosen once) checked against the oracle, then the router + FFN captured in one CUDA
+    graph and replayed: its grid-barrier counters return to zero after every launch."""
+    fused_mode(1)
+    ffn, gq, gs, dq, ds = config4
+    T, k = 40, 8
+    g = torch.Generator(device="cuda").manual_seed(6)
+    x = torch.randn(T, ffn.H, device="cuda", generator=g).to(torch.bfloat16)
+    ids = torch.arange(8, dtype=torch.int32, device="cuda").repeat(T, 1) * 3
+    ids[7, 7] = 127
+    w = torch.rand(T, k, device="cuda", generator=g)
+    w = (w / w.sum(-1, keepdim=True)).contiguous()
+    y = ffn(x, ids, w)
+    torch.cuda.synchronize()
+    ref = _ffn_oracle(x.float().cpu().numpy(), ids.cpu().numpy(), w.cpu().numpy(), gq, gs, dq, ds)
+    _assert_close(y.cpu().numpy(), ref)
+
+    T = 8
+    x = torch.randn(T, ffn.H, device="cuda", generator=g).to(torch.bfloat16)
+    wr = (torch.randn(ffn.E, ffn.H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    s = torch.cuda.Stream()
+    yl = torch.empty(T, ffn.H, device="cuda")
+    with torch.cuda.stream(s):
+        _, il, wl = ffn.layer(x, wr, 8, out=yl, stream=s)
+    s.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=s):
+        ffn.layer(x, wr, 8, out=yl, ids=il, w=wl, stream=s)
+    for _ in range(3):
+        x.copy_(torch.randn(T, ffn.H, device="cuda", generator=g).to(torch.bfloat16))
+        graph.replay()
+        torch.cuda.synchronize()
+        ri, rw = route(x, wr, 8)
+        ref = _ffn_oracle(x.float().cpu().numpy(), ri.cpu().numpy(), rw.cpu().numpy(), gq, gs, dq, ds)
+        assert torch.equal(il, ri)
+        _assert_close(yl.cpu().numpy(), ref)
+    del graph
+    assert L.load().onpu_check_device() == 0, L.last_error()
+
+
+def test_moe_set_fused_rejects_bad_modes():
+    lib = L.load()
+    assert lib.onpu_moe_set_fused(2) == -1 and lib.onpu_moe_set_fused(-1) == -1
+    assert "mode" in L.last_error()
+
+
 # ------------------------------------------------------------------ expert parallelism
 @pytest.mark.parametrize("world", [2, 4])
 def test_moe_ffn_expert_shards_sum_to_the_full_layer(world):
