@@ -130,12 +130,18 @@ __device__ __forceinline__ void consume_phase(const MoeFfnFused &p, uint8_t *sme
             }
             if (!failed) {
                 const uint32_t wsb = wring + slot * STAGE_W + s * SB;
-                for (int ci = 0; ci < n; ++ci) {
+                auto chunk = [&](int ci) {
                     const int kcc = c0 + ci;
                     uint32_t xa[NT];
 #pragma unroll
                     for (int nt = 0; nt < NT; ++nt) xa[nt] = xrb[nt] + kcc * xkm[nt];
                     strip_chunk_h<FMT, NT>(wsb + ci * CB, xa, ctab + kcc * tab_chunk_bytes(NT), lane, r, mul, u, acc);
+                };
+                if (n == kCPS) {                      // a full stage: unrolled, so the chunks' chains overlap
+#pragma unroll
+                    for (int ci = 0; ci < kCPS; ++ci) chunk(ci);
+                } else {
+                    for (int ci = 0; ci < n; ++ci) chunk(ci);
                 }
             }
             __syncwarp();

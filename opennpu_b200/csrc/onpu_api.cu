@@ -1589,8 +1589,8 @@ struct RouteSpec {
 
 // Whether a layer's expert FFN runs as one persistent launch (moe_ffn.cu) instead of gate/up,
 // down and combine launches: both banks in one format and the kernel's layout resident. Measured
-// on a B200 at config 4's shapes (48 layers, CUDA graph): 35.4 -> 30.0 us a layer at T = 1,
-// 74.8 -> 67.8 at T = 8, 98.8 -> 93.5 at T = 16, 144.7 -> 143.4 at T = 64.
+// on a B200 at config 4's shapes (48 layers, CUDA graph): 35.4 -> 29.4 us a layer at T = 1,
+// 98.8 -> 88.9 at T = 16, 144.7 -> 136.0 at T = 64.
 bool moe_fused_path(Ctx &c, const GpuMat &gu, const GpuMat &dn, int per_job) {
     if (c.moe_fused == 0 || gu.gm.fmt != dn.gm.fmt) return false;
     const int smem = moe_ffn_fused_smem(gu.gm.fmt, per_job, static_cast<int>(gu.gm.K), 2 * per_job,
