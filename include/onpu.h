@@ -349,7 +349,8 @@ int onpu_dense_unpack_dev(void *h, uint8_t *q, uint16_t *scales, uint16_t *mins,
 /* ---- the ggml-opennpu backend's operator layer (llama/ggml-opennpu/ggml-opennpu.cpp:270-539,
  * 703-753) over this library: which MUL_MAT / MUL_MAT_ID nodes it takes, their tensor layouts,
  * and the learned sibling fusion. Tensors are described by the ggml_tensor fields the layer
- * reads; the ggml_backend_* registration around it needs llama.cpp's headers. */
+ * reads; the ggml_backend_* registration around it is llama.cpp code (it needs llama.cpp's
+ * headers) and calls these entry points from its supports_op and graph_compute callbacks. */
 typedef struct onpu_ggml_tensor {
     int32_t type;            /* ggml type id: F32 0, F16 1, Q4_0 2, Q4_K 12, I32 26, BF16 30 */
     int32_t weights;         /* non-zero: the tensor lives in a weights buffer */
