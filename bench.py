@@ -789,8 +789,11 @@ SWIGLU_UNIT_GAIN = 1.269
 def tp_layer0_parity(work, rank):
     """One layer of the timed stack against the oracle: layer 0's weights drawn again from the
     stack's seed, dequantised per 32 on the host and multiplied in float64 (reference.py:24-28,
-    :55-57, :84 semantics; o takes q's output as the attention stand-in). At one rank the whole
-    layer (all-reduced output) is checked; with more ranks, this rank's q/k/v shard."""
+    :55-57, :84 semantics; o takes q's output as the attention stand-in). At one rank with fp32
+    activations between the projections the whole layer (all-reduced output) is checked; with
+    more ranks, or with bf16 activations (rows that do not fit the fp32 staging), this rank's
+    q/k/v shard: the reference's fp32 chain rounds nothing between the projections, and bf16
+    roundings there are the engine's choice, not the kernel's arithmetic."""
     gen = torch.Generator(device="cuda")
     gen.manual_seed(work.seed)
     mats = [gen_int4_cuda(N, K, gen, gain=g, k_full=kf) for N, K, g, kf in work.gen_args]
@@ -811,7 +814,7 @@ def tp_layer0_parity(work, rank):
         return torch.cat(out, 1)
 
     xd = x.double().cpu()
-    if work.world == 1:
+    if work.world == 1 and work.f32:
         y = lay(x, b).double().cpu()
         torch.cuda.synchronize()
         q = mm(xd, *mats[0])[:, :lay.nq]

@@ -598,14 +598,14 @@ int occ_fmt(int nt, int smem) {
 
 }  // namespace
 
-GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks) {
+GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks, int64_t budget) {
     GemvLayout L{};
     const int chunks = static_cast<int>((K + kChunkK - 1) / kChunkK);
     if (wchunks <= 0 || wchunks > chunks) wchunks = chunks;
     const int64_t xstride = xres_stride(static_cast<int64_t>(wchunks) * kChunkK);
     // rows, zero block, table, scales
     const int64_t res_bytes = xres_bytes(mrows, static_cast<int64_t>(wchunks) * kChunkK, mrows > 8 ? 2 : 1, xstride);
-    L.xres = res_bytes <= kResidentXBudget;       // several jobs: staged again per job
+    L.xres = res_bytes <= budget;                 // several jobs: staged again per job
     L.wchunks = wchunks;
     L.xstride = static_cast<int>(xstride);
     L.ctab_off = static_cast<int>(mrows * xstride + 128);

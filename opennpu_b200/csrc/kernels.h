@@ -13,6 +13,9 @@ namespace onpu_b200 {
 // Activations of a single-job launch stay resident in shared memory when they take at most this
 // many bytes (tokens x padded K x 2 B); otherwise every stage carries its own slice.
 constexpr int64_t kResidentXBudget = 40 * 1024;
+// A one-job launch whose rows do not fit that budget (5..16 rows of a long K) may instead run one
+// CTA per SM with up to this many bytes of resident rows (the ring takes the rest of the 227 KB)
+constexpr int64_t kWideResidentXBudget = 136 * 1024;
 
 struct GemvLayout {
     int xres;          // activations resident
@@ -25,7 +28,7 @@ struct GemvLayout {
 };
 // mrows: activation rows of the largest job (twice its tokens for fp32 split activations);
 // wchunks: chunks of K each resident row holds (0 = all of K)
-GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks = 0);
+GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks = 0, int64_t budget = kResidentXBudget);
 // true when jobs of up to mrows activation rows stay resident (fp16 path) for this K
 bool gemv_resident(int mrows, int64_t K);
 int gemv_ctas_per_sm(int fmt, int ntiles, int smem);

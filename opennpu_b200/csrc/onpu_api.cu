@@ -282,6 +282,24 @@ GemvPlan plan_gemv(const Ctx &c, const GpuMatrix &gm, int njobs, int mrows, bool
             }
         }
     }
+    if (njobs == 1 && !device_count && !pl.lay.xres) {
+        // the rows do not fit beside two CTAs' rings (5..16 rows of a long K): one CTA per SM with
+        // the rows resident (all of K, or the CTA's window of it) instead of a slice of every row
+        // per stage. The tokens already share each MMA's 8 (16) columns, so the math per chunk is
+        // the one-row launch's; the staged rows are what grows.
+        for (int per_sm = 2; per_sm >= 1; --per_sm) {
+            const int Wb = align_workers(std::min(c.nsm * per_sm, T), 1, gm.row_groups);
+            const int len = (T + Wb - 1) / Wb;
+            const GemvLayout lw =
+                gemv_layout(gm.fmt, mrows, gm.K, len < gm.chunks ? len : 0, kWideResidentXBudget);
+            if (lw.xres && c.nsm * gemv_ctas_per_sm(gm.fmt, pl.ntiles, lw.smem) >= Wb) {
+                pl.lay = lw;
+                pl.kwin = len < gm.chunks;
+                pl.workers = Wb;
+                break;
+            }
+        }
+    }
     return pl;
 }
 
