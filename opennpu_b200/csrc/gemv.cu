@@ -49,6 +49,9 @@ namespace {
 
 using namespace gemv_core;
 
+constexpr int kBarRegion = 2 * kNS * 8;          // full + empty mbarriers of the finest ring (4-chunk stages)
+constexpr int kWideStageChunks = 32;             // chunks per CTA from which a launch takes 8-chunk stages
+
 
 // Store the finished sums of strip rows r (v_lo) and r+8 (v_hi) of one token (output row yr).
 // call: kEpiPeer's all-reduce call number of this CTA.
@@ -126,9 +129,10 @@ __device__ void peer_receive(const GemvParams &p, int lo, int hi, uint32_t call,
 
 // XS: fp32 activations staged as two fp16 rows per token (resident only); a template parameter so
 // the bf16 kernels keep their register allocation
-template <int FMT, int NT, int EPI, bool CI, bool XS>
+template <int FMT, int NT, int EPI, bool CI, bool XS, int CPS>
 __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams p) {
-    constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT), STAGE_W = stage_w_bytes(FMT);
+    constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT), STAGE_W = CPS * CB;
+    constexpr int NS = kCPS * kNS / CPS;              // ring stages: the same 32 chunks either way
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int W = p.workers, cta = blockIdx.x;
@@ -142,19 +146,19 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     const int lo = static_cast<int>(static_cast<int64_t>(cta) * T / W);
     const int hi = static_cast<int>(static_cast<int64_t>(cta + 1) * T / W);
     if (lo >= hi) return;      // no chunks (a device-side job count below the grid, or zero jobs)
-    const int nst = (hi - lo + kCPS - 1) / kCPS;
+    const int nst = (hi - lo + CPS - 1) / CPS;
     const int per_job = p.row_groups * p.chunks;
     constexpr bool xres = CI;                         // resident activations carry the offset table
-    const int xchunk = p.xslots * kXSlot, xstage_bytes = kCPS * xchunk;   // per-stage activation layout
+    const int xchunk = p.xslots * kXSlot, xstage_bytes = CPS * xchunk;   // per-stage activation layout
     const uint32_t sbase = smem_u32(smem);
-    const uint32_t wring = sbase, xregion = sbase + kNS * STAGE_W;
-    const uint32_t full = sbase + p.off_bar, empty = full + kNS * 8;
+    const uint32_t wring = sbase, xregion = sbase + NS * STAGE_W;
+    const uint32_t full = sbase + p.off_bar, empty = full + NS * 8;
 
     if (!xres)   // the zero slot is never written; a chunk half past K gets a 64-B copy only
-        for (int e = threadIdx.x; e < kNS * xstage_bytes / 16; e += blockDim.x)
-            *reinterpret_cast<uint4 *>(smem + kNS * STAGE_W + e * 16) = make_uint4(0, 0, 0, 0);
+        for (int e = threadIdx.x; e < NS * xstage_bytes / 16; e += blockDim.x)
+            *reinterpret_cast<uint4 *>(smem + NS * STAGE_W + e * 16) = make_uint4(0, 0, 0, 0);
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kNS; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(full + s * 8, xres ? 1 : 2);   // weights arrival (+ activations arrival)
             mbar_init(empty + s * 8, kConsumers);
         }
@@ -168,10 +172,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         const uint8_t *wbase = p.jobs_ready ? p.jobs[wj].w : nullptr;
         const uint64_t wpol = l2_evict_first_policy();   // weights are read once per launch
         auto issue_weights = [&](int st) {            // lane 0 only
-            const int c0 = lo + st * kCPS, c1 = min(hi, c0 + kCPS);
-            const uint32_t bar = full + (st % kNS) * 8;
+            const int c0 = lo + st * CPS, c1 = min(hi, c0 + CPS);
+            const uint32_t bar = full + (st % NS) * 8;
             mbar_arrive_expect_tx(bar, static_cast<uint32_t>((c1 - c0) * CB));
-            uint32_t dst = wring + (st % kNS) * STAGE_W;
+            uint32_t dst = wring + (st % NS) * STAGE_W;
             int c = c0;
             while (c < c1) {                          // one copy per run of chunks within a job
                 if (c >= (wj + 1) * per_job) wbase = p.jobs[++wj].w;
@@ -182,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
                 c = run_end;
             }
         };
-        const int npro = min(kNS, nst);
+        const int npro = min(NS, nst);
         if (lane == 0 && p.jobs_ready)
             for (int st = 0; st < npro; ++st) issue_weights(st);
         if (trace && lane == 0) trace[1] = global_timer_ns();
@@ -199,9 +203,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         int xm = p.jobs[cj].m, xrow = p.jobs[cj].xrow[lane & 15];
         bool failed = false;
         for (int st = 0; st < nst; ++st) {
-            const int slot = st % kNS;
-            if (st >= kNS) {
-                if (!failed && !mbar_wait_bounded(empty + slot * 8, ((st / kNS) - 1) & 1, kWaitLimitNs)) {
+            const int slot = st % NS;
+            if (st >= NS) {
+                if (!failed && !mbar_wait_bounded(empty + slot * 8, ((st / NS) - 1) & 1, kWaitLimitNs)) {
                     failed = true;
                     if (lane == 0) atomicOr(p.err, 2);
                 }
@@ -211,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
             if (xres) continue;
             // activations of this stage: per chunk one 128-B copy per token (64 B when the chunk's
             // second group lies past K); the byte total is announced first
-            const int c0 = lo + st * kCPS, c1 = min(hi, c0 + kCPS);
+            const int c0 = lo + st * CPS, c1 = min(hi, c0 + CPS);
             uint32_t xbytes = 0;
             {
                 int jj = cj, kk = ckc, mm = xm;
@@ -246,8 +250,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
 
     // ================================================================ consumers (strip s = warp)
     const int s = warp, r = lane >> 2, t = lane & 3;
-    volatile int *flag = reinterpret_cast<volatile int *>(smem + p.off_bar + 2 * kNS * 8);
-    int *s_xrow = reinterpret_cast<int *>(smem + p.off_bar + 2 * kNS * 8 + 16);   // the staged job's rows
+    volatile int *flag = reinterpret_cast<volatile int *>(smem + p.off_bar + kBarRegion);
+    int *s_xrow = reinterpret_cast<int *>(smem + p.off_bar + kBarRegion + 16);   // the staged job's rows
     int j = lo / per_job;
     int g = (lo - j * per_job) / p.chunks;
     int kc = lo - j * per_job - g * p.chunks;
@@ -282,10 +286,10 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         constexpr int SU = decltype(su)::value;
         if constexpr (XS)
             stage_activations<FMT, NT, false, true, SU>(p.xf, p.ldx, row_of, mj, mslots, p.K, kc0, nch, p.wchunks,
-                                                        p.xstride, smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
+                                                        p.xstride, smem + NS * STAGE_W, threadIdx.x, kConsumers * 32);
         else
             stage_activations<FMT, NT, false, false, SU>(p.x, p.ldx, row_of, mj, mslots, p.K, kc0, nch, p.wchunks,
-                                                         p.xstride, smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
+                                                         p.xstride, smem + NS * STAGE_W, threadIdx.x, kConsumers * 32);
     };
     if (xres) stage(m, std::integral_constant<int, 4>{});
     if (tr) trace[3] = global_timer_ns();
@@ -296,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
         if (threadIdx.x < kMaxTokensPerJob) s_xrow[threadIdx.x] = p.jobs[jj].xrow[threadIdx.x];
         stage(p.jobs[jj].m, std::integral_constant<int, 1>{});
     };
-    const float *tscale = reinterpret_cast<const float *>(smem + kNS * STAGE_W + p.ctab_off +
+    const float *tscale = reinterpret_cast<const float *>(smem + NS * STAGE_W + p.ctab_off +
                                                           p.wchunks * tab_chunk_bytes(NT));
 
     // m counts activation rows (MMA columns): the job's tokens, twice that when split (rows 2n and
@@ -463,9 +467,9 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
 
     bool failed = false;
     for (int st = 0; st < nst; ++st) {
-        const int slot = st % kNS;
+        const int slot = st % NS;
         const uint64_t tw = tr ? global_timer_ns() : 0;
-        if (!failed && !mbar_wait_bounded(full + slot * 8, (st / kNS) & 1, kWaitLimitNs)) {
+        if (!failed && !mbar_wait_bounded(full + slot * 8, (st / NS) & 1, kWaitLimitNs)) {
             failed = true;
             if (lane == 0) atomicOr(p.err, 1);
         }
@@ -474,23 +478,23 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
             waited += now - tw;
             if (st == 0) trace[4] = now;
         }
-        const int c0 = lo + st * kCPS, n = min(hi - c0, kCPS);
+        const int c0 = lo + st * CPS, n = min(hi - c0, CPS);
         const uint32_t wsb = wring + slot * STAGE_W + s * SB, xstage = slot * xstage_bytes;
         // after a timed-out wait (failed is per thread) only the math is skipped: the bookkeeping
         // and every named barrier in flush() stay the same in all consumer threads
         // resident activations of chunk c sit at window chunk c - lo (kwin) or at its k chunk
-        if (n == kCPS && kc + kCPS < p.chunks) {
+        if (n == CPS && kc + CPS < p.chunks) {
             // the common case: a full stage inside one row group
             if (!failed) {
                 const int xb = win ? c0 - lo : kc;
 #pragma unroll
-                for (int ci = 0; ci < kCPS; ++ci) {
+                for (int ci = 0; ci < CPS; ++ci) {
                     uint32_t xa[NT];
                     xaddr(xa, xstage, ci, xb + ci);
                     chunk_math(wsb + ci * CB, xa, xb + ci);
                 }
             }
-            kc += kCPS;
+            kc += CPS;
         } else {
             for (int ci = 0; ci < n; ++ci) {
                 if (!failed) {
@@ -520,20 +524,20 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_int4_kernel(const GemvParams
     }
 }
 
-template <int FMT, int NT, int EPI, bool CI, bool XS>
+template <int FMT, int NT, int EPI, bool CI, bool XS, int CPS>
 struct GemvKernel {
     static void prepare() {
         static bool done = false;
         if (!done) {
             done = true;
-            cudaFuncSetAttribute(gemv_int4_kernel<FMT, NT, EPI, CI, XS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(gemv_int4_kernel<FMT, NT, EPI, CI, XS, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  227 * 1024);
         }
     }
     static int occupancy(int smem) {
         prepare();
         int o = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_int4_kernel<FMT, NT, EPI, CI, XS>, kThreads,
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, gemv_int4_kernel<FMT, NT, EPI, CI, XS, CPS>, kThreads,
                                                           smem) != cudaSuccess)
             o = 1;
         return o > 0 ? o : 1;
@@ -550,50 +554,57 @@ struct GemvKernel {
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = pdl ? 1 : 0;
-        return cudaLaunchKernelEx(&cfg, gemv_int4_kernel<FMT, NT, EPI, CI, XS>, p);
+        return cudaLaunchKernelEx(&cfg, gemv_int4_kernel<FMT, NT, EPI, CI, XS, CPS>, p);
     }
 };
 
-template <int FMT, int NT, bool CI>
+template <int FMT, int NT, bool CI, int CPS>
 cudaError_t dispatch_epi_ci(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
     switch (epi) {
-        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, CI, false>::launch(p, smem, s, pdl);
-        case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16, CI, false>::launch(p, smem, s, pdl);
-        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, CI, false>::launch(p, smem, s, pdl);
-        case kEpiPairSum: return GemvKernel<FMT, NT, kEpiPairSum, CI, false>::launch(p, smem, s, pdl);
-        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, CI, false>::launch(p, smem, s, pdl);
+        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, CI, false, CPS>::launch(p, smem, s, pdl);
+        case kEpiBF16: return GemvKernel<FMT, NT, kEpiBF16, CI, false, CPS>::launch(p, smem, s, pdl);
+        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, CI, false, CPS>::launch(p, smem, s, pdl);
+        case kEpiPairSum: return GemvKernel<FMT, NT, kEpiPairSum, CI, false, CPS>::launch(p, smem, s, pdl);
+        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, CI, false, CPS>::launch(p, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
 
 // fp32 (split) activations: the epilogues of the projections that take them (a down or o
 // projection, a gate/up fed by one, a row-parallel projection); resident activations only
-template <int FMT, int NT>
+template <int FMT, int NT, int CPS>
 cudaError_t dispatch_split(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
     switch (epi) {
-        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, true, true>::launch(p, smem, s, pdl);
-        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, true, true>::launch(p, smem, s, pdl);
-        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, true, true>::launch(p, smem, s, pdl);
+        case kEpiF32: return GemvKernel<FMT, NT, kEpiF32, true, true, CPS>::launch(p, smem, s, pdl);
+        case kEpiSwiGLU: return GemvKernel<FMT, NT, kEpiSwiGLU, true, true, CPS>::launch(p, smem, s, pdl);
+        case kEpiPeer: return GemvKernel<FMT, NT, kEpiPeer, true, true, CPS>::launch(p, smem, s, pdl);
         default: return cudaErrorInvalidValue;
     }
 }
 
-template <int FMT, int NT>
+template <int FMT, int NT, int CPS>
 cudaError_t dispatch_epi(int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
-    if (p.xsplit) return p.xres ? dispatch_split<FMT, NT>(epi, p, smem, s, pdl) : cudaErrorInvalidValue;
-    return p.xres ? dispatch_epi_ci<FMT, NT, true>(epi, p, smem, s, pdl)
-                  : dispatch_epi_ci<FMT, NT, false>(epi, p, smem, s, pdl);
+    if (p.xsplit) return p.xres ? dispatch_split<FMT, NT, CPS>(epi, p, smem, s, pdl) : cudaErrorInvalidValue;
+    return p.xres ? dispatch_epi_ci<FMT, NT, true, CPS>(epi, p, smem, s, pdl)
+                  : dispatch_epi_ci<FMT, NT, false, CPS>(epi, p, smem, s, pdl);
 }
 
+// Stages of 8 chunks for launches whose CTAs stream long ranges (more independent chunk chains
+// per consumer warp between ring waits: the 32B gate/up launch 3826 -> 4233 GB/s), of 4 chunks for
+// short ranges and device-counted (expert) launches, whose ring fills and drains dominate
 template <int FMT>
 cudaError_t dispatch_nt(int nt, int epi, const GemvParams &p, int smem, cudaStream_t s, bool pdl) {
-    return nt == 1 ? dispatch_epi<FMT, 1>(epi, p, smem, s, pdl) : dispatch_epi<FMT, 2>(epi, p, smem, s, pdl);
+    const bool wide = !p.njobs_dev && p.workers > 0 && (p.total_chunks + p.workers - 1) / p.workers >= kWideStageChunks;
+    if (wide)
+        return nt == 1 ? dispatch_epi<FMT, 1, 2 * kCPS>(epi, p, smem, s, pdl)
+                       : dispatch_epi<FMT, 2, 2 * kCPS>(epi, p, smem, s, pdl);
+    return nt == 1 ? dispatch_epi<FMT, 1, kCPS>(epi, p, smem, s, pdl) : dispatch_epi<FMT, 2, kCPS>(epi, p, smem, s, pdl);
 }
 
 template <int FMT>
 int occ_fmt(int nt, int smem) {
-    return nt == 1 ? GemvKernel<FMT, 1, kEpiF32, true, false>::occupancy(smem)
-                   : GemvKernel<FMT, 2, kEpiF32, true, false>::occupancy(smem);
+    return nt == 1 ? GemvKernel<FMT, 1, kEpiF32, true, false, kCPS>::occupancy(smem)
+                   : GemvKernel<FMT, 2, kEpiF32, true, false, kCPS>::occupancy(smem);
 }
 
 }  // namespace
@@ -612,7 +623,7 @@ GemvLayout gemv_layout(int fmt, int mrows, int64_t K, int wchunks, int64_t budge
     L.xslots = mrows + 1;
     const int64_t xbytes = L.xres ? res_bytes : static_cast<int64_t>(kNS) * kCPS * L.xslots * kXSlot;
     L.off_bar = static_cast<int>(kNS * stage_w_bytes(fmt) + (xbytes + 15) / 16 * 16);
-    L.smem = L.off_bar + 2 * kNS * 8 + 16 + kMaxTokensPerJob * 4;   // mbarriers, flag, staged job's rows
+    L.smem = L.off_bar + kBarRegion + 16 + kMaxTokensPerJob * 4;   // mbarriers, flag, staged job's rows
     return L;
 }
 
