@@ -40,6 +40,8 @@ namespace {
 using namespace gemv_core;
 
 constexpr int kCombineThreads = kConsumers * 32;
+constexpr int kBarRegion = 2 * kNS * 8;             // full + empty mbarriers of the finest ring
+constexpr int64_t kWideStageSlots = 128;            // routed slots (T * k) from which stages hold 8 chunks
 
 // bounded wait until the barrier counter reaches `target`; false (and err |= 4) after the limit
 __device__ __forceinline__ bool grid_wait(const unsigned *ctr, unsigned target, int *err) {
@@ -58,9 +60,10 @@ __device__ __forceinline__ bool grid_wait(const unsigned *ctr, unsigned target, 
 // activations staged as two fp16 rows per token (down), else bf16 (gate/up). st: the ring stage
 // counter, shared with the producer's order. EPI_SWIGLU: out[yrow][g*32 + s*8 + r] =
 // silu(rows r) * rows r+8 (the interleaved gate/up layout); else out[yrow][row].
-template <int FMT, int NT, bool SPLIT, bool SWIGLU>
+template <int FMT, int NT, bool SPLIT, bool SWIGLU, int CPS>
 __device__ __forceinline__ void consume_phase(const MoeFfnFused &p, uint8_t *smem, int nj, int &st, bool &failed) {
-    constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT), STAGE_W = stage_w_bytes(FMT);
+    constexpr int CB = chunk_bytes(FMT), SB = strip_bytes(FMT), STAGE_W = CPS * CB;
+    constexpr int NS = kCPS * kNS / CPS;              // ring stages: the same 32 chunks either way
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, s = warp, r = lane >> 2, t = lane & 3;
     const int W = p.workers;
     const GemvJob *jobs = SWIGLU ? p.jobs_gu : p.jobs_dn;
@@ -69,13 +72,13 @@ __device__ __forceinline__ void consume_phase(const MoeFfnFused &p, uint8_t *sme
     const int mslots = SWIGLU ? p.mslots_gu : p.mslots_dn, xstride = SWIGLU ? p.xstride_gu : p.xstride_dn;
     float *out = SWIGLU ? p.af : p.o;
     const int64_t ldo = SWIGLU ? p.K_dn : p.N_dn;
-    const uint32_t sbase = smem_u32(smem), wring = sbase, xregion = sbase + kNS * STAGE_W;
-    const uint32_t full = sbase + p.off_bar, empty = full + kNS * 8;
-    int *s_xrow = reinterpret_cast<int *>(smem + p.off_bar + 2 * kNS * 8);
+    const uint32_t sbase = smem_u32(smem), wring = sbase, xregion = sbase + NS * STAGE_W;
+    const uint32_t full = sbase + p.off_bar, empty = full + NS * 8;
+    int *s_xrow = reinterpret_cast<int *>(smem + p.off_bar + kBarRegion);
     const uint32_t mul[4] = {p.mul[0], p.mul[1], p.mul[2], p.mul[3]};
     const Unpack u{p.unpk[0], p.unpk[1], p.unpk[2]};
     const uint32_t ctab = xregion + mslots * xstride + 128 + t * 8;
-    const float *tscale = reinterpret_cast<const float *>(smem + kNS * STAGE_W + mslots * xstride + 128 +
+    const float *tscale = reinterpret_cast<const float *>(smem + NS * STAGE_W + mslots * xstride + 128 +
                                                           ch * tab_chunk_bytes(NT));
     int cur = -1, m = 0;
     uint32_t xrb[NT], xkm[NT];
@@ -93,10 +96,10 @@ __device__ __forceinline__ void consume_phase(const MoeFfnFused &p, uint8_t *sme
             auto row_of = [s_xrow](int n) { return s_xrow[n]; };
             if constexpr (SPLIT)
                 stage_activations<FMT, NT, true, true, 1>(p.af, p.K_dn, row_of, mt, mslots, K, 0, ch, ch, xstride,
-                                                          smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
+                                                          smem + NS * STAGE_W, threadIdx.x, kConsumers * 32);
             else
                 stage_activations<FMT, NT, false, false, 4>(p.x, p.ldx, row_of, mt, mslots, K, 0, ch, ch, xstride,
-                                                            smem + kNS * STAGE_W, threadIdx.x, kConsumers * 32);
+                                                            smem + NS * STAGE_W, threadIdx.x, kConsumers * 32);
             m = SPLIT ? 2 * mt : mt;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
@@ -122,9 +125,9 @@ __device__ __forceinline__ void consume_phase(const MoeFfnFused &p, uint8_t *sme
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int f = 0; f < 4; ++f) acc[nt][f] = 0.f;
-        for (int c0 = 0; c0 < ch; c0 += kCPS, ++st) {
-            const int slot = st % kNS, n = min(kCPS, ch - c0);
-            if (!failed && !mbar_wait_bounded(full + slot * 8, (st / kNS) & 1, kWaitLimitNs)) {
+        for (int c0 = 0; c0 < ch; c0 += CPS, ++st) {
+            const int slot = st % NS, n = min(CPS, ch - c0);
+            if (!failed && !mbar_wait_bounded(full + slot * 8, (st / NS) & 1, kWaitLimitNs)) {
                 failed = true;
                 if (lane == 0) atomicOr(p.err, 1);
             }
@@ -137,9 +140,9 @@ __device__ __forceinline__ void consume_phase(const MoeFfnFused &p, uint8_t *sme
                     for (int nt = 0; nt < NT; ++nt) xa[nt] = xrb[nt] + kcc * xkm[nt];
                     strip_chunk_h<FMT, NT>(wsb + ci * CB, xa, ctab + kcc * tab_chunk_bytes(NT), lane, r, mul, u, acc);
                 };
-                if (n == kCPS) {                      // a full stage: unrolled, so the chunks' chains overlap
+                if (n == CPS) {                      // a full stage: unrolled, so the chunks' chains overlap
 #pragma unroll
-                    for (int ci = 0; ci < kCPS; ++ci) chunk(ci);
+                    for (int ci = 0; ci < CPS; ++ci) chunk(ci);
                 } else {
                     for (int ci = 0; ci < n; ++ci) chunk(ci);
                 }
@@ -169,16 +172,17 @@ __device__ __forceinline__ void consume_phase(const MoeFfnFused &p, uint8_t *sme
     }
 }
 
-template <int FMT>
+template <int FMT, int CPS>
 __global__ void __launch_bounds__(kThreads, 2) moe_ffn_kernel(const MoeFfnFused p) {
-    constexpr int CB = chunk_bytes(FMT), STAGE_W = stage_w_bytes(FMT);
+    constexpr int CB = chunk_bytes(FMT), STAGE_W = CPS * CB;
+    constexpr int NS = kCPS * kNS / CPS;
     extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int W = p.workers, cta = blockIdx.x;
     const uint32_t sbase = smem_u32(smem), wring = sbase;
-    const uint32_t full = sbase + p.off_bar, empty = full + kNS * 8;
+    const uint32_t full = sbase + p.off_bar, empty = full + NS * 8;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kNS; ++s) {
+        for (int s = 0; s < NS; ++s) {
             mbar_init(full + s * 8, 1);
             mbar_init(empty + s * 8, kConsumers);
         }
@@ -204,10 +208,10 @@ __global__ void __launch_bounds__(kThreads, 2) moe_ffn_kernel(const MoeFfnFused 
                 for (int it = lo; it < hi; ++it) {
                     const int j = it / rg, g = it - j * rg;
                     const uint8_t *base = jobs[j].w + static_cast<int64_t>(g) * ch * CB;
-                    for (int c0 = 0; c0 < ch; c0 += kCPS, ++st) {
-                        const int slot = st % kNS, n = min(kCPS, ch - c0);
-                        if (st >= kNS && !failed &&
-                            !mbar_wait_bounded(empty + slot * 8, ((st / kNS) - 1) & 1, kWaitLimitNs)) {
+                    for (int c0 = 0; c0 < ch; c0 += CPS, ++st) {
+                        const int slot = st % NS, n = min(CPS, ch - c0);
+                        if (st >= NS && !failed &&
+                            !mbar_wait_bounded(empty + slot * 8, ((st / NS) - 1) & 1, kWaitLimitNs)) {
                             failed = true;
                             atomicOr(p.err, 2);
                         }
@@ -224,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 2) moe_ffn_kernel(const MoeFfnFused 
     // ================================================================ consumers
     int st = 0;
     bool failed = false;
-    consume_phase<FMT, 1, false, true>(p, smem, nj, st, failed);
+    consume_phase<FMT, 1, false, true, CPS>(p, smem, nj, st, failed);
     // grid barrier 0: every CTA's gate/up outputs are stored before any down activations are read
     named_bar_sync(1, kConsumers * 32);
     if (threadIdx.x == 0) {
@@ -233,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 2) moe_ffn_kernel(const MoeFfnFused 
         grid_wait(p.bar, static_cast<unsigned>(W), p.err);
     }
     named_bar_sync(1, kConsumers * 32);
-    consume_phase<FMT, 2, true, false>(p, smem, nj, st, failed);
+    consume_phase<FMT, 2, true, false, CPS>(p, smem, nj, st, failed);
     // grid barrier 1: every expert output is stored before the combine reads it
     named_bar_sync(1, kConsumers * 32);
     if (threadIdx.x == 0) {
@@ -271,14 +275,19 @@ __global__ void __launch_bounds__(kThreads, 2) moe_ffn_kernel(const MoeFfnFused 
     }
 }
 
-template <int FMT>
+template <int FMT, int CPS>
 struct MoeFfnKernel {
     static void prepare() {
         static bool done = false;
         if (!done) {
             done = true;
-            cudaFuncSetAttribute(moe_ffn_kernel<FMT>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            cudaFuncSetAttribute(moe_ffn_kernel<FMT, CPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         }
+    }
+    static cudaError_t launch(const MoeFfnFused &p, int smem, cudaStream_t stream) {
+        prepare();
+        return launch_pdl(moe_ffn_kernel<FMT, CPS>, dim3(static_cast<unsigned>(p.workers)), dim3(kThreads), smem,
+                          stream, p);
     }
 };
 
@@ -299,30 +308,32 @@ int moe_ffn_fused_smem(int fmt, int mslots_gu, int K_gu, int mslots_dn, int K_dn
 int moe_ffn_fused_ctas_per_sm(int fmt, int smem) {
     int o = 0;
     if (fmt == kFmtQ4S) {
-        MoeFfnKernel<kFmtQ4S>::prepare();
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, moe_ffn_kernel<kFmtQ4S>, kThreads, smem);
+        MoeFfnKernel<kFmtQ4S, kCPS>::prepare();
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, moe_ffn_kernel<kFmtQ4S, kCPS>, kThreads, smem);
     } else if (fmt == kFmtQ4F16) {
-        MoeFfnKernel<kFmtQ4F16>::prepare();
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, moe_ffn_kernel<kFmtQ4F16>, kThreads, smem);
+        MoeFfnKernel<kFmtQ4F16, kCPS>::prepare();
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, moe_ffn_kernel<kFmtQ4F16, kCPS>, kThreads, smem);
     } else {
-        MoeFfnKernel<kFmtQ4NX>::prepare();
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, moe_ffn_kernel<kFmtQ4NX>, kThreads, smem);
+        MoeFfnKernel<kFmtQ4NX, kCPS>::prepare();
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, moe_ffn_kernel<kFmtQ4NX, kCPS>, kThreads, smem);
     }
     return o;
 }
 
+// 8-chunk stages when the layer routes many slots (each CTA then streams several row groups:
+// longer unrolled chunk runs between ring waits), 4-chunk stages for few (one row group a CTA)
 cudaError_t moe_ffn_fused_launch(const MoeFfnFused &p, int smem, cudaStream_t stream) {
-    const dim3 grid(static_cast<unsigned>(p.workers)), block(kThreads);
+    const bool wide = p.T * p.k >= kWideStageSlots;
     switch (p.fmt) {
         case kFmtQ4S:
-            MoeFfnKernel<kFmtQ4S>::prepare();
-            return launch_pdl(moe_ffn_kernel<kFmtQ4S>, grid, block, smem, stream, p);
+            return wide ? MoeFfnKernel<kFmtQ4S, 2 * kCPS>::launch(p, smem, stream)
+                        : MoeFfnKernel<kFmtQ4S, kCPS>::launch(p, smem, stream);
         case kFmtQ4F16:
-            MoeFfnKernel<kFmtQ4F16>::prepare();
-            return launch_pdl(moe_ffn_kernel<kFmtQ4F16>, grid, block, smem, stream, p);
+            return wide ? MoeFfnKernel<kFmtQ4F16, 2 * kCPS>::launch(p, smem, stream)
+                        : MoeFfnKernel<kFmtQ4F16, kCPS>::launch(p, smem, stream);
         case kFmtQ4NX:
-            MoeFfnKernel<kFmtQ4NX>::prepare();
-            return launch_pdl(moe_ffn_kernel<kFmtQ4NX>, grid, block, smem, stream, p);
+            return wide ? MoeFfnKernel<kFmtQ4NX, 2 * kCPS>::launch(p, smem, stream)
+                        : MoeFfnKernel<kFmtQ4NX, kCPS>::launch(p, smem, stream);
         default: return cudaErrorInvalidValue;
     }
 }
